@@ -1,0 +1,27 @@
+// C ABI of the CPU oracle (oracle/liboracle.so). Test infrastructure only.
+#pragma once
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+int oracle_chunk_rule(int64_t num_heads, int64_t seq_len, int64_t key_dim, int64_t value_dim,
+                      int64_t chunk_size, int use_qk_l2norm, const float* query,
+                      const float* key, const float* value, const float* g, const float* beta,
+                      const float* initial_state, float* core_attn_out, float* final_state,
+                      int num_threads);
+int oracle_conv_l2_qk(int batch, int conv_dim, int kernel_size, int key_total, int num_heads,
+                      uint16_t* qkv, uint16_t* conv_state, const uint16_t* conv_w,
+                      int num_threads);
+int oracle_rec_norm_gate(int batch, int num_heads, int k_dim, int v_dim, float q_scale,
+                         float eps, const uint16_t* a, const uint16_t* b,
+                         const float* a_log_bias, const uint16_t* qkv, float* state,
+                         const uint16_t* z, const float* norm_w, uint16_t* out,
+                         int num_threads);
+int oracle_recurrent_raw(int num_heads, int k_dim, int v_dim, float q_scale, const uint16_t* q,
+                         const uint16_t* k, const uint16_t* v, float* state_with_tail,
+                         uint16_t* out);
+void oracle_f32_to_f16(const float* x, uint16_t* y, int64_t n);
+void oracle_f16_to_f32(const uint16_t* x, float* y, int64_t n);
+#ifdef __cplusplus
+}
+#endif

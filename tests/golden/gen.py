@@ -1,0 +1,61 @@
+"""Seeded synthetic input generators shared by tests, smoke() and bench.py.
+
+probe_inputs restates the deterministic generator of the reference's GPU
+chunk-prefill probe (apps/spock-deltanet-chunk-prefill-probe.cpp:215-270):
+xorshift32 (13/17/5) per array with fixed seeds, mapped to [lo, hi], q and k
+L2-normalised per (head, token) with eps 1e-6 inside the sqrt, head-major
+layouts. The BASELINE configs use numpy's PCG64 (default_rng) instead.
+"""
+import numpy as np
+
+PROBE_SEEDS = dict(q=0xDEADBEEF, k=0xCAFEBABE, v=0xDECAFBAD, g=0xABADCAFE, beta=0xBEEFCACE)
+PROBE_RANGES = dict(q=(-1.0, 1.0), k=(-1.0, 1.0), v=(-20.0, 20.0), g=(-9.0, -1e-6), beta=(0.0, 1.0))
+
+
+def xorshift32_stream(n, seed):
+    out = np.empty(n, np.uint32)
+    s = np.uint32(seed)
+    # vectorised in blocks is not possible (serial recurrence); plain loop on uint32
+    s = int(seed) & 0xFFFFFFFF
+    for i in range(n):
+        s ^= (s << 13) & 0xFFFFFFFF
+        s ^= s >> 17
+        s ^= (s << 5) & 0xFFFFFFFF
+        out[i] = s
+    return out
+
+
+def bounded_rand(n, lo, hi, seed):
+    t = xorshift32_stream(n, seed).astype(np.float32) * np.float32(1.0 / 4294967296.0)
+    return (np.float32(lo) + t * (np.float32(hi) - np.float32(lo))).astype(np.float32)
+
+
+def l2norm_rows(x, eps=1e-6):
+    x = x.astype(np.float32)
+    nrm = np.sqrt((x.astype(np.float32) ** 2).sum(-1, dtype=np.float32, keepdims=True) + np.float32(eps))
+    return (x / nrm).astype(np.float32)
+
+
+def probe_inputs(heads=16, seq=104, k_dim=128, v_dim=128, full_heads=16):
+    """The probe draws all 16 heads; `heads` keeps the first few of them."""
+    H = full_heads
+    q = bounded_rand(H * seq * k_dim, *PROBE_RANGES["q"], PROBE_SEEDS["q"]).reshape(H, seq, k_dim)
+    k = bounded_rand(H * seq * k_dim, *PROBE_RANGES["k"], PROBE_SEEDS["k"]).reshape(H, seq, k_dim)
+    v = bounded_rand(H * seq * v_dim, *PROBE_RANGES["v"], PROBE_SEEDS["v"]).reshape(H, seq, v_dim)
+    g = bounded_rand(H * seq, *PROBE_RANGES["g"], PROBE_SEEDS["g"]).reshape(H, seq)
+    b = bounded_rand(H * seq, *PROBE_RANGES["beta"], PROBE_SEEDS["beta"]).reshape(H, seq)
+    q, k = l2norm_rows(q), l2norm_rows(k)
+    return q[:heads].copy(), k[:heads].copy(), v[:heads].copy(), g[:heads].copy(), b[:heads].copy()
+
+
+def chunk_inputs(heads, seq, k_dim=128, v_dim=128, seed=0, batch=None):
+    """BASELINE configs 0/2: q,k ~ N(0,1) then L2-normalised per (head, token);
+    v ~ N(0,1); g ~ U(-1,-0.01); beta ~ U(0,1). fp32, head-major [.., H, S, D]."""
+    rng = np.random.default_rng(seed)
+    lead = (heads,) if batch is None else (batch, heads)
+    q = l2norm_rows(rng.standard_normal(lead + (seq, k_dim), dtype=np.float32))
+    k = l2norm_rows(rng.standard_normal(lead + (seq, k_dim), dtype=np.float32))
+    v = rng.standard_normal(lead + (seq, v_dim), dtype=np.float32)
+    g = rng.uniform(-1.0, -0.01, lead + (seq,)).astype(np.float32)
+    b = rng.uniform(0.0, 1.0, lead + (seq,)).astype(np.float32)
+    return q, k, v, g, b
