@@ -1,0 +1,162 @@
+/*
+ * spock_b200 — C ABI of the B200 (sm_100a) Gated DeltaNet hot path.
+ *
+ * This is the drop-in boundary that replaces the Vulkan command-buffer /
+ * descriptor layer behind spock's DeltaNet entry points. Every function takes
+ * plain pointers and sizes, returns a status code (never throws, never aborts)
+ * and enqueues its work asynchronously on the given CUDA stream (NULL = the
+ * legacy default stream). All tensor pointers are DEVICE pointers owned by the
+ * caller unless stated otherwise. Layouts are row-major, innermost last.
+ *
+ * There is no CPU fallback: a call on a machine without an sm_100 GPU returns
+ * SPOCK_ERR_CUDA with the CUDA error text in spock_last_error().
+ */
+#ifndef SPOCK_B200_H
+#define SPOCK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. Replaces the std::runtime_error thrown by the reference
+ * (src/runtime/deltanet_chunk.cpp:41-58, src/runtime/vk_device.cpp). */
+typedef enum {
+  SPOCK_OK = 0,
+  SPOCK_ERR_INVALID = -1,     /* zero / negative field, size mismatch, NULL pointer */
+  SPOCK_ERR_UNSUPPORTED = -2, /* a shape the CUDA kernels do not implement */
+  SPOCK_ERR_CUDA = -3,        /* a CUDA runtime / driver call failed */
+  SPOCK_ERR_ALLOC = -4,       /* device allocation failed */
+  SPOCK_ERR_TIMEOUT = -5      /* a bounded device-side wait gave up */
+} spock_status;
+
+typedef enum { SPOCK_F32 = 0, SPOCK_F16 = 1, SPOCK_BF16 = 2 } spock_dtype;
+
+/* Opaque per-GPU context: device ordinal, scratch buffers, error text.
+ * Replaces spock::runtime::VulkanDevice (src/runtime/vk_device.hpp:29-117).
+ * One context per GPU; calls on one context must not race from several host
+ * threads (the same contract as DecodeSession, src/runtime/vk_session.hpp:27-28). */
+typedef struct spock_ctx spock_ctx;
+
+int spock_create(int device, spock_ctx** out);
+int spock_destroy(spock_ctx* ctx);
+/* Text of the last error on this context (or of the last context-less error
+ * when ctx is NULL). Valid until the next call on the same context. */
+const char* spock_last_error(const spock_ctx* ctx);
+/* Blocks until the stream's work is done; returns SPOCK_ERR_TIMEOUT when a
+ * kernel reported a bounded wait that gave up. */
+int spock_sync(spock_ctx* ctx, void* stream);
+/* Number of kernels this library has launched since load (diagnostics). */
+uint64_t spock_kernel_launch_count(void);
+
+/* ------------------------------------------------------------------------ */
+/* Chunked gated delta rule (prefill).                                      */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces spock::runtime::DeltaNetChunkConfig (src/runtime/deltanet_chunk.hpp:8-15),
+ * extended with a batch of independent sequences and storage dtypes. */
+typedef struct {
+  int64_t batch;         /* independent sequences, >= 1 */
+  int64_t num_heads;     /* >= 1 */
+  int64_t seq_len;       /* tokens per sequence, >= 1; padded internally to chunk_size */
+  int64_t key_dim;       /* 128 on the CUDA path */
+  int64_t value_dim;     /* 128 on the CUDA path */
+  int64_t chunk_size;    /* 64 on the CUDA path */
+  int32_t dtype_in;      /* q, k, v storage: SPOCK_F32 / SPOCK_F16 / SPOCK_BF16 */
+  int32_t dtype_out;     /* core_attn_out storage: SPOCK_F32 / SPOCK_F16 / SPOCK_BF16 */
+  int32_t use_qk_l2norm; /* 1: L2-normalise q and k per (head, token), eps 1e-6 */
+  int32_t reserved;
+} spock_chunk_desc;
+
+/*
+ * Replaces run_deltanet_chunk_rule (src/runtime/deltanet_chunk.hpp:39-40,
+ * src/runtime/deltanet_chunk.cpp:53-284) and the GPU dispatch of
+ * deltanet_chunk_prefill_tiled.comp in
+ * DecodeSession::gpu_chunk_prefill_from_gpu_collect
+ * (src/runtime/vk_session.cpp:4466-4828).
+ *
+ *   q, k        [batch][num_heads][seq_len][key_dim]    dtype_in
+ *   v           [batch][num_heads][seq_len][value_dim]  dtype_in
+ *   g, beta     [batch][num_heads][seq_len]             fp32 (log-decay, write strength)
+ *   init_state  [batch][num_heads][key_dim][value_dim]  fp32, NULL = zeros
+ *   core_out    [batch][num_heads][seq_len][value_dim]  dtype_out
+ *   final_state [batch][num_heads][key_dim][value_dim]  fp32 (may alias init_state)
+ *
+ * Internally the intra-chunk contractions run on tcgen05 tensor cores with
+ * fp16 operands and fp32 accumulation in TMEM; the recurrent state is fp32.
+ * fp32 inputs, or use_qk_l2norm=1, are first staged as fp16 in the context's
+ * device scratch (grown on demand with cudaMalloc).
+ */
+int spock_chunk_prefill(spock_ctx* ctx, const spock_chunk_desc* desc, const void* q,
+                        const void* k, const void* v, const float* g, const float* beta,
+                        const float* init_state, void* core_out, float* final_state,
+                        void* stream);
+
+/*
+ * Last-token extraction of core_attn_out to fp16 by truncation with
+ * flush-to-zero, as deltanet_chunk_last_to_fp16.comp:37-66 does for the
+ * prefill -> decode handoff (src/runtime/vk_session.cpp:4621-4631).
+ *   core_out [batch][num_heads][seq_len][value_dim] fp32 -> out [batch][num_heads*value_dim] fp16
+ */
+int spock_chunk_last_to_fp16(spock_ctx* ctx, int64_t batch, int64_t num_heads, int64_t seq_len,
+                             int64_t value_dim, const float* core_out, void* out, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Fused single-token DeltaNet decode step.                                 */
+/* ------------------------------------------------------------------------ */
+
+/* Per-layer constants of one Gated DeltaNet layer (Qwen3.5-0.8B: 16 heads,
+ * key/value dim 128, conv width 4, conv_dim = heads*(2*key_dim+value_dim) = 6144). */
+typedef struct {
+  int32_t num_heads;
+  int32_t key_dim;
+  int32_t value_dim;
+  int32_t conv_kernel;      /* depthwise conv width (4) */
+  const void* conv_weight;  /* fp16 [conv_dim][conv_kernel] */
+  const float* a_log_bias;  /* fp32 [num_heads][2]: (A_log, dt_bias) per head */
+  const float* norm_weight; /* fp32 [value_dim]: gated RMSNorm weight */
+  float eps;                /* RMSNorm epsilon (1e-6) */
+  int32_t reserved;
+} spock_dn_layer;
+
+/*
+ * One decode token for `batch` independent sequences through one DeltaNet
+ * layer's mixer core. Replaces the fused pair deltanet_conv_l2_qk.comp
+ * (:41-110) + deltanet_recurrent_gbeta_norm_gate.comp (:202-335) dispatched
+ * from DecodeSession::decode (src/runtime/vk_session.cpp:2878-2883, 3213-3218),
+ * fused into ONE kernel (one CTA per (sequence, head)).
+ *
+ *   qkv        [batch][conv_dim] fp16, in/out: raw projection in; conv+SiLU
+ *              output with Q/K L2-normalised out (the reference's in-place contract)
+ *   conv_state [batch][conv_dim][conv_kernel] fp16, in/out (shift + insert)
+ *   state      [batch][num_heads][key_dim][value_dim] fp32, in/out
+ *   a, b       [batch][num_heads] fp16 raw gate projections
+ *   z          [batch][num_heads*value_dim] fp16 output gate
+ *   out        [batch][num_heads*value_dim] fp16 gated, normalised mixer output
+ *   core_raw   optional [batch][num_heads*value_dim] fp16: raw S^T q before the
+ *              norm-gate (deltanet_recurrent.comp's output); NULL to skip
+ */
+int spock_deltanet_decode_step(spock_ctx* ctx, const spock_dn_layer* layer, int64_t batch,
+                               void* qkv, void* conv_state, float* state, const void* a,
+                               const void* b, const void* z, void* out, void* core_raw,
+                               void* stream);
+
+/*
+ * Unfused recurrent update with g/beta given directly, the contract of
+ * deltanet_recurrent.comp:55-125 (g and beta read from the state tail there):
+ *   q, k, v  [batch][num_heads*key_dim] fp16 (q already L2-normalised, unscaled)
+ *   g, beta  [batch][num_heads] fp32
+ *   state    [batch][num_heads][key_dim][value_dim] fp32 in/out
+ *   out      [batch][num_heads*value_dim] fp16 raw S^T (q/sqrt(key_dim))
+ */
+int spock_deltanet_recurrent(spock_ctx* ctx, int64_t batch, int32_t num_heads, int32_t key_dim,
+                             int32_t value_dim, const void* q, const void* k, const void* v,
+                             const float* g, const float* beta, float* state, void* out,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPOCK_B200_H */

@@ -1,0 +1,70 @@
+// Shared helpers for the spock_b200 CUDA kernels (sm_100a only).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "../../include/spock_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "spock_b200 kernels are written for sm_100a (B200) only"
+#endif
+
+namespace spock {
+
+// Launch accounting (spock_kernel_launch_count).
+extern std::atomic<uint64_t> g_launches;
+
+// Error record filled by the launchers and read by the C ABI layer.
+struct Status {
+  int code = SPOCK_OK;
+  std::string msg;
+  static Status ok() { return Status(); }
+  static Status err(int c, std::string m) {
+    Status s;
+    s.code = c;
+    s.msg = std::move(m);
+    return s;
+  }
+};
+
+inline Status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return Status::ok();
+  return Status::err(SPOCK_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define SPOCK_LAUNCH_CHECK(what)                                   \
+  do {                                                             \
+    spock::g_launches.fetch_add(1, std::memory_order_relaxed);     \
+    cudaError_t _e = cudaGetLastError();                           \
+    if (_e != cudaSuccess) return spock::cuda_status(_e, what);    \
+  } while (0)
+
+// ---- device helpers -------------------------------------------------------
+
+// IEEE arithmetic with contraction disabled, so per-element updates round
+// exactly as the reference shaders' separate multiply and add.
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+template <typename T>
+__device__ __forceinline__ float load_as_f32(const T* p, int64_t i);
+template <>
+__device__ __forceinline__ float load_as_f32<float>(const float* p, int64_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float load_as_f32<__half>(const __half* p, int64_t i) {
+  return __half2float(p[i]);
+}
+template <>
+__device__ __forceinline__ float load_as_f32<__nv_bfloat16>(const __nv_bfloat16* p, int64_t i) {
+  return __bfloat162float(p[i]);
+}
+
+}  // namespace spock
