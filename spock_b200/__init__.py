@@ -1,0 +1,283 @@
+"""spock_b200: B200 (sm_100a) Gated DeltaNet hot path behind a C ABI.
+
+Host-side mirror of spock's DeltaNet entry points over libspock_b200.so
+(include/spock_b200.h). PyTorch provides device memory and streams only; every
+computation runs in this package's own CUDA kernels. There is no CPU fallback:
+if the library or a B200 is missing, calls raise SpockError.
+
+Reference interfaces mirrored here:
+  DeltaNetChunkConfig / Inputs / Outputs, run_deltanet_chunk_rule
+      src/runtime/deltanet_chunk.hpp:8-40 (same field names, layouts and the
+      same "fields must be non-zero" / size-mismatch errors)
+  chunk_prefill        batched device-tensor form used by
+                       DecodeSession::gpu_chunk_prefill_from_gpu_collect
+                       (src/runtime/vk_session.cpp:4466-4828)
+  deltanet_decode_step fused conv_l2_qk + recurrent_gbeta_norm_gate
+                       (src/runtime/vk_session.cpp:2878-2883, 3213-3218)
+"""
+import ctypes
+import os
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libspock_b200.so")
+
+SPOCK_OK = 0
+SPOCK_ERR_INVALID = -1
+SPOCK_ERR_UNSUPPORTED = -2
+SPOCK_ERR_CUDA = -3
+SPOCK_ERR_ALLOC = -4
+SPOCK_ERR_TIMEOUT = -5
+F32, F16, BF16 = 0, 1, 2
+
+EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
+            "spock_kernel_launch_count", "spock_chunk_prefill", "spock_chunk_last_to_fp16",
+            "spock_deltanet_decode_step", "spock_deltanet_recurrent"]
+
+
+class SpockError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class ChunkDesc(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("num_heads", ctypes.c_int64), ("seq_len", ctypes.c_int64),
+                ("key_dim", ctypes.c_int64), ("value_dim", ctypes.c_int64), ("chunk_size", ctypes.c_int64),
+                ("dtype_in", ctypes.c_int32), ("dtype_out", ctypes.c_int32),
+                ("use_qk_l2norm", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class DnLayer(ctypes.Structure):
+    _fields_ = [("num_heads", ctypes.c_int32), ("key_dim", ctypes.c_int32), ("value_dim", ctypes.c_int32),
+                ("conv_kernel", ctypes.c_int32), ("conv_weight", ctypes.c_void_p),
+                ("a_log_bias", ctypes.c_void_p), ("norm_weight", ctypes.c_void_p),
+                ("eps", ctypes.c_float), ("reserved", ctypes.c_int32)]
+
+
+_LIB = None
+
+
+def build(force=False):
+    from . import build as _b
+    return _b.build(force=force)
+
+
+def lib():
+    """Loads libspock_b200.so (building it in-tree when absent or stale)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+        L.spock_create.argtypes = [ctypes.c_int, ctypes.POINTER(vp)]
+        L.spock_destroy.argtypes = [vp]
+        L.spock_last_error.argtypes = [vp]
+        L.spock_last_error.restype = ctypes.c_char_p
+        L.spock_sync.argtypes = [vp, vp]
+        L.spock_kernel_launch_count.restype = ctypes.c_uint64
+        L.spock_chunk_prefill.argtypes = [vp, ctypes.POINTER(ChunkDesc)] + [vp] * 9
+        L.spock_chunk_last_to_fp16.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp]
+        L.spock_deltanet_decode_step.argtypes = [vp, ctypes.POINTER(DnLayer), i64] + [vp] * 9
+        L.spock_deltanet_recurrent.argtypes = [vp, i64, i32, i32, i32] + [vp] * 8
+        _LIB = L
+    return _LIB
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    import torch
+    if not t.is_cuda:
+        raise SpockError(SPOCK_ERR_INVALID, "expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise SpockError(SPOCK_ERR_INVALID, "expected a contiguous tensor")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _dtype_code(dt):
+    import torch
+    return {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}[dt]
+
+
+class Context:
+    """One per GPU (spock_ctx). Replaces VulkanDevice (src/runtime/vk_device.hpp:29-117)."""
+
+    _by_device = {}
+
+    def __init__(self, device=0):
+        L = lib()
+        h = ctypes.c_void_p()
+        rc = L.spock_create(int(device), ctypes.byref(h))
+        if rc != SPOCK_OK:
+            raise SpockError(rc, L.spock_last_error(None).decode())
+        self.h = h
+        self.device = device
+
+    @classmethod
+    def get(cls, device=0):
+        if device not in cls._by_device:
+            cls._by_device[device] = Context(device)
+        return cls._by_device[device]
+
+    def check(self, rc):
+        if rc != SPOCK_OK:
+            raise SpockError(rc, lib().spock_last_error(self.h).decode())
+
+    def sync(self, stream=None):
+        self.check(lib().spock_sync(self.h, _stream(stream)))
+
+    def close(self):
+        if self.h:
+            lib().spock_destroy(self.h)
+            self.h = None
+
+
+def _stream(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def chunk_prefill(q, k, v, g, beta, initial_state=None, out_dtype=None, use_qk_l2norm=False,
+                  chunk_size=64, out=None, final_state=None, ctx=None, stream=None):
+    """Batched chunked gated delta rule on device tensors.
+
+    q, k [B,H,S,K] and v [B,H,S,V] (fp32/fp16/bf16, same dtype); g, beta [B,H,S]
+    fp32; initial_state [B,H,K,V] fp32 or None. Returns (core_attn_out [B,H,S,V]
+    in out_dtype (default: q's dtype), final_state [B,H,K,V] fp32).
+    """
+    import torch
+    B, H, S, K = q.shape
+    V = v.shape[-1]
+    out_dtype = out_dtype or q.dtype
+    ctx = ctx or Context.get(q.device.index or 0)
+    if out is None:
+        out = torch.empty((B, H, S, V), dtype=out_dtype, device=q.device)
+    if final_state is None:
+        final_state = torch.empty((B, H, K, V), dtype=torch.float32, device=q.device)
+    d = ChunkDesc(B, H, S, K, V, chunk_size, _dtype_code(q.dtype), _dtype_code(out_dtype),
+                  int(bool(use_qk_l2norm)), 0)
+    ctx.check(lib().spock_chunk_prefill(ctx.h, ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(g),
+                                        _ptr(beta), _ptr(initial_state), _ptr(out), _ptr(final_state),
+                                        _stream(stream)))
+    return out, final_state
+
+
+def chunk_last_to_fp16(core_out, ctx=None, stream=None):
+    """Last token of core_attn_out [B,H,S,V] fp32 -> fp16 [B,H*V] by truncation (FTZ)."""
+    import torch
+    B, H, S, V = core_out.shape
+    ctx = ctx or Context.get(core_out.device.index or 0)
+    out = torch.empty((B, H * V), dtype=torch.float16, device=core_out.device)
+    ctx.check(lib().spock_chunk_last_to_fp16(ctx.h, B, H, S, V, _ptr(core_out), _ptr(out), _stream(stream)))
+    return out
+
+
+@dataclass
+class DeltaNetLayer:
+    """Per-layer constants (spock_dn_layer). Tensors are device tensors."""
+    conv_weight: object   # fp16 [conv_dim, conv_kernel]
+    a_log_bias: object    # fp32 [num_heads, 2]
+    norm_weight: object   # fp32 [value_dim]
+    num_heads: int = 16
+    key_dim: int = 128
+    value_dim: int = 128
+    conv_kernel: int = 4
+    eps: float = 1e-6
+
+    def c_struct(self):
+        return DnLayer(self.num_heads, self.key_dim, self.value_dim, self.conv_kernel,
+                       _ptr(self.conv_weight), _ptr(self.a_log_bias), _ptr(self.norm_weight),
+                       self.eps, 0)
+
+
+def deltanet_decode_step(layer, qkv, conv_state, state, a, b, z, out=None, core_raw=None, ctx=None,
+                         stream=None):
+    """One decode token through a DeltaNet mixer core; qkv, conv_state, state updated in place."""
+    import torch
+    B = qkv.shape[0]
+    ctx = ctx or Context.get(qkv.device.index or 0)
+    if out is None:
+        out = torch.empty((B, layer.num_heads * layer.value_dim), dtype=torch.float16, device=qkv.device)
+    st = layer.c_struct()
+    ctx.check(lib().spock_deltanet_decode_step(ctx.h, ctypes.byref(st), B, _ptr(qkv), _ptr(conv_state),
+                                               _ptr(state), _ptr(a), _ptr(b), _ptr(z), _ptr(out),
+                                               _ptr(core_raw), _stream(stream)))
+    return out
+
+
+def deltanet_recurrent(q, k, v, g, beta, state, num_heads=16, key_dim=128, value_dim=128, ctx=None,
+                       stream=None):
+    """Unfused recurrent update (deltanet_recurrent.comp contract); state updated in place."""
+    import torch
+    B = q.shape[0]
+    ctx = ctx or Context.get(q.device.index or 0)
+    out = torch.empty((B, num_heads * value_dim), dtype=torch.float16, device=q.device)
+    ctx.check(lib().spock_deltanet_recurrent(ctx.h, B, num_heads, key_dim, value_dim, _ptr(q), _ptr(k),
+                                             _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(out),
+                                             _stream(stream)))
+    return out
+
+
+# ---- reference-shaped API (host vectors in, host vectors out) ----------------
+
+@dataclass
+class DeltaNetChunkConfig:
+    num_heads: int = 0
+    sequence_length: int = 0
+    key_dim: int = 0
+    value_dim: int = 0
+    chunk_size: int = 64
+    use_qk_l2norm: bool = True
+
+
+@dataclass
+class DeltaNetChunkInputs:
+    query: List[float] = field(default_factory=list)   # [head][token][dim]
+    key: List[float] = field(default_factory=list)
+    value: List[float] = field(default_factory=list)
+    g: List[float] = field(default_factory=list)       # [head][token]
+    beta: List[float] = field(default_factory=list)
+    initial_state: List[float] = field(default_factory=list)  # [head][key][value] or empty
+
+
+@dataclass
+class DeltaNetChunkOutputs:
+    core_attn_out: np.ndarray = None   # flat [head][token][value]
+    final_state: np.ndarray = None     # flat [head][key][value]
+
+
+def run_deltanet_chunk_rule(config: DeltaNetChunkConfig, inputs: DeltaNetChunkInputs,
+                            device=0) -> DeltaNetChunkOutputs:
+    """Drop-in for spock::runtime::run_deltanet_chunk_rule on the GPU (fp32 in, fp32 out)."""
+    import torch
+    c = config
+    if min(c.num_heads, c.sequence_length, c.key_dim, c.value_dim, c.chunk_size) <= 0:
+        raise SpockError(SPOCK_ERR_INVALID, "DeltaNet chunk config fields must be non-zero")
+    H, S, K, V = c.num_heads, c.sequence_length, c.key_dim, c.value_dim
+
+    def checked(x, n, name):
+        a = np.asarray(x, dtype=np.float32).reshape(-1)
+        if a.size != n:
+            raise SpockError(SPOCK_ERR_INVALID, f"{name} size mismatch: expected {n}, got {a.size}")
+        return a
+
+    dev = torch.device("cuda", device)
+    t = lambda a, shape: torch.from_numpy(a.reshape(shape)).to(dev)
+    q = t(checked(inputs.query, H * S * K, "query"), (1, H, S, K))
+    k = t(checked(inputs.key, H * S * K, "key"), (1, H, S, K))
+    v = t(checked(inputs.value, H * S * V, "value"), (1, H, S, V))
+    g = t(checked(inputs.g, H * S, "g"), (1, H, S))
+    b = t(checked(inputs.beta, H * S, "beta"), (1, H, S))
+    init = None
+    if len(inputs.initial_state):
+        init = t(checked(inputs.initial_state, H * K * V, "initial_state"), (1, H, K, V))
+    out, st = chunk_prefill(q, k, v, g, b, initial_state=init, out_dtype=torch.float32,
+                            use_qk_l2norm=c.use_qk_l2norm, chunk_size=c.chunk_size)
+    return DeltaNetChunkOutputs(out.reshape(-1).cpu().numpy(), st.reshape(-1).cpu().numpy())

@@ -59,3 +59,30 @@ def chunk_inputs(heads, seq, k_dim=128, v_dim=128, seed=0, batch=None):
     g = rng.uniform(-1.0, -0.01, lead + (seq,)).astype(np.float32)
     b = rng.uniform(0.0, 1.0, lead + (seq,)).astype(np.float32)
     return q, k, v, g, b
+
+
+def f16bits(x):
+    return np.asarray(x, np.float32).astype(np.float16).view(np.uint16)
+
+
+def decode_inputs(batch, heads=16, k_dim=128, v_dim=128, ks=4, seed=0):
+    """BASELINE config 1 per sequence: state ~ N(0,0.02) fp32; conv cache fp16
+    (the reference's [conv_dim][4] slot layout) ~ N(0,1); conv weight ~ N(0,0.02);
+    qkv ~ N(0,1); a, b ~ N(0,1); A_log ~ U(-2,1); dt_bias ~ N(0,0.1) (fp16-rounded,
+    the reference reads it from fp16); z ~ N(0,1); norm weight ~ N(0,0.1) + 1."""
+    rng = np.random.default_rng(seed)
+    conv_dim = heads * (2 * k_dim + v_dim)
+    d = dict(
+        state=(rng.standard_normal((batch, heads, k_dim, v_dim), dtype=np.float32) * 0.02).astype(np.float32),
+        conv_state=f16bits(rng.standard_normal((batch, conv_dim, ks), dtype=np.float32)),
+        conv_w=f16bits(rng.standard_normal((conv_dim, ks), dtype=np.float32) * 0.02),
+        qkv=f16bits(rng.standard_normal((batch, conv_dim), dtype=np.float32)),
+        a=f16bits(rng.standard_normal((batch, heads), dtype=np.float32)),
+        b=f16bits(rng.standard_normal((batch, heads), dtype=np.float32)),
+        z=f16bits(rng.standard_normal((batch, heads * v_dim), dtype=np.float32)),
+        norm_w=(1.0 + 0.1 * rng.standard_normal(v_dim, dtype=np.float32)).astype(np.float32),
+    )
+    a_log = rng.uniform(-2, 1, heads).astype(np.float32)
+    dt = np.float16(rng.standard_normal(heads, dtype=np.float32) * 0.1).astype(np.float32)
+    d["a_log_bias"] = np.stack([a_log, dt], 1).astype(np.float32)
+    return d

@@ -1,0 +1,124 @@
+"""Parity of the tcgen05 chunk-prefill kernel (through the C ABI) with the CPU
+oracle, which is itself pinned bit-exactly to the reference's
+run_deltanet_chunk_rule. Bar: max |gpu-ref|/max(1,|ref|) <= 1e-3 (BASELINE
+north_star tolerance, fp32 outputs)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import spock_b200
+from tests.golden.gen import chunk_inputs
+from tests.util import max_rel
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def run_gpu(q, k, v, g, b, init=None, dtype_in=torch.float32, dtype_out=torch.float32, l2=False):
+    dev = torch.device("cuda", 0)
+    T = lambda a, dt=torch.float32: torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(dt)
+    lead = q.shape[:-2]
+    out, st = spock_b200.chunk_prefill(T(q, dtype_in), T(k, dtype_in), T(v, dtype_in), T(g), T(b),
+                                       initial_state=None if init is None else T(init),
+                                       out_dtype=dtype_out, use_qk_l2norm=l2)
+    torch.cuda.synchronize()
+    spock_b200.Context.get(0).sync()
+    return out.float().cpu().numpy(), st.cpu().numpy()
+
+
+def batched_oracle(q, k, v, g, b, init=None, l2=False):
+    """[B,H,...] inputs through the oracle one sequence at a time."""
+    outs, sts = [], []
+    for i in range(q.shape[0]):
+        o, s = oracle.chunk_rule(q[i], k[i], v[i], g[i], b[i], use_qk_l2norm=l2,
+                                 initial_state=None if init is None else init[i], threads=8)
+        outs.append(o)
+        sts.append(s)
+    return np.stack(outs), np.stack(sts)
+
+
+def test_config0_fp32(cuda_ok):
+    """H16, S104 (padded to 128), C64, d128, fp32."""
+    q, k, v, g, b = chunk_inputs(16, 104, seed=0, batch=1)
+    ro, rs = batched_oracle(q, k, v, g, b)
+    go, gs = run_gpu(q, k, v, g, b)
+    assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL, (max_rel(go, ro), max_rel(gs, rs))
+
+
+def test_probe_golden_fixture(cuda_ok):
+    """The reference probe's xorshift case (v in [-20,20], g in [-9,0)) vs the
+    reference's own outputs stored in the fixture."""
+    d = np.load(os.path.join(GOLD, "chunk_probe_h4.npz"))
+    go, gs = run_gpu(d["q"][None], d["k"][None], d["v"][None], d["g"][None], d["beta"][None])
+    assert max_rel(go[0], d["ref_out"]) <= TOL and max_rel(gs[0], d["ref_state"]) <= TOL, (
+        max_rel(go[0], d["ref_out"]), max_rel(gs[0], d["ref_state"]))
+
+
+@pytest.mark.parametrize("S", [1, 5, 63, 64, 65, 129, 300])
+def test_ragged_lengths_with_initial_state(cuda_ok, S):
+    q, k, v, g, b = chunk_inputs(2, S, seed=S, batch=2)
+    init = np.random.default_rng(S).standard_normal((2, 2, 128, 128)).astype(np.float32) * 0.1
+    ro, rs = batched_oracle(q, k, v, g, b, init)
+    go, gs = run_gpu(q, k, v, g, b, init)
+    assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL, (max_rel(go, ro), max_rel(gs, rs))
+
+
+@pytest.mark.parametrize("dt_out", [torch.bfloat16, torch.float32])
+def test_bf16_inputs_config2_shape(cuda_ok, dt_out):
+    """Config-2 layout at a size the oracle finishes quickly: bf16 q/k/v, fp32 g/beta/state."""
+    q, k, v, g, b = chunk_inputs(16, 512, seed=7, batch=2)
+    qb, kb, vb = (torch.from_numpy(x).bfloat16().float().numpy() for x in (q, k, v))
+    ro, rs = batched_oracle(qb, kb, vb, g, b)
+    go, gs = run_gpu(qb, kb, vb, g, b, dtype_in=torch.bfloat16, dtype_out=dt_out)
+    tol_out = TOL if dt_out == torch.float32 else 2 ** -8  # bf16 output rounding
+    assert max_rel(go, ro) <= tol_out and max_rel(gs, rs) <= TOL, (max_rel(go, ro), max_rel(gs, rs))
+
+
+def test_fp16_inputs_and_in_kernel_l2norm(cuda_ok):
+    rng = np.random.default_rng(11)
+    q, k, v = (rng.standard_normal((1, 3, 100, 128), dtype=np.float32) for _ in range(3))
+    g = rng.uniform(-1, -0.01, (1, 3, 100)).astype(np.float32)
+    b = rng.uniform(0, 1, (1, 3, 100)).astype(np.float32)
+    ro, rs = batched_oracle(q, k, v, g, b, l2=True)
+    go, gs = run_gpu(q, k, v, g, b, l2=True)
+    assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL
+    qh, kh, vh = (torch.from_numpy(x).half().float().numpy() for x in (q, k, v))
+    ro, rs = batched_oracle(qh, kh, vh, g, b, l2=True)
+    go, gs = run_gpu(qh, kh, vh, g, b, dtype_in=torch.float16, l2=True)
+    assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL
+
+
+def test_reference_shaped_api(cuda_ok):
+    q, k, v, g, b = chunk_inputs(2, 70, seed=2)
+    cfg = spock_b200.DeltaNetChunkConfig(2, 70, 128, 128, 64, use_qk_l2norm=False)
+    res = spock_b200.run_deltanet_chunk_rule(cfg, spock_b200.DeltaNetChunkInputs(
+        q.ravel(), k.ravel(), v.ravel(), g.ravel(), b.ravel()))
+    ro, rs = oracle.chunk_rule(q, k, v, g, b)
+    assert max_rel(res.core_attn_out, ro.ravel()) <= TOL and max_rel(res.final_state, rs.ravel()) <= TOL
+
+
+def test_unsupported_shape_reports_error(cuda_ok):
+    x = torch.zeros((1, 2, 5, 3), device="cuda")
+    with pytest.raises(spock_b200.SpockError, match="key_dim=value_dim=128"):
+        spock_b200.chunk_prefill(x, x, torch.zeros((1, 2, 5, 2), device="cuda"),
+                                 torch.zeros((1, 2, 5), device="cuda"), torch.zeros((1, 2, 5), device="cuda"),
+                                 chunk_size=4)
+
+
+def test_last_token_truncation(cuda_ok):
+    core = torch.tensor([1.0009765625 + 2 ** -12, -3e-8, 70000.0, float("nan")] * 32, device="cuda").reshape(1, 1, 1, 128)
+    core = core.repeat(1, 1, 3, 1).contiguous()
+    out = spock_b200.chunk_last_to_fp16(core).cpu().view(torch.int16).numpy().astype(np.uint16)
+    assert out[0] == 0x3C01 and out[1] == 0x8000 and out[2] == 0x7C00 and out[3] == 0x7E00
+
+
+def test_state_is_resident_long_sequence(cuda_ok):
+    """Many chunks (S=2048): state carried in TMEM across 32 chunks."""
+    q, k, v, g, b = chunk_inputs(2, 2048, seed=9, batch=1)
+    ro, rs = batched_oracle(q, k, v, g, b)
+    go, gs = run_gpu(q, k, v, g, b)
+    assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL, (max_rel(go, ro), max_rel(gs, rs))
