@@ -1,0 +1,371 @@
+"""Benchmark of the B200 Gated DeltaNet hot path (one JSON line on rank 0).
+
+Default workload: long batched chunk prefill, 64
+independent sequences x 16 heads x 8192 tokens per GPU, chunk 64, k=v=128,
+bf16 q/k/v, fp32 g/beta/state/accumulation, bf16 core_attn_out. Synthetic
+seeded inputs with config 0's distributions. A step is one chunk-prefill call
+over the whole batch. Under torchrun each rank runs its own 64 sequences
+(independent (sequence, head) pairs, no collective): weak scaling.
+
+  value    Mtok/s over all ranks, inputs resident in HBM (token = one position
+           of one sequence across all 16 heads), device-timed with CUDA events,
+           max over ranks
+  e2e      the same metric through the public API with pinned host buffers:
+           H2D of q/k/v/g/beta and D2H of core_attn_out + final_state timed
+  roofline dominant kernel (chunk_rule_kernel) against MEASURED_PEAKS.json
+  cpu_baseline the reference's own run_deltanet_chunk_rule (oracle/_ref) or
+           the oracle port, on a bounded sample, all host threads
+
+--config 1 runs the fused decode step instead (batch 64).
+--impl reference times the reference CPU implementation on the same metric.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, K, V, C = 16, 128, 128, 64
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.dev, self.rows, self.proc = dev, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) == 8:
+                self.rows.append(f)
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        num = lambda x: float(x) if x.replace(".", "").isdigit() else None
+        sm = [num(r[1]) for r in self.rows if num(r[1])]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[4:]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(self.rows[0][2]),
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_init(args):
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch.distributed as dist
+        backend = "nccl" if args.impl != "reference" else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend)
+    elif args.impl != "reference":
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, ws):
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if dist.get_backend() == "nccl" else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- config 2 ---
+
+def make_chunk_inputs(B, S, seed, dev):
+    """Seeded on device (bf16 q/k/v with q,k L2-normalised; fp32 g, beta)."""
+    import torch
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    def l2(x):
+        return x / torch.sqrt((x * x).sum(-1, keepdim=True) + 1e-6)
+    q = l2(torch.randn(B, H, S, K, device=dev, generator=gen)).bfloat16()
+    k = l2(torch.randn(B, H, S, K, device=dev, generator=gen)).bfloat16()
+    v = torch.randn(B, H, S, V, device=dev, generator=gen).bfloat16()
+    g = torch.empty(B, H, S, device=dev).uniform_(-1.0, -0.01, generator=gen)
+    b = torch.empty(B, H, S, device=dev).uniform_(0.0, 1.0, generator=gen)
+    return q, k, v, g, b
+
+
+def cpu_reference_sample(threads, S=1024, seqs=None):
+    """Times the reference chunk rule (or the oracle port) on a bounded sample;
+    returns (Mtok/s, kind, sample description)."""
+    import numpy as np
+    import oracle
+    from tests.golden.gen import chunk_inputs
+    seqs = seqs or threads
+    q, k, v, g, b = chunk_inputs(H, S, seed=0, batch=seqs)
+    out = np.zeros_like(v)
+    st = np.zeros((seqs, H, K, V), np.float32)
+    ref = oracle.ref_lib()
+    import ctypes
+    f = ctypes.POINTER(ctypes.c_float)
+    P = lambda a: a.ctypes.data_as(f)
+    t0 = time.perf_counter()
+    if ref is not None:
+        rc = ref.ref_chunk_rule_batched(seqs, H, S, K, V, C, P(q), P(k), P(v), P(g), P(b), P(out), P(st), threads)
+        kind = "reference"
+        assert rc == 0
+    else:  # oracle port: one call per sequence, heads over threads
+        kind = "port"
+        for i in range(seqs):
+            oracle.chunk_rule(q[i], k[i], v[i], g[i], b[i], threads=threads)
+    dt = time.perf_counter() - t0
+    return seqs * S / dt / 1e6, kind, f"{seqs} sequences x {H} heads x {S} tokens, fp32, {threads} threads, {dt:.1f} s"
+
+
+def bench_chunk(args, ws, rank, local):
+    import torch
+    import spock_b200
+    dev = torch.device("cuda", local)
+    B, S = args.batch, args.seq
+    q, k, v, g, b = make_chunk_inputs(B, S, 1234 + rank, dev)
+    out = torch.empty(B, H, S, V, dtype=torch.bfloat16, device=dev)
+    st = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
+    ctx = spock_b200.Context.get(local)
+    stream = torch.cuda.current_stream()
+    run = lambda: spock_b200.chunk_prefill(q, k, v, g, b, out_dtype=torch.bfloat16, out=out,
+                                           final_state=st, ctx=ctx, stream=stream)
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    ctx.sync()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    n0 = spock_b200.lib().spock_kernel_launch_count()
+    barrier(ws)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for e0, e1 in evs:
+            e0.record(stream)
+            run()
+            e1.record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(ws)
+    launches = spock_b200.lib().spock_kernel_launch_count() - n0
+    ctx.sync()
+    total_ms = max_over_ranks(t0.elapsed_time(t1), ws)
+    kern_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    kern_ms = max_over_ranks(kern_ms, ws)
+    ms_step = total_ms / args.steps
+    tokens_step = B * S * ws
+    value = tokens_step / (ms_step / 1e3) / 1e6
+
+    # end to end through the public API with pinned host buffers
+    hq = [x.cpu().pin_memory() for x in (q, k, v, g, b)]
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    hst = torch.empty(st.shape, dtype=st.dtype).pin_memory()
+    dq = [torch.empty_like(x) for x in (q, k, v, g, b)]
+    h2d = sum(x.numel() * x.element_size() for x in hq)
+    d2h = hout.numel() * hout.element_size() + hst.numel() * hst.element_size()
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+
+    def e2e_step():
+        for d_, h_ in zip(dq, hq):
+            d_.copy_(h_, non_blocking=True)
+        spock_b200.chunk_prefill(*dq, out_dtype=torch.bfloat16, out=out, final_state=st, ctx=ctx, stream=stream)
+        hout.copy_(out, non_blocking=True)
+        hst.copy_(st, non_blocking=True)
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    a1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(a0.elapsed_time(a1), ws) / e2e_steps
+    e2e_val = tokens_step / (e2e_ms / 1e3) / 1e6
+
+    hbm, tf, pk = peaks()
+    alg_bytes = B * H * S * (3 * K * 2 + 8 + V * 2) + B * H * K * V * 4
+    alg_flops = B * H * S * 2 * (5 * C * K + 3 * K * V)
+    achieved_gbs = alg_bytes / (kern_ms / 1e3) / 1e9
+    achieved_tf = alg_flops / (kern_ms / 1e3) / 1e12
+    t_hbm, t_tc = alg_bytes / (hbm * 1e9), alg_flops / (tf * 1e12)
+    res = {
+        "metric": "chunk-prefill Mtok/s (token = one sequence position across all 16 heads)",
+        "value": round(value, 3), "unit": "Mtok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 in/out, fp16 tensor-core operands, fp32 state+accumulation", "data": "synthetic (seeded, config-0 distributions)",
+        "config": {"workload": "config 2: batched chunk prefill", "sequences_per_gpu": B, "heads": H,
+                   "seq_len": S, "chunk": C, "k_dim": K, "v_dim": V, "parallelism": f"dp{ws} over sequences",
+                   "l2": "inputs (%.1f GB/GPU) larger than L2" % (alg_bytes / 1e9)},
+        "per_gpu_Mtok_s": round(value / ws, 3),
+        "e2e": {"value": round(e2e_val, 4), "unit": "Mtok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm" if t_hbm >= t_tc else "tensor", "achieved": round(achieved_gbs, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved_gbs / hbm, 4),
+                     "traffic": None, "peak_source": pk,
+                     "tensor": {"achieved": round(achieved_tf, 1), "peak": tf, "unit": "TFLOP/s",
+                                "frac": round(achieved_tf / tf, 4)},
+                     "kernel_ms": round(kern_ms, 4), "alg_bytes": alg_bytes, "alg_flops": alg_flops},
+        "clocks": clk.summary(),
+    }
+    return res
+
+
+# ---------------------------------------------------------------- config 1 ---
+
+def bench_decode(args, ws, rank, local):
+    import numpy as np
+    import torch
+    import spock_b200
+    from tests.golden.gen import decode_inputs
+    dev = torch.device("cuda", local)
+    B = args.batch
+    layers = args.layers  # independent layer states so successive steps stream fresh HBM
+    d = decode_inputs(B, seed=rank)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    h16 = lambda a: T(a.view(np.int16))
+    layer = spock_b200.DeltaNetLayer(h16(d["conv_w"]), T(d["a_log_bias"]), T(d["norm_w"]))
+    states = [T(d["state"]) for _ in range(layers)]
+    convs = [h16(d["conv_state"]) for _ in range(layers)]
+    qkv0 = h16(d["qkv"])
+    qkv = [qkv0.clone() for _ in range(layers)]
+    a, b_, z = h16(d["a"]), h16(d["b"]), h16(d["z"])
+    out = torch.empty((B, 2048), dtype=torch.int16, device=dev)
+    ctx = spock_b200.Context.get(local)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for l in range(layers):
+            spock_b200.deltanet_decode_step(layer, qkv[l], convs[l], states[l], a, b_, z, out=out, ctx=ctx, stream=stream)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    n0 = spock_b200.lib().spock_kernel_launch_count()
+    barrier(ws)
+    with ClockSampler(local) as clk:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    launches = spock_b200.lib().spock_kernel_launch_count() - n0
+    ms = max_over_ranks(t0.elapsed_time(t1), ws) / args.steps
+    per_launch_ms = ms / layers
+    value = B * layers * ws / (ms / 1e3)  # sequence-layer steps per second
+    hbm, tf, pk = peaks()
+    alg = B * (H * K * V * 4 * 2 + 6144 * 4 * 2 * 2 + 6144 * 2 + 2048 * 2 * 2 + 64) + 6144 * 8 + 512 + 128
+    gbs = alg / (per_launch_ms / 1e3) / 1e9
+    return {
+        "metric": "fused DeltaNet decode step: sequence-layer steps/s", "value": round(value, 1), "unit": "steps/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16 io, fp32 state",
+        "data": "synthetic (seeded, config-1 distributions)",
+        "config": {"workload": "config 1: fused decode step", "batch": B, "layers_per_step": layers,
+                   "l2": "%d independent layer states (%.0f MB) larger than L2" % (layers, layers * B * 1.05)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": pk,
+                     "kernel_us": round(per_launch_ms * 1e3, 2), "alg_bytes": alg},
+        "clocks": clk.summary(),
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="spock_b200", choices=["spock_b200", "reference"])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2])
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=8192)
+    ap.add_argument("--layers", type=int, default=18)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.batch is None:
+        args.batch = 64
+    args.warmup = max(args.warmup, 3) if args.impl != "reference" else args.warmup
+    ws, rank, local = dist_init(args)
+
+    if args.impl == "reference":
+        if rank == 0:
+            threads = os.cpu_count() or 1
+            vals, kind, sample = [], None, None
+            for i in range(args.warmup + args.steps):
+                v, kind, sample = cpu_reference_sample(threads, S=512)
+                if i >= args.warmup:
+                    vals.append(v)
+            val = statistics.mean(vals)
+            print(json.dumps({
+                "impl": "reference", "metric": "chunk-prefill Mtok/s (token = one sequence position across all 16 heads)",
+                "value": round(val, 6), "unit": "Mtok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded, config-0 distributions)",
+                "config": {"workload": "config 2: batched chunk prefill (bounded sample per step)", "heads": H,
+                           "chunk": C, "k_dim": K, "v_dim": V},
+                "cpu_baseline": {"value": round(val, 6), "unit": "Mtok/s", "cores": threads, "kind": kind, "sample": sample},
+                "e2e": {"value": round(val, 6), "unit": "Mtok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+                flush=True)
+        return
+
+    res = bench_chunk(args, ws, rank, local) if args.config == 2 else bench_decode(args, ws, rank, local)
+    if rank == 0:
+        if ws == 1 and not args.no_cpu_baseline and args.config == 2:
+            threads = os.cpu_count() or 1
+            v, kind, sample = cpu_reference_sample(threads, S=1024)
+            res["cpu_baseline"] = {"value": round(v, 6), "unit": "Mtok/s", "cores": threads, "kind": kind, "sample": sample}
+        print(json.dumps(res), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -59,6 +59,13 @@ constexpr int OFF_TM = OFF_NM + C * LDN * 4;
 constexpr int OFF_YM = OFF_TM + C * LDN * 4;
 constexpr int OFF_SMALL = OFF_YM + 3 * 256 * 4;
 constexpr int SMEM_BYTES = OFF_SMALL + 2048 + 1024;  // + alignment slack
+// Extra regions of the precise (fp32-input) variant: the low fp16 half of V,
+// and [T diag(beta)]_lo with its own zero block. The low half of
+// diag(e^{gL-gc}) v_new reuses the AW region, which is dead after step 7.
+constexpr int OFF_VLO = 182 * 1024;
+constexpr int OFF_TBL = OFF_VLO + 16 * 1024;
+constexpr int SMEM_BYTES_PRECISE = OFF_TBL + 16 * 1024 + 1024;
+static_assert(OFF_VLO >= OFF_SMALL + 2048, "smem regions overlap");
 
 // Byte offset of 16-byte chunk `ch` (0..7) of row `row` in a SWIZZLE_128B
 // region whose rows are 128 bytes (the layout TMA writes and UMMA reads).
@@ -152,10 +159,15 @@ __device__ __forceinline__ void store_row32(void* out, size_t idx, const float (
   }
 }
 
-template <bool kBf16In, int kOut>
+// kPrecise (fp32 inputs): V arrives as an fp16 hi/lo pair and the products
+// [T diag(beta)] V and K^T [diag(e^{gL-gc}) v_new] are carried to ~22 bits by
+// adding the lo x hi cross terms, so fp32 inputs are not limited to fp16's
+// 11-bit significand where it matters for the state.
+template <bool kBf16In, int kOut, bool kPrecise>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_rule_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                      const __grid_constant__ CUtensorMap tmv, const float* __restrict__ g,
+                      const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmvlo,
+                      const float* __restrict__ g,
                       const float* __restrict__ beta, const float* __restrict__ init,
                       void* __restrict__ out, float* __restrict__ final_state, int S,
                       int* __restrict__ err_flag) {
@@ -183,14 +195,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::prefetch_tmap(&tmq);
     tc::prefetch_tmap(&tmk);
     tc::prefetch_tmap(&tmv);
+    if constexpr (kPrecise) tc::prefetch_tmap(&tmvlo);
   }
   if (warp == 0) {
     tc::tmem_alloc(s_tmem, 512);
     tc::tmem_relinquish();
   }
-  // zero block between T diag(beta) and P
-  for (int i = t; i < 8 * 1024 / 16; i += kThreads)
+  // zero block between T diag(beta) and P (and after [T diag(beta)]_lo)
+  for (int i = t; i < 8 * 1024 / 16; i += kThreads) {
     reinterpret_cast<uint4*>(sm + OFF_TB + 8 * 1024)[i] = make_uint4(0, 0, 0, 0);
+    if constexpr (kPrecise) reinterpret_cast<uint4*>(sm + OFF_TBL + 8 * 1024)[i] = make_uint4(0, 0, 0, 0);
+  }
   tc::fence_async_smem();
   tc::tc_fence_before();
   __syncthreads();
@@ -232,12 +247,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int c = 0; c < nchunks; ++c) {
     // ---- 1. loads: q/k/v tiles by TMA, g/beta by threads -----------------
     if (t == 0) {
-      tc::mbar_arrive_expect_tx(bar_tma, 6 * 64 * 64 * 2);
+      tc::mbar_arrive_expect_tx(bar_tma, (kPrecise ? 8 : 6) * 64 * 64 * 2);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         tc::tma_load_3d(sm + OFF_QK + h * 16384, &tmq, bar_tma, h * 64, c * C, p);
         tc::tma_load_3d(sm + OFF_QK + h * 16384 + 8192, &tmk, bar_tma, h * 64, c * C, p);
         tc::tma_load_3d(sm + OFF_V + h * 8192, &tmv, bar_tma, h * 64, c * C, p);
+        if constexpr (kPrecise) tc::tma_load_3d(sm + OFF_VLO + h * 8192, &tmvlo, bar_tma, h * 64, c * C, p);
       }
     }
     if (t < C) {
@@ -350,8 +366,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           y[k] = x[k] * s_eg[j];
         }
         const int ch = (jh >> 3) + q;
-        *reinterpret_cast<uint4*>(sm + OFF_TB + sw128(i, ch)) = pack8(x);
+        const uint4 xh = pack8(x);
+        *reinterpret_cast<uint4*>(sm + OFF_TB + sw128(i, ch)) = xh;
         *reinterpret_cast<uint4*>(sm + OFF_TBE + sw128(i, ch)) = pack8(y);
+        if constexpr (kPrecise) {
+          float xr[8];
+          unpack8(xh, xr);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) xr[k] = x[k] - xr[k];
+          *reinterpret_cast<uint4*>(sm + OFF_TBL + sw128(i, ch)) = pack8(xr);
+        }
       }
     }
     {
@@ -377,6 +401,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < 4; ++ks)
         tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + ks * 32, 16, 1024),
                     tc::sdesc(sbase + OFF_V + ks * 2048, 8192, 1024), ID_U, ks > 0);
+      if constexpr (kPrecise) {
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + ks * 32, 16, 1024),
+                      tc::sdesc(sbase + OFF_VLO + ks * 2048, 8192, 1024), ID_U, 1);
+          tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TBL + ks * 32, 16, 1024),
+                      tc::sdesc(sbase + OFF_V + ks * 2048, 8192, 1024), ID_U, 1);
+        }
+      }
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         tc::mma_f16(mWT, tc::sdesc(sbase + OFF_QK + 8192 + ks * 2048, 16384, 1024),
@@ -428,7 +461,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           float y[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) y[k] = v[8 * q + k] * fs;
-          *reinterpret_cast<uint4*>(sm + OFF_VS + h * 8192 + sw128(t, ch)) = pack8(y);
+          const uint4 yh = pack8(y);
+          *reinterpret_cast<uint4*>(sm + OFF_VS + h * 8192 + sw128(t, ch)) = yh;
+          if constexpr (kPrecise) {  // low half into the dead AW region
+            float yr[8];
+            unpack8(yh, yr);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) yr[k] = y[k] - yr[k];
+            *reinterpret_cast<uint4*>(sm + OFF_AW + h * 8192 + sw128(t, ch)) = pack8(yr);
+          }
         }
       }
     }
@@ -443,6 +484,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < 4; ++ks)
         tc::mma_f16(mS, tc::sdesc(sbase + OFF_QK + 8192 + ks * 2048, 16384, 1024),
                     tc::sdesc(sbase + OFF_VS + ks * 2048, 8192, 1024), ID_2A, 1);
+      if constexpr (kPrecise) {
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_f16(mS, tc::sdesc(sbase + OFF_QK + 8192 + ks * 2048, 16384, 1024),
+                      tc::sdesc(sbase + OFF_AW + ks * 2048, 8192, 1024), ID_2A, 1);
+      }
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + 8192 + ks * 32, 16, 1024),
@@ -491,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // One warp per 128-wide row.
 template <typename Tin>
 __global__ void chunk_stage_fp16_kernel(const Tin* __restrict__ x, __half* __restrict__ y,
-                                        int64_t rows, int l2) {
+                                        __half* __restrict__ y_lo, int64_t rows, int l2) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -510,6 +557,14 @@ __global__ void chunk_stage_fp16_kernel(const Tin* __restrict__ x, __half* __res
   o.x = pack_h2(v[0], v[1]);
   o.y = pack_h2(v[2], v[3]);
   *reinterpret_cast<uint2*>(y + row * D + lane * 4) = o;
+  if (y_lo) {  // residual x - fp16(x), itself rounded to fp16
+    const __half2* hh = reinterpret_cast<const __half2*>(&o);
+    const float2 a = __half22float2(hh[0]), b = __half22float2(hh[1]);
+    uint2 r;
+    r.x = pack_h2(v[0] - a.x, v[1] - a.y);
+    r.y = pack_h2(v[2] - b.x, v[3] - b.y);
+    *reinterpret_cast<uint2*>(y_lo + row * D + lane * 4) = r;
+  }
 }
 
 // Truncating, flush-to-zero fp32 -> fp16 of deltanet_chunk_last_to_fp16.comp:37-66.
@@ -570,14 +625,15 @@ Status make_map(CUtensorMap* m, const void* base, int64_t pairs, int64_t S) {
   return Status::ok();
 }
 
-template <bool kBf16In, int kOut>
+template <bool kBf16In, int kOut, bool kPrecise>
 Status launch_kernel(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                     const float* g, const float* beta, const float* init, void* out,
-                     float* final_state, int64_t pairs, int S, int* err, cudaStream_t st) {
-  auto kern = chunk_rule_kernel<kBf16In, kOut>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+                     const CUtensorMap& mvlo, const float* g, const float* beta, const float* init,
+                     void* out, float* final_state, int64_t pairs, int S, int* err, cudaStream_t st) {
+  auto kern = chunk_rule_kernel<kBf16In, kOut, kPrecise>;
+  const int smem = kPrecise ? SMEM_BYTES_PRECISE : SMEM_BYTES;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "chunk_rule_kernel smem attribute");
-  kern<<<(unsigned)pairs, kThreads, SMEM_BYTES, st>>>(mq, mk, mv, g, beta, init, out, final_state, S, err);
+  kern<<<(unsigned)pairs, kThreads, smem, st>>>(mq, mk, mv, mvlo, g, beta, init, out, final_state, S, err);
   SPOCK_LAUNCH_CHECK("chunk_rule_kernel");
   return Status::ok();
 }
@@ -602,10 +658,13 @@ Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, co
   const int S = (int)d.seq_len;
   const void *q16 = q, *k16 = k, *v16 = v;
   bool bf16 = d.dtype_in == SPOCK_BF16;
+  const bool precise = d.dtype_in == SPOCK_F32;
+  const void* vlo16 = nullptr;
   if (d.dtype_in == SPOCK_F32 || d.use_qk_l2norm) {
-    // Stage fp16 copies (and the optional L2 norm) in the context's scratch.
+    // Stage fp16 copies (the optional L2 norm, and for fp32 inputs the low
+    // fp16 half of v) in the context's scratch.
     const size_t n = (size_t)pairs * S * D;
-    cudaError_t e = scratch.reserve(3 * n * sizeof(__half));
+    cudaError_t e = scratch.reserve((precise ? 4 : 3) * n * sizeof(__half));
     if (e != cudaSuccess) return Status::err(SPOCK_ERR_ALLOC, "chunk prefill: scratch allocation failed");
     __half* base = static_cast<__half*>(scratch.buf);
     const int64_t rows = (int64_t)pairs * S;
@@ -614,36 +673,43 @@ Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, co
     for (int i = 0; i < 3; ++i) {
       const int l2 = (i < 2) && d.use_qk_l2norm;
       __half* dst = base + i * n;
+      __half* lo = (precise && i == 2) ? base + 3 * n : nullptr;
       if (d.dtype_in == SPOCK_F32)
-        chunk_stage_fp16_kernel<float><<<blocks, 256, 0, stream>>>((const float*)src[i], dst, rows, l2);
+        chunk_stage_fp16_kernel<float><<<blocks, 256, 0, stream>>>((const float*)src[i], dst, lo, rows, l2);
       else if (d.dtype_in == SPOCK_F16)
-        chunk_stage_fp16_kernel<__half><<<blocks, 256, 0, stream>>>((const __half*)src[i], dst, rows, l2);
+        chunk_stage_fp16_kernel<__half><<<blocks, 256, 0, stream>>>((const __half*)src[i], dst, lo, rows, l2);
       else
-        chunk_stage_fp16_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>((const __nv_bfloat16*)src[i], dst, rows, l2);
+        chunk_stage_fp16_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>((const __nv_bfloat16*)src[i], dst, lo, rows, l2);
       SPOCK_LAUNCH_CHECK("chunk_stage_fp16_kernel");
     }
     q16 = base;
     k16 = base + n;
     v16 = base + 2 * n;
+    if (precise) vlo16 = base + 3 * n;
     bf16 = false;
   }
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mvlo;
   Status s = make_map(&mq, q16, pairs, S);
   if (s.code) return s;
   s = make_map(&mk, k16, pairs, S);
   if (s.code) return s;
   s = make_map(&mv, v16, pairs, S);
   if (s.code) return s;
-#define SPOCK_CHUNK_CASE(BF, OUT)                                                              \
-  if (bf16 == BF && d.dtype_out == OUT)                                                        \
-    return launch_kernel<BF, OUT>(mq, mk, mv, g, beta, init, out, final_state, pairs, S,       \
-                                  err_flag, stream);
-  SPOCK_CHUNK_CASE(false, SPOCK_F32)
-  SPOCK_CHUNK_CASE(false, SPOCK_F16)
-  SPOCK_CHUNK_CASE(false, SPOCK_BF16)
-  SPOCK_CHUNK_CASE(true, SPOCK_F32)
-  SPOCK_CHUNK_CASE(true, SPOCK_F16)
-  SPOCK_CHUNK_CASE(true, SPOCK_BF16)
+  s = make_map(&mvlo, precise ? vlo16 : v16, pairs, S);
+  if (s.code) return s;
+#define SPOCK_CHUNK_CASE(BF, OUT, PR)                                                          \
+  if (bf16 == BF && d.dtype_out == OUT && precise == PR)                                       \
+    return launch_kernel<BF, OUT, PR>(mq, mk, mv, mvlo, g, beta, init, out, final_state, pairs, \
+                                      S, err_flag, stream);
+  SPOCK_CHUNK_CASE(false, SPOCK_F32, false)
+  SPOCK_CHUNK_CASE(false, SPOCK_F16, false)
+  SPOCK_CHUNK_CASE(false, SPOCK_BF16, false)
+  SPOCK_CHUNK_CASE(true, SPOCK_F32, false)
+  SPOCK_CHUNK_CASE(true, SPOCK_F16, false)
+  SPOCK_CHUNK_CASE(true, SPOCK_BF16, false)
+  SPOCK_CHUNK_CASE(false, SPOCK_F32, true)
+  SPOCK_CHUNK_CASE(false, SPOCK_F16, true)
+  SPOCK_CHUNK_CASE(false, SPOCK_BF16, true)
 #undef SPOCK_CHUNK_CASE
   return Status::err(SPOCK_ERR_INVALID, "chunk prefill: unknown dtype");
 }

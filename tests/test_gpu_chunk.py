@@ -112,7 +112,7 @@ def test_unsupported_shape_reports_error(cuda_ok):
 def test_last_token_truncation(cuda_ok):
     core = torch.tensor([1.0009765625 + 2 ** -12, -3e-8, 70000.0, float("nan")] * 32, device="cuda").reshape(1, 1, 1, 128)
     core = core.repeat(1, 1, 3, 1).contiguous()
-    out = spock_b200.chunk_last_to_fp16(core).cpu().view(torch.int16).numpy().astype(np.uint16)
+    out = spock_b200.chunk_last_to_fp16(core).cpu().view(torch.int16).numpy().view(np.uint16).ravel()
     assert out[0] == 0x3C01 and out[1] == 0x8000 and out[2] == 0x7C00 and out[3] == 0x7E00
 
 

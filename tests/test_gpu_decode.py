@@ -12,7 +12,7 @@ import torch
 import oracle
 import spock_b200
 from tests.golden.gen import decode_inputs
-from tests.util import fp16_ulp_diff, max_rel
+from tests.util import close16, fp16_ulp_diff, max_rel
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden", "decode_layer0")
@@ -47,7 +47,7 @@ def test_fused_decode_step_matches_oracle(cuda_ok, batch):
     assert np.array_equal(gcs, ccs)                       # conv state: pure data movement
     assert fp16_ulp_diff(gqkv, cqkv).max() <= 1           # conv + SiLU + L2 (exp ulp)
     assert max_rel(gst, cst) <= 1e-5                      # fp32 state
-    assert fp16_ulp_diff(go, co).max() <= ULP, fp16_ulp_diff(go, co).max()
+    assert close16(go, co), (fp16_ulp_diff(go, co).max(), int((fp16_ulp_diff(go, co) > ULP).sum()))
 
 
 def test_decode_two_steps_carry_state(cuda_ok):
@@ -58,7 +58,7 @@ def test_decode_two_steps_carry_state(cuda_ok):
     go, _, _, gst2, _ = gpu_step(d2)
     co, _, _, cst2 = cpu_step(dict(d2, conv_state=ccs, state=cst))
     assert max_rel(gst2, cst2) <= 1e-5
-    assert fp16_ulp_diff(go, co).max() <= ULP
+    assert close16(go, co)
 
 
 def test_recurrent_raw_matches_reference_fixture(cuda_ok):
