@@ -95,6 +95,30 @@ int spock_chunk_prefill(spock_ctx* ctx, const spock_chunk_desc* desc, const void
                         void* stream);
 
 /*
+ * Allocation-free form of spock_chunk_prefill, for callers that cannot
+ * allocate device memory when they call in: code running under an allocator
+ * or memory budget it does not own, code that must not risk the device-wide
+ * synchronisation cudaMalloc/cudaFree can cause, and plugins handed only the
+ * caller's buffers with no context. It has no counterpart in the reference.
+ *
+ * Same arguments, layouts and results as spock_chunk_prefill, but no context:
+ * the fp16 staging of q/k/v (needed for fp32 inputs or use_qk_l2norm=1) goes
+ * to a fixed 16 MiB array compiled into the library, held on every GPU that
+ * loads it until the process exits. Limit when staging is needed:
+ * batch*num_heads*seq_len <= 16384; larger requests return SPOCK_ERR_INVALID
+ * with the reason in spock_last_error(NULL). The call enqueues work on the
+ * current device and calls no cudaMalloc, cudaFree or other allocating routine.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls on a device share the array, so calls whose work overlaps on the
+ * GPU (different streams, no ordering between them) race and must not be made.
+ */
+int spock_chunk_prefill_noalloc(const spock_chunk_desc* desc, const void* q, const void* k,
+                                const void* v, const float* g, const float* beta,
+                                const float* init_state, void* core_out, float* final_state,
+                                void* stream);
+
+/*
  * Last-token extraction of core_attn_out to fp16 by truncation with
  * flush-to-zero, as deltanet_chunk_last_to_fp16.comp:37-66 does for the
  * prefill -> decode handoff (src/runtime/vk_session.cpp:4621-4631).

@@ -35,7 +35,7 @@ F32, F16, BF16 = 0, 1, 2
 
 EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
             "spock_kernel_launch_count", "spock_chunk_prefill", "spock_chunk_last_to_fp16",
-            "spock_deltanet_decode_step", "spock_deltanet_recurrent"]
+            "spock_deltanet_decode_step", "spock_deltanet_recurrent", "spock_chunk_prefill_noalloc"]
 
 
 class SpockError(RuntimeError):
@@ -81,6 +81,7 @@ def lib():
         L.spock_sync.argtypes = [vp, vp]
         L.spock_kernel_launch_count.restype = ctypes.c_uint64
         L.spock_chunk_prefill.argtypes = [vp, ctypes.POINTER(ChunkDesc)] + [vp] * 9
+        L.spock_chunk_prefill_noalloc.argtypes = [ctypes.POINTER(ChunkDesc)] + [vp] * 9
         L.spock_chunk_last_to_fp16.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp]
         L.spock_deltanet_decode_step.argtypes = [vp, ctypes.POINTER(DnLayer), i64] + [vp] * 9
         L.spock_deltanet_recurrent.argtypes = [vp, i64, i32, i32, i32] + [vp] * 8

@@ -37,6 +37,17 @@ struct spock_ctx {
 namespace {
 std::mutex g_err_mu;
 std::string g_err;  // context-less errors
+}  // namespace
+
+namespace spock {
+// Records the text returned by spock_last_error(NULL) (context-less calls).
+void record_global_error(const std::string& msg) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  g_err = msg;
+}
+}  // namespace spock
+
+namespace {
 
 int fail(spock_ctx* ctx, int code, const std::string& msg) {
   if (ctx) {

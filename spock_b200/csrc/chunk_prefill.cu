@@ -723,3 +723,160 @@ Status launch_last_to_fp16(int64_t batch, int64_t H, int64_t S, int64_t V, const
 }
 
 }  // namespace spock
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of spock_chunk_prefill.
+//
+// Some callers cannot allocate device memory at call time: code that runs
+// under an allocator it does not own (a host framework's caching allocator or
+// a memory pool with a hard budget), code that must not synchronise the
+// device (cudaMalloc/cudaFree can), and plugins that receive only the
+// caller's buffers and no context. spock_chunk_prefill grows a per-context
+// scratch buffer with cudaMalloc when it has to stage fp16 copies of the
+// inputs (fp32 inputs, or use_qk_l2norm=1); this variant stages them in a
+// fixed array compiled into the library instead and calls no allocator.
+// ---------------------------------------------------------------------------
+namespace spock {
+void record_global_error(const std::string& msg);
+
+namespace {
+// Staged tensors hold at most this many elements each (batch*num_heads*
+// seq_len*128), i.e. batch*num_heads*seq_len <= 16384 token-heads.
+constexpr size_t kNoAllocMaxElems = size_t(1) << 21;
+constexpr size_t kNoAllocHeader = 256;  // error word of the bounded waits
+constexpr size_t kNoAllocBytes = kNoAllocHeader + 4 * kNoAllocMaxElems * sizeof(__half);  // 16 MiB + 256 B
+
+// Every GPU that loads this library holds this array until the process exits.
+// It is shared by all calls on a device and keeps the last call's contents.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch for the current device. In host code the
+// symbol's name is only a host-side stand-in, so the address must come from
+// cudaGetSymbolAddress, once per device, with that device current.
+Status noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "spock_chunk_prefill_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices)
+    return Status::err(SPOCK_ERR_UNSUPPORTED, "spock_chunk_prefill_noalloc: device ordinal >= 64");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "spock_chunk_prefill_noalloc: cudaGetSymbolAddress");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return Status::ok();
+}
+
+Status chunk_prefill_noalloc(const spock_chunk_desc& d, const void* q, const void* k, const void* v,
+                             const float* g, const float* beta, const float* init, void* out,
+                             float* final_state, cudaStream_t stream) {
+  if (d.key_dim != D || d.value_dim != D || d.chunk_size != C)
+    return Status::err(SPOCK_ERR_UNSUPPORTED,
+                       "chunk prefill: CUDA path implements key_dim=value_dim=128, chunk_size=64");
+  const int64_t pairs = d.batch * d.num_heads;
+  if (pairs > 0x7fffffff || d.seq_len > 0x7fffffff)
+    return Status::err(SPOCK_ERR_INVALID, "chunk prefill: batch*num_heads and seq_len must fit in int32");
+  for (const void* ptr : {q, k, v})
+    if ((uintptr_t)ptr & 15) return Status::err(SPOCK_ERR_INVALID, "chunk prefill: q/k/v must be 16-byte aligned");
+  if (((uintptr_t)final_state & 15) || ((uintptr_t)out & 15) || ((uintptr_t)init & 15))
+    return Status::err(SPOCK_ERR_INVALID, "chunk prefill: outputs and init_state must be 16-byte aligned");
+  const int S = (int)d.seq_len;
+  const bool stage = d.dtype_in == SPOCK_F32 || d.use_qk_l2norm;
+  const size_t n = (size_t)pairs * S * D;
+  if (stage && n > kNoAllocMaxElems)
+    return Status::err(SPOCK_ERR_INVALID,
+                       "spock_chunk_prefill_noalloc: batch*num_heads*seq_len = " + std::to_string(pairs * (int64_t)S) +
+                           " exceeds the fixed scratch of this entry point (max 16384 token-heads when the "
+                           "inputs are fp32 or use_qk_l2norm=1); use spock_chunk_prefill");
+  void* base_v = nullptr;
+  Status s = noalloc_scratch(&base_v);
+  if (s.code) return s;
+  unsigned char* base = static_cast<unsigned char*>(base_v);
+  int* err_flag = reinterpret_cast<int*>(base);
+  // The error word must start at zero; the staged tensors are fully rewritten.
+  cudaError_t e = cudaMemsetAsync(err_flag, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return cuda_status(e, "spock_chunk_prefill_noalloc: cudaMemsetAsync");
+
+  const void *q16 = q, *k16 = k, *v16 = v, *vlo16 = nullptr;
+  bool bf16 = d.dtype_in == SPOCK_BF16;
+  const bool precise = d.dtype_in == SPOCK_F32;
+  if (stage) {
+    __half* st = reinterpret_cast<__half*>(base + kNoAllocHeader);
+    const int64_t rows = (int64_t)pairs * S;
+    const unsigned blocks = (unsigned)((rows + 7) / 8);
+    const void* src[3] = {q, k, v};
+    for (int i = 0; i < 3; ++i) {
+      const int l2 = (i < 2) && d.use_qk_l2norm;
+      __half* dst = st + i * n;
+      __half* lo = (precise && i == 2) ? st + 3 * n : nullptr;
+      if (d.dtype_in == SPOCK_F32)
+        chunk_stage_fp16_kernel<float><<<blocks, 256, 0, stream>>>((const float*)src[i], dst, lo, rows, l2);
+      else if (d.dtype_in == SPOCK_F16)
+        chunk_stage_fp16_kernel<__half><<<blocks, 256, 0, stream>>>((const __half*)src[i], dst, lo, rows, l2);
+      else
+        chunk_stage_fp16_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>((const __nv_bfloat16*)src[i], dst, lo, rows, l2);
+      SPOCK_LAUNCH_CHECK("chunk_stage_fp16_kernel");
+    }
+    q16 = st;
+    k16 = st + n;
+    v16 = st + 2 * n;
+    if (precise) vlo16 = st + 3 * n;
+    bf16 = false;
+  }
+  CUtensorMap mq, mk, mv, mvlo;
+  if ((s = make_map(&mq, q16, pairs, S)).code) return s;
+  if ((s = make_map(&mk, k16, pairs, S)).code) return s;
+  if ((s = make_map(&mv, v16, pairs, S)).code) return s;
+  if ((s = make_map(&mvlo, precise ? vlo16 : v16, pairs, S)).code) return s;
+#define SPOCK_NOALLOC_CASE(BF, OUT, PR)                                                            \
+  if (bf16 == BF && d.dtype_out == OUT && precise == PR)                                           \
+    return launch_kernel<BF, OUT, PR>(mq, mk, mv, mvlo, g, beta, init, out, final_state, pairs, S, \
+                                      err_flag, stream);
+  SPOCK_NOALLOC_CASE(false, SPOCK_F32, false)
+  SPOCK_NOALLOC_CASE(false, SPOCK_F16, false)
+  SPOCK_NOALLOC_CASE(false, SPOCK_BF16, false)
+  SPOCK_NOALLOC_CASE(true, SPOCK_F32, false)
+  SPOCK_NOALLOC_CASE(true, SPOCK_F16, false)
+  SPOCK_NOALLOC_CASE(true, SPOCK_BF16, false)
+  SPOCK_NOALLOC_CASE(false, SPOCK_F32, true)
+  SPOCK_NOALLOC_CASE(false, SPOCK_F16, true)
+  SPOCK_NOALLOC_CASE(false, SPOCK_BF16, true)
+#undef SPOCK_NOALLOC_CASE
+  return Status::err(SPOCK_ERR_INVALID, "chunk prefill: unknown dtype");
+}
+}  // namespace
+}  // namespace spock
+
+extern "C" __attribute__((visibility("default"))) int spock_chunk_prefill_noalloc(
+    const spock_chunk_desc* d, const void* q, const void* k, const void* v, const float* g,
+    const float* beta, const float* init_state, void* core_out, float* final_state, void* stream) {
+  if (!d) {
+    spock::record_global_error("spock_chunk_prefill_noalloc: desc is NULL");
+    return SPOCK_ERR_INVALID;
+  }
+  if (d->batch <= 0 || d->num_heads <= 0 || d->seq_len <= 0 || d->key_dim <= 0 ||
+      d->value_dim <= 0 || d->chunk_size <= 0) {
+    spock::record_global_error("DeltaNet chunk config fields must be non-zero");
+    return SPOCK_ERR_INVALID;
+  }
+  if (!q || !k || !v || !g || !beta || !core_out || !final_state) {
+    spock::record_global_error("spock_chunk_prefill_noalloc: NULL tensor pointer");
+    return SPOCK_ERR_INVALID;
+  }
+  if (d->dtype_in < SPOCK_F32 || d->dtype_in > SPOCK_BF16 || d->dtype_out < SPOCK_F32 ||
+      d->dtype_out > SPOCK_BF16) {
+    spock::record_global_error("spock_chunk_prefill_noalloc: unknown dtype");
+    return SPOCK_ERR_INVALID;
+  }
+  spock::Status s = spock::chunk_prefill_noalloc(*d, q, k, v, g, beta, init_state, core_out,
+                                                 final_state, (cudaStream_t)stream);
+  if (s.code) spock::record_global_error(s.msg);
+  return s.code;
+}
