@@ -1,0 +1,111 @@
+// Device helpers shared by the chunk-rule kernels (serial and pipelined).
+#pragma once
+#include "common.cuh"
+
+namespace spock {
+namespace chunk {
+
+constexpr int C = 64;    // chunk size
+constexpr int D = 128;   // key_dim == value_dim
+constexpr int LDN = 65;  // padded fp32 row stride of the 64x64 N and T matrices
+
+// Byte offset of 16-byte chunk `ch` (0..7) of row `row` in a SWIZZLE_128B
+// region whose rows are 128 bytes (the layout TMA writes and UMMA reads).
+__device__ __forceinline__ uint32_t sw128(int row, int ch) {
+  return (uint32_t)row * 128u + ((uint32_t)(ch ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint4 pack8(const float* x) {
+  return make_uint4(pack_h2(x[0], x[1]), pack_h2(x[2], x[3]), pack_h2(x[4], x[5]),
+                    pack_h2(x[6], x[7]));
+}
+
+__device__ __forceinline__ void unpack8(uint4 u, float* x) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __half22float2(h[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+// T = (I - N)^-1 for strictly lower N (64x64, fp32, row stride LDN).
+// 16x16 diagonal blocks by forward substitution, then off-diagonal blocks by
+// block diagonals: T_ij = T_ii * sum_{k=j}^{i-1} N_ik T_kj. Executed by
+// `nthreads` threads (thread index t), `sync()` synchronises exactly them.
+template <class Sync>
+__device__ __forceinline__ void solve_unit_lower(const float* __restrict__ N, float* __restrict__ T,
+                                                 float* __restrict__ Y, int t, int nthreads, Sync sync) {
+  if (t < 64) {
+    const int o = (t >> 4) * 16, j = t & 15;
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float acc = (i == j) ? 1.f : 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) acc = fmaf(N[(o + i) * LDN + o + m], x[m], acc);
+      x[i] = (i < j) ? 0.f : acc;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) T[(o + i) * LDN + o + j] = x[i];
+  }
+  sync();
+  for (int d = 1; d < 4; ++d) {
+    const int nb = 4 - d;
+    for (int e = t; e < nb * 256; e += nthreads) {
+      const int jb = e >> 8, r = (e >> 4) & 15, c = e & 15, ib = jb + d;
+      float acc = 0.f;
+      for (int col = 16 * jb; col < 16 * ib; ++col)
+        acc = fmaf(N[(16 * ib + r) * LDN + col], T[col * LDN + 16 * jb + c], acc);
+      Y[jb * 256 + r * 16 + c] = acc;
+    }
+    sync();
+    for (int e = t; e < nb * 256; e += nthreads) {
+      const int jb = e >> 8, r = (e >> 4) & 15, c = e & 15, ib = jb + d;
+      float acc = 0.f;
+      for (int m = 0; m <= r; ++m)
+        acc = fmaf(T[(16 * ib + r) * LDN + 16 * ib + m], Y[jb * 256 + m * 16 + c], acc);
+      T[(16 * ib + r) * LDN + 16 * jb + c] = acc;
+    }
+    sync();
+  }
+}
+
+template <int kOut>
+__device__ __forceinline__ void store_row32(void* out, size_t idx, const float (&v)[32]) {
+  if constexpr (kOut == SPOCK_F32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + idx);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else if constexpr (kOut == SPOCK_F16) {
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(out) + idx);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[q] = pack8(&v[8 * q]);
+  } else {
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + idx);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(v[8 * q + 2 * k], v[8 * q + 2 * k + 1]);
+        w[k] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      o[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// kPrecise (fp32 inputs): V arrives as an fp16 hi/lo pair and the products
+// [T diag(beta)] V and K^T [diag(e^{gL-gc}) v_new] are carried to ~22 bits by
+// adding the lo x hi cross terms, so fp32 inputs are not limited to fp16's
+// 11-bit significand where it matters for the state.
+
+}  // namespace chunk
+}  // namespace spock

@@ -1,0 +1,578 @@
+// Warp-specialised, pipelined chunked gated delta rule for sm_100a.
+//
+// Same mathematics and operand formulation as chunk_rule_kernel (see the
+// header of chunk_prefill.cu), reorganised so the tensor cores, TMA and CUDA
+// cores overlap. The per-chunk work splits into a state-INDEPENDENT part
+// (cumulative g, G1 = [Q;K]K^T, P, N, T = (I-N)^-1, W, Q') and a state-
+// DEPENDENT recurrence (S16, U + MMA1, v_new, state update + output). Chunk
+// n+1's independent part runs on the PREP warpgroup while chunk n's recurrence
+// runs on the REC warpgroup:
+//
+//   warps 0-3  PREP : bf16->fp16, g scan, G1 epilogue (P, N), fp32 solve,
+//                     T diag(beta e^g) -> MMA, -W and Q' and T diag(beta) -> smem
+//   warps 4-7  REC  : S -> S16 (+ decay of S in TMEM), v_new epilogue, output
+//                     epilogue and stores, initial / final state
+//   warp 8     TMA  : q/k tiles (2-stage ring) and v (1 stage)
+//   warp 9     MMA  : one thread issues every tcgen05.mma in dependency order
+//
+// CTAs are persistent (grid <= #SMs) and walk a stream of (pair, chunk) items:
+// pair p = blockIdx.x + i*gridDim.x, all of its chunks in order, so the prep
+// of a pair's first chunk overlaps the previous pair's last recurrence.
+//
+// Hand-offs are mbarriers (async proxy + cross-role) and named barriers
+// (inside a warpgroup). Every wait is bounded; a timeout sets a shared abort
+// flag and *err_flag, every role leaves its loop, TMEM is released.
+#include <cuda.h>
+
+#include "chunk_common.cuh"
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace spock {
+namespace pipe {
+namespace {
+
+using chunk::C;
+using chunk::D;
+using chunk::LDN;
+using chunk::pack8;
+using chunk::pack_h2;
+using chunk::store_row32;
+using chunk::sw128;
+using chunk::unpack8;
+
+constexpr int kThreads = 320;
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+// Shared memory (offsets from a 1024-aligned base).
+constexpr int OFF_QK = 0;                    // 2 stages x 32K: per column half [Q 8K | K 8K]
+constexpr int OFF_AW = 64 * 1024;            // [-W ; Q'] K-major 128x128 (2 halves x 16K)
+constexpr int OFF_TB = 96 * 1024;            // [T diag(beta) 8K | zero 8K | P 8K]
+constexpr int OFF_TBE = 120 * 1024;          // T diag(beta e^gc), K-major 64x64
+constexpr int OFF_V = 128 * 1024;            // V, 2 halves x 8K
+constexpr int OFF_SB = 144 * 1024;           // S16 MN-major [kd][v]; later VN | VS
+constexpr int OFF_VN = OFF_SB;
+constexpr int OFF_VS = OFF_SB + 16 * 1024;
+constexpr int OFF_NM = 176 * 1024;
+constexpr int OFF_TM = OFF_NM + C * LDN * 4;
+constexpr int OFF_YM = OFF_TM + C * LDN * 4;
+constexpr int OFF_SMALL = OFF_YM + 3 * 256 * 4;
+constexpr int SMALL_BYTES = 4096;
+constexpr int SMEM_BYTES = OFF_SMALL + SMALL_BYTES + 1024;
+
+enum Bar {
+  QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE, TBE_READY, WT_DONE,
+  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, DRAIN, NUM_BARS
+};
+
+struct Small {
+  float gc[2][C];    // cumulative g per stage
+  float beta[2][C];
+  float eg[2][C];    // exp(gc)
+  uint64_t bar[NUM_BARS];
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(sizeof(Small) <= SMALL_BYTES, "small region");
+
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Barrier over one warpgroup (named barrier `id`, 128 threads) that also ORs a
+// predicate, so every thread of the group takes the same branch afterwards.
+__device__ __forceinline__ bool group_any(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n"
+      " bar.red.or.pred p, %2, 128, q;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void group_sync(int id) {
+  asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
+}
+
+// Bounded wait that also gives up early once another role has aborted.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (tc::mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort) return false;
+  }
+  return false;
+}
+
+struct Items {
+  int nch, pairs, S;
+  __device__ int count() const {
+    const int my_pairs = pairs > (int)blockIdx.x ? (pairs - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    return my_pairs * nch;
+  }
+  __device__ int pair(int n) const { return (int)blockIdx.x + (n / nch) * (int)gridDim.x; }
+  __device__ int chunk(int n) const { return n % nch; }
+};
+
+// ---- TMA producer (one thread) -------------------------------------------------
+__device__ void tma_role(uint8_t* sm, Small* sh, const CUtensorMap* mq, const CUtensorMap* mk,
+                         const CUtensorMap* mv, Items it, int* err) {
+  volatile int* abort = &sh->abort;
+  const int N = it.count();
+  int nv = 0;  // next item whose V is to be loaded
+  for (int n = 0; n < N; ++n) {
+    const int s = n & 1, p = it.pair(n), c = it.chunk(n);
+    if (!wait_bar(&sh->bar[QK_EMPTY0 + s], ((n >> 1) & 1) ^ 1, abort)) goto fail;
+    tc::mbar_arrive_expect_tx(&sh->bar[QK_FULL0 + s], 4 * 64 * 64 * 2);
+    for (int h = 0; h < 2; ++h) {
+      uint8_t* base = sm + OFF_QK + s * 32768 + h * 16384;
+      tc::tma_load_3d(base, mq, &sh->bar[QK_FULL0 + s], h * 64, c * C, p);
+      tc::tma_load_3d(base + 8192, mk, &sh->bar[QK_FULL0 + s], h * 64, c * C, p);
+    }
+    // V of the oldest item whose U product has released the single V buffer
+    for (; nv <= n; ++nv) {
+      if (!wait_bar(&sh->bar[V_EMPTY], (nv & 1) ^ 1, abort)) goto fail;
+      tc::mbar_arrive_expect_tx(&sh->bar[V_FULL], 2 * 64 * 64 * 2);
+      for (int h = 0; h < 2; ++h)
+        tc::tma_load_3d(sm + OFF_V + h * 8192, mv, &sh->bar[V_FULL], h * 64, it.chunk(nv) * C, it.pair(nv));
+    }
+  }
+  return;
+fail:
+  sh->abort = 1;
+  atomicExch(err, 2);
+}
+
+// ---- MMA issuer (one thread) -----------------------------------------------------
+__device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err) {
+  volatile int* abort = &sh->abort;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const uint32_t mS = tb, mD1 = tb + 128, mG1 = tb + 256, mWT = tb + 320;
+  constexpr uint32_t ID_G1 = tc::idesc_f16(128, 64, false, false);
+  constexpr uint32_t ID_U = tc::idesc_f16(128, 128, false, true);
+  constexpr uint32_t ID_WT = tc::idesc_f16(128, 64, true, false);
+  constexpr uint32_t ID_2A = tc::idesc_f16(128, 128, true, true);
+  const int N = it.count();
+
+  auto issue_g1 = [&](int n) -> bool {
+    if (!wait_bar(&sh->bar[PREP_A], n & 1, abort)) return false;
+    tc::tc_fence_after();
+    const uint32_t qk = sbase + OFF_QK + (n & 1) * 32768;
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
+      tc::mma_f16(mG1, tc::sdesc(qk + koff, 16, 1024), tc::sdesc(qk + 8192 + koff, 16, 1024), ID_G1, ks > 0);
+    }
+    tc::mma_commit(&sh->bar[G1_DONE]);
+    return true;
+  };
+  auto issue_wt = [&](int n) -> bool {
+    if (!wait_bar(&sh->bar[TBE_READY], n & 1, abort)) return false;
+    tc::tc_fence_after();
+    const uint32_t k = sbase + OFF_QK + (n & 1) * 32768 + 8192;
+    for (int ks = 0; ks < 4; ++ks)
+      tc::mma_f16(mWT, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_TBE + ks * 32, 16, 1024),
+                  ID_WT, ks > 0);
+    tc::mma_commit(&sh->bar[WT_DONE]);
+    return true;
+  };
+
+  if (N > 0 && (!issue_g1(0) || !issue_wt(0))) goto fail;
+  for (int n = 0; n < N; ++n) {
+    // (a) U + MMA1 of item n: D1 = [T diag(beta); 0] V ; D1 += [-W ; Q'] S16
+    if (!wait_bar(&sh->bar[PREP_DONE], n & 1, abort)) goto fail;
+    if (!wait_bar(&sh->bar[S16_READY], n & 1, abort)) goto fail;
+    tc::tc_fence_after();
+    for (int ks = 0; ks < 4; ++ks)
+      tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + ks * 32, 16, 1024),
+                  tc::sdesc(sbase + OFF_V + ks * 2048, 8192, 1024), ID_U, ks > 0);
+    for (int ks = 0; ks < 8; ++ks)
+      tc::mma_f16(mD1, tc::sdesc(sbase + OFF_AW + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
+                  tc::sdesc(sbase + OFF_SB + ks * 2048, 16384, 1024), ID_U, 1);
+    tc::mma_commit(&sh->bar[M1_DONE]);
+    tc::mma_commit(&sh->bar[V_EMPTY]);
+    // (b) G1 of item n+1 (its prep overlaps this item's recurrence)
+    if (n + 1 < N && !issue_g1(n + 1)) goto fail;
+    // (c) state update + output of item n: S += K^T VS ; D1 += [0 ; P] VN
+    if (!wait_bar(&sh->bar[VN_READY], n & 1, abort)) goto fail;
+    tc::tc_fence_after();
+    {
+      const uint32_t k = sbase + OFF_QK + (n & 1) * 32768 + 8192;
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_f16(mS, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_VS + ks * 2048, 8192, 1024),
+                    ID_2A, 1);
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + 8192 + ks * 32, 16, 1024),
+                    tc::sdesc(sbase + OFF_VN + ks * 2048, 8192, 1024), ID_U, 1);
+    }
+    tc::mma_commit(&sh->bar[M2_DONE]);
+    tc::mma_commit(&sh->bar[QK_EMPTY0 + (n & 1)]);
+    // (d) W^T of item n+1
+    if (n + 1 < N && !issue_wt(n + 1)) goto fail;
+  }
+  return;
+fail:
+  sh->abort = 1;
+  atomicExch(err, 2);
+  // let MMAs already issued finish before TMEM is released (bounded)
+  tc::mma_commit(&sh->bar[DRAIN]);
+  for (uint32_t i = 0; i < kWaitLimit && !tc::mbar_try_wait(&sh->bar[DRAIN], 0); ++i) {
+  }
+}
+
+__device__ __forceinline__ void bf16_to_f16_inplace(uint4* p, int n16, int t, int nt) {
+  for (int i = t; i < n16; i += nt) {
+    uint4 u = p[i];
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[k]));
+      w[k] = pack_h2(f.x, f.y);
+    }
+    p[i] = u;
+  }
+}
+
+constexpr int BAR_PREP = 1, BAR_REC = 2;  // named barriers of the two warpgroups
+
+// ---- PREP warpgroup (warps 0-3; thread t <-> TMEM lane t) ----------------------------
+template <bool kBf16>
+__device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const float* __restrict__ g,
+                          const float* __restrict__ beta, int* err) {
+  volatile int* abort = &sh->abort;
+  const int t = threadIdx.x;
+  const uint32_t lane_base = (uint32_t)((t >> 5) * 32) << 16;
+  const uint32_t tG1 = tb + 256 + lane_base, tWT = tb + 320 + lane_base;
+  float* NM = reinterpret_cast<float*>(sm + OFF_NM);
+  float* TM = reinterpret_cast<float*>(sm + OFF_TM);
+  float* YM = reinterpret_cast<float*>(sm + OFF_YM);
+  __shared__ float s_warp_total;
+  const float scale = 0.08838834764831845f;
+  const int N = it.count();
+  auto sync = [] { group_sync(BAR_PREP); };
+  // all threads wait, then agree (bounded, never leaves a thread behind a named barrier)
+  auto wait_all = [&](int b, uint32_t parity) -> bool {
+    const bool ok = wait_bar(&sh->bar[b], parity, abort);
+    return !group_any(BAR_PREP, !ok);
+  };
+
+  for (int n = 0; n < N; ++n) {
+    const int s = n & 1, p = it.pair(n), c = it.chunk(n);
+    uint8_t* qk = sm + OFF_QK + s * 32768;
+    // 1. g, beta -> cumulative g (two warps, shuffle scan)
+    float gv = 0.f, bv = 0.f;
+    if (t < C) {
+      const int tok = c * C + t;
+      if (tok < it.S) {
+        gv = g[(size_t)p * it.S + tok];
+        bv = beta[(size_t)p * it.S + tok];
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, gv, o);
+        if ((t & 31) >= o) gv += y;
+      }
+      if (t == 31) s_warp_total = gv;
+    }
+    sync();
+    if (t < C) {
+      if (t >= 32) gv += s_warp_total;
+      sh->gc[s][t] = gv;
+      sh->beta[s][t] = bv;
+      sh->eg[s][t] = ex2(gv * kLog2e);
+    }
+    // 2. q/k tile landed: convert, publish for G1
+    if (!wait_all(QK_FULL0 + s, (n >> 1) & 1)) break;
+    if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(qk), 32768 / 16, t, 128);
+    tc::fence_async_smem();
+    sync();
+    if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_A], 0);
+    // 3. G1 epilogue: P row (kept in registers) or N row
+    if (!wait_all(G1_DONE, n & 1)) break;
+    tc::tc_fence_after();
+    uint4 preg[8];
+    {
+      float a[64];
+      tc::tmem_ld32(tG1, *reinterpret_cast<float(*)[32]>(&a[0]));
+      tc::tmem_ld32(tG1 + 32, *reinterpret_cast<float(*)[32]>(&a[32]));
+      const float* gc = sh->gc[s];
+      if (t < C) {
+        const float gi = gc[t];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float x[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int j = q * 8 + k;
+            x[k] = (j <= t) ? (a[j] * scale) * ex2((gi - gc[j]) * kLog2e) : 0.f;
+          }
+          preg[q] = pack8(x);
+        }
+      } else {
+        const int i = t - C;
+        const float gi = gc[i], bi = sh->beta[s][i];
+#pragma unroll
+        for (int j = 0; j < C; ++j) NM[i * LDN + j] = (j < i) ? -(bi * a[j]) * ex2((gi - gc[j]) * kLog2e) : 0.f;
+      }
+    }
+    tc::tc_fence_before();
+    sync();
+    // 4. T = (I - N)^-1
+    chunk::solve_unit_lower(NM, TM, YM, t, 128, sync);
+    // 5. T diag(beta e^gc) -> TBE (for W^T); T diag(beta) kept in registers
+    uint4 tbreg[4];
+    {
+      const int i = t >> 1, jh = (t & 1) * 32;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float x[8], y[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int j = jh + q * 8 + k;
+          const float tv = (j <= i) ? TM[i * LDN + j] : 0.f;
+          x[k] = tv * sh->beta[s][j];
+          y[k] = x[k] * sh->eg[s][j];
+        }
+        tbreg[q] = pack8(x);
+        *reinterpret_cast<uint4*>(sm + OFF_TBE + sw128(i, (jh >> 3) + q)) = pack8(y);
+      }
+    }
+    tc::fence_async_smem();
+    sync();
+    if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[TBE_READY], 0);
+    // 6. once MMA1 of the previous item has read them: T diag(beta) and Q'
+    if (n > 0 && !wait_all(M1_DONE, (n - 1) & 1)) break;
+    {
+      const int i = t >> 1, jh = (t & 1) * 32;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(sm + OFF_TB + sw128(i, (jh >> 3) + q)) = tbreg[q];
+      const int row = t & 63, h = t >> 6;
+      const float f = scale * sh->eg[s][row];
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        float x[8];
+        unpack8(*reinterpret_cast<const uint4*>(qk + h * 16384 + sw128(row, ch)), x);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] *= f;
+        *reinterpret_cast<uint4*>(sm + OFF_AW + h * 16384 + sw128(64 + row, ch)) = pack8(x);
+      }
+    }
+    // 7. -W -> AW rows 0..63 (thread t holds column kd = t of W)
+    if (!wait_all(WT_DONE, n & 1)) break;
+    tc::tc_fence_after();
+    {
+      float w[64];
+      tc::tmem_ld32(tWT, *reinterpret_cast<float(*)[32]>(&w[0]));
+      tc::tmem_ld32(tWT + 32, *reinterpret_cast<float(*)[32]>(&w[32]));
+      const int h = t >> 6, cc = t & 63, ch = cc >> 3, e = cc & 7;
+      uint8_t* base = sm + OFF_AW + h * 16384 + e * 2;
+#pragma unroll
+      for (int i = 0; i < C; ++i) *reinterpret_cast<__half*>(base + sw128(i, ch)) = __float2half_rn(-w[i]);
+    }
+    tc::tc_fence_before();
+    // 8. once the previous item's output MMA has read it: P
+    if (n > 0 && !wait_all(M2_DONE, (n - 1) & 1)) break;
+    if (t < C) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(sm + OFF_TB + 16384 + sw128(t, q)) = preg[q];
+    }
+    // 9. V of this item
+    if (!wait_all(V_FULL, n & 1)) break;
+    if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(sm + OFF_V), 16384 / 16, t, 128);
+    tc::fence_async_smem();
+    sync();
+    if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_DONE], 0);
+  }
+  if (*abort && t == 0) atomicExch(err, 2);
+}
+
+// ---- REC warpgroup (warps 4-7; rt <-> TMEM lane rt) --------------------------------------
+template <int kOut>
+__device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const float* __restrict__ init,
+                         void* __restrict__ out, float* __restrict__ final_state, int* err) {
+  volatile int* abort = &sh->abort;
+  const int rt = threadIdx.x - 128;
+  const uint32_t lane_base = (uint32_t)((rt >> 5) * 32) << 16;
+  const uint32_t tS = tb + lane_base, tD1 = tb + 128 + lane_base;
+  const int N = it.count();
+  auto sync = [] { group_sync(BAR_REC); };
+  auto wait_all = [&](int b, uint32_t parity) -> bool {
+    const bool ok = wait_bar(&sh->bar[b], parity, abort);
+    return !group_any(BAR_REC, !ok);
+  };
+
+  for (int n = 0; n < N; ++n) {
+    const int s = n & 1, p = it.pair(n), c = it.chunk(n);
+    // 1. first chunk of a pair: initial state -> TMEM (row rt = key index)
+    if (c == 0) {
+      const float* src = init ? init + ((size_t)p * D + rt) * D : nullptr;
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        float v[32];
+        if (src) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 x = reinterpret_cast<const float4*>(src + cb * 32)[q];
+            v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = 0.f;
+        }
+        tc::tmem_st32(tS + cb * 32, v);
+      }
+      tc::tmem_st_wait();
+    }
+    // 2. S16 <- S ; S <- e^{gL} S
+    if (!wait_all(PREP_A, n & 1)) break;
+    const float egL = sh->eg[s][C - 1];
+    tc::tc_fence_after();
+#pragma unroll 1
+    for (int cb = 0; cb < 4; ++cb) {
+      float v[32];
+      tc::tmem_ld32(tS + cb * 32, v);
+      uint8_t* dst = sm + OFF_SB + (cb >> 1) * 16384;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(dst + sw128(rt, (cb & 1) * 4 + q)) = pack8(&v[8 * q]);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = mul_rn(v[k], egL);
+      tc::tmem_st32(tS + cb * 32, v);
+    }
+    tc::tmem_st_wait();
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    sync();
+    if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[S16_READY], 0);
+    // 3. v_new rows (lanes 0..63) -> VN, VS
+    if (!wait_all(M1_DONE, n & 1)) break;
+    tc::tc_fence_after();
+    if (rt < C) {
+      const float fs = ex2((sh->gc[s][C - 1] - sh->gc[s][rt]) * kLog2e);
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        float v[32];
+        tc::tmem_ld32(tD1 + cb * 32, v);
+        const int h = cb >> 1;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ch = (cb & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(sm + OFF_VN + h * 8192 + sw128(rt, ch)) = pack8(&v[8 * q]);
+          float y[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) y[k] = v[8 * q + k] * fs;
+          *reinterpret_cast<uint4*>(sm + OFF_VS + h * 8192 + sw128(rt, ch)) = pack8(y);
+        }
+      }
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    sync();
+    if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[VN_READY], 0);
+    // 4. output rows (lanes 64..127); final state after a pair's last chunk
+    if (!wait_all(M2_DONE, n & 1)) break;
+    tc::tc_fence_after();
+    if (rt >= C) {
+      const int tok = c * C + (rt - C);
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        float v[32];
+        tc::tmem_ld32(tD1 + cb * 32, v);
+        if (tok < it.S) store_row32<kOut>(out, ((size_t)p * it.S + tok) * D + cb * 32, v);
+      }
+    }
+    if (c == it.nch - 1) {
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        float v[32];
+        tc::tmem_ld32(tS + cb * 32, v);
+        float4* dst = reinterpret_cast<float4*>(final_state + ((size_t)p * D + rt) * D + cb * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+    }
+    tc::tc_fence_before();
+  }
+  if (*abort && rt == 0) atomicExch(err, 2);
+}
+
+template <bool kBf16, int kOut>
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_pipe_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                      const __grid_constant__ CUtensorMap tmv, const float* __restrict__ g,
+                      const float* __restrict__ beta, const float* __restrict__ init, void* __restrict__ out,
+                      float* __restrict__ final_state, int S, int pairs, int* __restrict__ err_flag) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Small* sh = reinterpret_cast<Small*>(sm + OFF_SMALL);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < NUM_BARS; ++b) tc::mbar_init(&sh->bar[b], 1);
+    sh->abort = 0;
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmq);
+    tc::prefetch_tmap(&tmk);
+    tc::prefetch_tmap(&tmv);
+  }
+  if (warp == 9) {
+    tc::tmem_alloc(&sh->tmem_base, 512);
+    tc::tmem_relinquish();
+  }
+  for (int i = threadIdx.x; i < 8192 / 16; i += kThreads)  // zero block of [T diag(beta) | 0 | P]
+    reinterpret_cast<uint4*>(sm + OFF_TB + 8192)[i] = make_uint4(0, 0, 0, 0);
+  tc::fence_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tb = sh->tmem_base;
+  const Items it{(S + C - 1) / C, pairs, S};
+  if (warp < 4) {
+    prep_role<kBf16>(sm, sh, tb, it, g, beta, err_flag);
+  } else if (warp < 8) {
+    rec_role<kOut>(sm, sh, tb, it, init, out, final_state, err_flag);
+  } else if (warp == 8) {
+    if (lane == 0) tma_role(sm, sh, &tmq, &tmk, &tmv, it, err_flag);
+  } else if (lane == 0) {
+    mma_role(sm, sh, tb, it, err_flag);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) tc::tmem_dealloc(tb, 512);
+}
+
+}  // namespace
+}  // namespace pipe
+
+// Launches the pipelined kernel: persistent, grid = min(pairs, #SMs).
+template <bool kBf16, int kOut>
+Status launch_chunk_pipeline(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                             const float* g, const float* beta, const float* init, void* out,
+                             float* final_state, int64_t pairs, int S, int* err, cudaStream_t st) {
+  auto kern = pipe::chunk_pipe_kernel<kBf16, kOut>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pipe::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "chunk_pipe_kernel smem attribute");
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned grid = (unsigned)(pairs < sms ? pairs : sms);
+  kern<<<grid, pipe::kThreads, pipe::SMEM_BYTES, st>>>(mq, mk, mv, g, beta, init, out, final_state, S,
+                                                       (int)pairs, err);
+  SPOCK_LAUNCH_CHECK("chunk_pipe_kernel");
+  return Status::ok();
+}
+
+#define SPOCK_PIPE_INST(BF, OUT)                                                                   \
+  template Status launch_chunk_pipeline<BF, OUT>(const CUtensorMap&, const CUtensorMap&,          \
+                                                 const CUtensorMap&, const float*, const float*,  \
+                                                 const float*, void*, float*, int64_t, int, int*, \
+                                                 cudaStream_t);
+SPOCK_PIPE_INST(false, SPOCK_F32)
+SPOCK_PIPE_INST(false, SPOCK_F16)
+SPOCK_PIPE_INST(false, SPOCK_BF16)
+SPOCK_PIPE_INST(true, SPOCK_F32)
+SPOCK_PIPE_INST(true, SPOCK_F16)
+SPOCK_PIPE_INST(true, SPOCK_BF16)
+#undef SPOCK_PIPE_INST
+
+}  // namespace spock

@@ -30,17 +30,25 @@
 // code in *err_flag, releases TMEM and returns.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "chunk_scratch.h"
 #include "common.cuh"
 #include "tc.cuh"
+#include "chunk_common.cuh"
 
 namespace spock {
 namespace {
 
-constexpr int C = 64;    // chunk size
-constexpr int D = 128;   // key_dim == value_dim
+using chunk::C;
+using chunk::D;
+using chunk::LDN;
+using chunk::sw128;
+using chunk::pack_h2;
+using chunk::pack8;
+using chunk::unpack8;
+using chunk::store_row32;
 constexpr int kThreads = 128;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
@@ -53,7 +61,6 @@ constexpr int OFF_AW = 80 * 1024;          // [-W ; Q'] K-major 128x128
 constexpr int OFF_SB = 112 * 1024;         // S16, MN-major [kd][v] (aliased by VN/VS)
 constexpr int OFF_VN = OFF_SB;             // v_new16, MN-major [token][v]
 constexpr int OFF_VS = OFF_SB + 16 * 1024; // v_new16 * e^{gL-gc}
-constexpr int LDN = 65;                    // padded fp32 row stride of N and T
 constexpr int OFF_NM = 144 * 1024;
 constexpr int OFF_TM = OFF_NM + C * LDN * 4;
 constexpr int OFF_YM = OFF_TM + C * LDN * 4;
@@ -67,102 +74,6 @@ constexpr int OFF_TBL = OFF_VLO + 16 * 1024;
 constexpr int SMEM_BYTES_PRECISE = OFF_TBL + 16 * 1024 + 1024;
 static_assert(OFF_VLO >= OFF_SMALL + 2048, "smem regions overlap");
 
-// Byte offset of 16-byte chunk `ch` (0..7) of row `row` in a SWIZZLE_128B
-// region whose rows are 128 bytes (the layout TMA writes and UMMA reads).
-__device__ __forceinline__ uint32_t sw128(int row, int ch) {
-  return (uint32_t)row * 128u + ((uint32_t)(ch ^ (row & 7)) << 4);
-}
-
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-  __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-__device__ __forceinline__ uint4 pack8(const float* x) {
-  return make_uint4(pack_h2(x[0], x[1]), pack_h2(x[2], x[3]), pack_h2(x[4], x[5]),
-                    pack_h2(x[6], x[7]));
-}
-
-__device__ __forceinline__ void unpack8(uint4 u, float* x) {
-  const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 f = __half22float2(h[i]);
-    x[2 * i] = f.x;
-    x[2 * i + 1] = f.y;
-  }
-}
-
-// T = (I - N)^-1 for strictly lower N (64x64, fp32, row stride LDN).
-// 16x16 diagonal blocks by forward substitution, then off-diagonal blocks by
-// block diagonals: T_ij = T_ii * sum_{k=j}^{i-1} N_ik T_kj.
-__device__ void solve_unit_lower(const float* __restrict__ N, float* __restrict__ T,
-                                 float* __restrict__ Y) {
-  const int t = threadIdx.x;
-  if (t < 64) {
-    const int o = (t >> 4) * 16, j = t & 15;
-    float x[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float acc = (i == j) ? 1.f : 0.f;
-#pragma unroll
-      for (int m = 0; m < i; ++m) acc = fmaf(N[(o + i) * LDN + o + m], x[m], acc);
-      x[i] = (i < j) ? 0.f : acc;
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) T[(o + i) * LDN + o + j] = x[i];
-  }
-  __syncthreads();
-  for (int d = 1; d < 4; ++d) {
-    const int nb = 4 - d;
-    for (int e = t; e < nb * 256; e += kThreads) {
-      const int jb = e >> 8, r = (e >> 4) & 15, c = e & 15, ib = jb + d;
-      float acc = 0.f;
-      for (int col = 16 * jb; col < 16 * ib; ++col)
-        acc = fmaf(N[(16 * ib + r) * LDN + col], T[col * LDN + 16 * jb + c], acc);
-      Y[jb * 256 + r * 16 + c] = acc;
-    }
-    __syncthreads();
-    for (int e = t; e < nb * 256; e += kThreads) {
-      const int jb = e >> 8, r = (e >> 4) & 15, c = e & 15, ib = jb + d;
-      float acc = 0.f;
-      for (int m = 0; m <= r; ++m)
-        acc = fmaf(T[(16 * ib + r) * LDN + 16 * ib + m], Y[jb * 256 + m * 16 + c], acc);
-      T[(16 * ib + r) * LDN + 16 * jb + c] = acc;
-    }
-    __syncthreads();
-  }
-}
-
-template <int kOut>
-__device__ __forceinline__ void store_row32(void* out, size_t idx, const float (&v)[32]) {
-  if constexpr (kOut == SPOCK_F32) {
-    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + idx);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-  } else if constexpr (kOut == SPOCK_F16) {
-    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(out) + idx);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) o[q] = pack8(&v[8 * q]);
-  } else {
-    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + idx);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t w[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        __nv_bfloat162 b = __floats2bfloat162_rn(v[8 * q + 2 * k], v[8 * q + 2 * k + 1]);
-        w[k] = *reinterpret_cast<uint32_t*>(&b);
-      }
-      o[q] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-  }
-}
-
-// kPrecise (fp32 inputs): V arrives as an fp16 hi/lo pair and the products
-// [T diag(beta)] V and K^T [diag(e^{gL-gc}) v_new] are carried to ~22 bits by
-// adding the lo x hi cross terms, so fp32 inputs are not limited to fp16's
-// 11-bit significand where it matters for the state.
 template <bool kBf16In, int kOut, bool kPrecise>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_rule_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
@@ -352,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     // ---- 4. T = (I - N)^-1, then T diag(beta), T diag(beta e^gc), Q' --------
-    solve_unit_lower(NM, TM, YM);
+    chunk::solve_unit_lower(NM, TM, YM, t, kThreads, [] { __syncthreads(); });
     {
       const int i = t >> 1, jh = (t & 1) * 32;
 #pragma unroll
@@ -590,6 +501,16 @@ __global__ void last_to_fp16_kernel(const float* __restrict__ core, uint16_t* __
 
 // ---- host side ---------------------------------------------------------------
 
+// SPOCK_CHUNK_SERIAL=1 selects the serial kernel for 16-bit inputs too
+// (diagnostics: both kernels implement the same contract).
+bool serial_forced() {
+  static const bool v = [] {
+    const char* e = getenv("SPOCK_CHUNK_SERIAL");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -625,10 +546,23 @@ Status make_map(CUtensorMap* m, const void* base, int64_t pairs, int64_t S) {
   return Status::ok();
 }
 
+}  // namespace
+template <bool kBf16, int kOut>
+Status launch_chunk_pipeline(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                             const float* g, const float* beta, const float* init, void* out,
+                             float* final_state, int64_t pairs, int S, int* err, cudaStream_t st);
+namespace {
+
+// fp16/bf16 inputs run the pipelined kernel (chunk_pipeline.cu); fp32 inputs
+// run the serial kernel above in its precise (hi/lo) form.
 template <bool kBf16In, int kOut, bool kPrecise>
 Status launch_kernel(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                      const CUtensorMap& mvlo, const float* g, const float* beta, const float* init,
                      void* out, float* final_state, int64_t pairs, int S, int* err, cudaStream_t st) {
+  if constexpr (!kPrecise) {
+    if (!serial_forced())
+      return launch_chunk_pipeline<kBf16In, kOut>(mq, mk, mv, g, beta, init, out, final_state, pairs, S, err, st);
+  }
   auto kern = chunk_rule_kernel<kBf16In, kOut, kPrecise>;
   const int smem = kPrecise ? SMEM_BYTES_PRECISE : SMEM_BYTES;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

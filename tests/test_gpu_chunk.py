@@ -122,3 +122,14 @@ def test_state_is_resident_long_sequence(cuda_ok):
     ro, rs = batched_oracle(q, k, v, g, b)
     go, gs = run_gpu(q, k, v, g, b)
     assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL, (max_rel(go, ro), max_rel(gs, rs))
+
+
+def test_more_pairs_than_sms_bf16(cuda_ok):
+    """160 (sequence, head) pairs > 148 SMs: persistent CTAs walk several pairs,
+    ragged last chunk, nonzero initial state."""
+    q, k, v, g, b = chunk_inputs(16, 130, seed=13, batch=10)
+    qb, kb, vb = (torch.from_numpy(x).bfloat16().float().numpy() for x in (q, k, v))
+    init = np.random.default_rng(13).standard_normal((10, 16, 128, 128)).astype(np.float32) * 0.05
+    ro, rs = batched_oracle(qb, kb, vb, g, b, init)
+    go, gs = run_gpu(qb, kb, vb, g, b, init, dtype_in=torch.bfloat16, dtype_out=torch.float32)
+    assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL, (max_rel(go, ro), max_rel(gs, rs))
