@@ -77,6 +77,80 @@ __device__ __forceinline__ void solve_unit_lower(const float* __restrict__ N, fl
   }
 }
 
+// Same inverse, register-blocked for a 128-thread warpgroup: T has row stride
+// LDT (16-byte aligned rows), every off-diagonal product is computed as 1x4
+// output tiles with fully unrolled 16-wide k loops (independent FMAs, float4
+// loads of T), so the solve is throughput- rather than latency-bound.
+constexpr int LDT = 68;
+
+template <int kD, class Sync>
+__device__ __forceinline__ void solve_level(const float* __restrict__ N, float* __restrict__ T,
+                                            float* __restrict__ Y, int t, Sync sync) {
+  constexpr int nb = 4 - kD;
+  // Y_ij = sum_{k=j}^{i-1} N_ik T_kj   (i = j + kD)
+  for (int e = t; e < nb * 64; e += 128) {
+    const int jb = e >> 6, r = (e >> 2) & 15, c0 = (e & 3) * 4, ib = jb + kD;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    const float* nrow = N + (16 * ib + r) * LDN;
+#pragma unroll
+    for (int kb = 0; kb < kD; ++kb) {
+      const int col0 = 16 * (jb + kb);
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float nv = nrow[col0 + m];
+        const float4 tv = *reinterpret_cast<const float4*>(T + (col0 + m) * LDT + 16 * jb + c0);
+        a0 = fmaf(nv, tv.x, a0);
+        a1 = fmaf(nv, tv.y, a1);
+        a2 = fmaf(nv, tv.z, a2);
+        a3 = fmaf(nv, tv.w, a3);
+      }
+    }
+    *reinterpret_cast<float4*>(Y + jb * 256 + r * 16 + c0) = make_float4(a0, a1, a2, a3);
+  }
+  sync();
+  // T_ij = T_ii Y_ij  (T_ii lower triangular, zeros above its diagonal)
+  for (int e = t; e < nb * 64; e += 128) {
+    const int jb = e >> 6, r = (e >> 2) & 15, c0 = (e & 3) * 4, ib = jb + kD;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    const float* trow = T + (16 * ib + r) * LDT + 16 * ib;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const float tv = trow[m];
+      const float4 y = *reinterpret_cast<const float4*>(Y + jb * 256 + m * 16 + c0);
+      a0 = fmaf(tv, y.x, a0);
+      a1 = fmaf(tv, y.y, a1);
+      a2 = fmaf(tv, y.z, a2);
+      a3 = fmaf(tv, y.w, a3);
+    }
+    *reinterpret_cast<float4*>(T + (16 * ib + r) * LDT + 16 * jb + c0) = make_float4(a0, a1, a2, a3);
+  }
+  sync();
+}
+
+// N: row stride LDN; T: row stride LDT (only the lower triangle incl. the
+// diagonal is written; callers mask j > i); Y: 768 floats, 16-byte aligned.
+template <class Sync>
+__device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ N, float* __restrict__ T,
+                                                      float* __restrict__ Y, int t, Sync sync) {
+  if (t < 64) {
+    const int o = (t >> 4) * 16, j = t & 15;
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float acc = (i == j) ? 1.f : 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) acc = fmaf(N[(o + i) * LDN + o + m], x[m], acc);
+      x[i] = (i < j) ? 0.f : acc;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) T[(o + i) * LDT + o + j] = x[i];
+  }
+  sync();
+  solve_level<1>(N, T, Y, t, sync);
+  solve_level<2>(N, T, Y, t, sync);
+  solve_level<3>(N, T, Y, t, sync);
+}
+
 template <int kOut>
 __device__ __forceinline__ void store_row32(void* out, size_t idx, const float (&v)[32]) {
   if constexpr (kOut == SPOCK_F32) {

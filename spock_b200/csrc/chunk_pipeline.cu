@@ -54,8 +54,8 @@ constexpr int OFF_SB = 144 * 1024;           // S16 MN-major [kd][v]; later VN |
 constexpr int OFF_VN = OFF_SB;
 constexpr int OFF_VS = OFF_SB + 16 * 1024;
 constexpr int OFF_NM = 176 * 1024;
-constexpr int OFF_TM = OFF_NM + C * LDN * 4;
-constexpr int OFF_YM = OFF_TM + C * LDN * 4;
+constexpr int OFF_TM = OFF_NM + 16896;          // N: 64 x 65 fp32 (16640 B), padded to 16 B
+constexpr int OFF_YM = OFF_TM + C * chunk::LDT * 4;
 constexpr int OFF_SMALL = OFF_YM + 3 * 256 * 4;
 constexpr int SMALL_BYTES = 4096;
 constexpr int SMEM_BYTES = OFF_SMALL + SMALL_BYTES + 1024;
@@ -320,7 +320,7 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     tc::tc_fence_before();
     sync();
     // 4. T = (I - N)^-1
-    chunk::solve_unit_lower(NM, TM, YM, t, 128, sync);
+    chunk::solve_unit_lower_fast(NM, TM, YM, t, sync);
     // 5. T diag(beta e^gc) -> TBE (for W^T); T diag(beta) kept in registers
     uint4 tbreg[4];
     {
@@ -328,10 +328,13 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float x[8], y[8];
+        const float4 t0 = *reinterpret_cast<const float4*>(TM + i * chunk::LDT + jh + q * 8);
+        const float4 t1 = *reinterpret_cast<const float4*>(TM + i * chunk::LDT + jh + q * 8 + 4);
+        const float tr[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int j = jh + q * 8 + k;
-          const float tv = (j <= i) ? TM[i * LDN + j] : 0.f;
+          const float tv = (j <= i) ? tr[k] : 0.f;
           x[k] = tv * sh->beta[s][j];
           y[k] = x[k] * sh->eg[s][j];
         }
