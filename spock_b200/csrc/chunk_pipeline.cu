@@ -107,6 +107,25 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
   return false;
 }
 
+// Optional per-phase cycle accounting (compile with -DSPOCK_PHASE_PROF; never
+// in the shipped library): one row of 32 counters per CTA and role.
+#ifdef SPOCK_PHASE_PROF
+__device__ unsigned long long g_phase_prof[148 * 4 * 32];
+#define PROF_DECL long long _pt = clock64();
+#define PROF_MARK(role, k)                                                                   \
+  do {                                                                                       \
+    long long _now = clock64();                                                              \
+    if ((threadIdx.x & 127) == 0 && blockIdx.x < 148)                                        \
+      g_phase_prof[(blockIdx.x * 4 + (role)) * 32 + (k)] += (unsigned long long)(_now - _pt); \
+    _pt = _now;                                                                              \
+  } while (0)
+#else
+#define PROF_DECL
+#define PROF_MARK(role, k) \
+  do {                     \
+  } while (0)
+#endif
+
 struct Items {
   int nch, pairs, S;
   __device__ int count() const {
@@ -258,6 +277,7 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     return !group_any(BAR_PREP, !ok);
   };
 
+  PROF_DECL
   for (int n = 0; n < N; ++n) {
     const int s = n & 1, p = it.pair(n), c = it.chunk(n);
     uint8_t* qk = sm + OFF_QK + s * 32768;
@@ -283,14 +303,18 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
       sh->beta[s][t] = bv;
       sh->eg[s][t] = ex2(gv * kLog2e);
     }
+    PROF_MARK(0, 0);
     // 2. q/k tile landed: convert, publish for G1
     if (!wait_all(QK_FULL0 + s, (n >> 1) & 1)) break;
+    PROF_MARK(0, 1);
     if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(qk), 32768 / 16, t, 128);
     tc::fence_async_smem();
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_A], 0);
+    PROF_MARK(0, 2);
     // 3. G1 epilogue: P row (kept in registers) or N row
     if (!wait_all(G1_DONE, n & 1)) break;
+    PROF_MARK(0, 3);
     tc::tc_fence_after();
     uint4 preg[8];
     {
@@ -319,8 +343,10 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     }
     tc::tc_fence_before();
     sync();
+    PROF_MARK(0, 4);
     // 4. T = (I - N)^-1
     chunk::solve_unit_lower_fast(NM, TM, YM, t, sync);
+    PROF_MARK(0, 5);
     // 5. T diag(beta e^gc) -> TBE (for W^T); T diag(beta) kept in registers
     uint4 tbreg[4];
     {
@@ -345,8 +371,10 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     tc::fence_async_smem();
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[TBE_READY], 0);
+    PROF_MARK(0, 6);
     // 6. once MMA1 of the previous item has read them: T diag(beta) and Q'
     if (n > 0 && !wait_all(M1_DONE, (n - 1) & 1)) break;
+    PROF_MARK(0, 7);
     {
       const int i = t >> 1, jh = (t & 1) * 32;
 #pragma unroll
@@ -362,8 +390,10 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
         *reinterpret_cast<uint4*>(sm + OFF_AW + h * 16384 + sw128(64 + row, ch)) = pack8(x);
       }
     }
+    PROF_MARK(0, 8);
     // 7. -W -> AW rows 0..63 (thread t holds column kd = t of W)
     if (!wait_all(WT_DONE, n & 1)) break;
+    PROF_MARK(0, 9);
     tc::tc_fence_after();
     {
       float w[64];
@@ -375,18 +405,23 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
       for (int i = 0; i < C; ++i) *reinterpret_cast<__half*>(base + sw128(i, ch)) = __float2half_rn(-w[i]);
     }
     tc::tc_fence_before();
+    PROF_MARK(0, 10);
     // 8. once the previous item's output MMA has read it: P
     if (n > 0 && !wait_all(M2_DONE, (n - 1) & 1)) break;
+    PROF_MARK(0, 11);
     if (t < C) {
 #pragma unroll
       for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(sm + OFF_TB + 16384 + sw128(t, q)) = preg[q];
     }
+    PROF_MARK(0, 12);
     // 9. V of this item
     if (!wait_all(V_FULL, n & 1)) break;
+    PROF_MARK(0, 13);
     if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(sm + OFF_V), 16384 / 16, t, 128);
     tc::fence_async_smem();
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_DONE], 0);
+    PROF_MARK(0, 14);
   }
   if (*abort && t == 0) atomicExch(err, 2);
 }
@@ -406,6 +441,7 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     return !group_any(BAR_REC, !ok);
   };
 
+  PROF_DECL
   for (int n = 0; n < N; ++n) {
     const int s = n & 1, p = it.pair(n), c = it.chunk(n);
     // 1. first chunk of a pair: initial state -> TMEM (row rt = key index)
@@ -428,8 +464,10 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
       }
       tc::tmem_st_wait();
     }
+    PROF_MARK(1, 0);
     // 2. S16 <- S ; S <- e^{gL} S
     if (!wait_all(PREP_A, n & 1)) break;
+    PROF_MARK(1, 1);
     const float egL = sh->eg[s][C - 1];
     tc::tc_fence_after();
 #pragma unroll 1
@@ -448,8 +486,10 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     tc::tc_fence_before();
     sync();
     if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[S16_READY], 0);
+    PROF_MARK(1, 2);
     // 3. v_new rows (lanes 0..63) -> VN, VS
     if (!wait_all(M1_DONE, n & 1)) break;
+    PROF_MARK(1, 3);
     tc::tc_fence_after();
     if (rt < C) {
       const float fs = ex2((sh->gc[s][C - 1] - sh->gc[s][rt]) * kLog2e);
@@ -473,8 +513,10 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     tc::tc_fence_before();
     sync();
     if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[VN_READY], 0);
+    PROF_MARK(1, 4);
     // 4. output rows (lanes 64..127); final state after a pair's last chunk
     if (!wait_all(M2_DONE, n & 1)) break;
+    PROF_MARK(1, 5);
     tc::tc_fence_after();
     if (rt >= C) {
       const int tok = c * C + (rt - C);
@@ -496,6 +538,7 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
       }
     }
     tc::tc_fence_before();
+    PROF_MARK(1, 6);
   }
   if (*abort && rt == 0) atomicExch(err, 2);
 }
@@ -579,3 +622,10 @@ SPOCK_PIPE_INST(true, SPOCK_BF16)
 #undef SPOCK_PIPE_INST
 
 }  // namespace spock
+
+#ifdef SPOCK_PHASE_PROF
+extern "C" __attribute__((visibility("default"))) int spock_debug_phase_profile(unsigned long long* out, int n) {
+  if (n > 148 * 4 * 32) n = 148 * 4 * 32;
+  return (int)cudaMemcpyFromSymbol(out, spock::pipe::g_phase_prof, n * sizeof(unsigned long long));
+}
+#endif
