@@ -77,18 +77,18 @@ __device__ __forceinline__ void solve_unit_lower(const float* __restrict__ N, fl
   }
 }
 
-// Same inverse, register-blocked for a 128-thread warpgroup: T has row stride
+// Same inverse, register-blocked for kNT threads: T has row stride
 // LDT (16-byte aligned rows), every off-diagonal product is computed as 1x4
 // output tiles with fully unrolled 16-wide k loops (independent FMAs, float4
 // loads of T), so the solve is throughput- rather than latency-bound.
 constexpr int LDT = 68;
 
-template <int kD, class Sync>
+template <int kNT, int kD, class Sync>
 __device__ __forceinline__ void solve_level(const float* __restrict__ N, float* __restrict__ T,
                                             float* __restrict__ Y, int t, Sync sync) {
   constexpr int nb = 4 - kD;
   // Y_ij = sum_{k=j}^{i-1} N_ik T_kj   (i = j + kD)
-  for (int e = t; e < nb * 64; e += 128) {
+  for (int e = t; e < nb * 64; e += kNT) {
     const int jb = e >> 6, r = (e >> 2) & 15, c0 = (e & 3) * 4, ib = jb + kD;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     const float* nrow = N + (16 * ib + r) * LDN;
@@ -109,7 +109,7 @@ __device__ __forceinline__ void solve_level(const float* __restrict__ N, float* 
   }
   sync();
   // T_ij = T_ii Y_ij  (T_ii lower triangular, zeros above its diagonal)
-  for (int e = t; e < nb * 64; e += 128) {
+  for (int e = t; e < nb * 64; e += kNT) {
     const int jb = e >> 6, r = (e >> 2) & 15, c0 = (e & 3) * 4, ib = jb + kD;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     const float* trow = T + (16 * ib + r) * LDT + 16 * ib;
@@ -129,7 +129,7 @@ __device__ __forceinline__ void solve_level(const float* __restrict__ N, float* 
 
 // N: row stride LDN; T: row stride LDT (only the lower triangle incl. the
 // diagonal is written; callers mask j > i); Y: 768 floats, 16-byte aligned.
-template <class Sync>
+template <int kNT, class Sync>
 __device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ N, float* __restrict__ T,
                                                       float* __restrict__ Y, int t, Sync sync) {
   if (t < 64) {
@@ -146,9 +146,9 @@ __device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ 
     for (int i = 0; i < 16; ++i) T[(o + i) * LDT + o + j] = x[i];
   }
   sync();
-  solve_level<1>(N, T, Y, t, sync);
-  solve_level<2>(N, T, Y, t, sync);
-  solve_level<3>(N, T, Y, t, sync);
+  solve_level<kNT, 1>(N, T, Y, t, sync);
+  solve_level<kNT, 2>(N, T, Y, t, sync);
+  solve_level<kNT, 3>(N, T, Y, t, sync);
 }
 
 template <int kOut>

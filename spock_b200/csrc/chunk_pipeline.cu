@@ -41,7 +41,10 @@ using chunk::store_row32;
 using chunk::sw128;
 using chunk::unpack8;
 
-constexpr int kThreads = 320;
+constexpr int kPrepThreads = 256;  // warps 0-7
+constexpr int kRecBase = 256;      // warps 8-11
+constexpr int kTmaWarp = 12, kMmaWarp = 13;
+constexpr int kThreads = 448;
 constexpr uint32_t kWaitLimit = 1u << 24;
 
 // Shared memory (offsets from a 1024-aligned base).
@@ -69,6 +72,7 @@ struct Small {
   float gc[2][C];    // cumulative g per stage
   float beta[2][C];
   float eg[2][C];    // exp(gc)
+  float gl[2][C];    // gc * log2(e)
   uint64_t bar[NUM_BARS];
   uint32_t tmem_base;
   int abort;
@@ -84,18 +88,18 @@ __device__ __forceinline__ float ex2(float x) {
 
 // Barrier over one warpgroup (named barrier `id`, 128 threads) that also ORs a
 // predicate, so every thread of the group takes the same branch afterwards.
-__device__ __forceinline__ bool group_any(int id, bool pred) {
+__device__ __forceinline__ bool group_any(int id, int nthreads, bool pred) {
   uint32_t r;
   asm volatile(
       "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n"
-      " bar.red.or.pred p, %2, 128, q;\n selp.u32 %0, 1, 0, p;\n}"
+      " bar.red.or.pred p, %2, %3, q;\n selp.u32 %0, 1, 0, p;\n}"
       : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
       : "memory");
   return r != 0;
 }
-__device__ __forceinline__ void group_sync(int id) {
-  asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
+__device__ __forceinline__ void group_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Bounded wait that also gives up early once another role has aborted.
@@ -256,39 +260,48 @@ __device__ __forceinline__ void bf16_to_f16_inplace(uint4* p, int n16, int t, in
 
 constexpr int BAR_PREP = 1, BAR_REC = 2;  // named barriers of the two warpgroups
 
-// ---- PREP warpgroup (warps 0-3; thread t <-> TMEM lane t) ----------------------------
+// ---- PREP (warps 0-7, 256 threads; TMEM lane l = t & 127, column half hf = t >> 7) ----
 template <bool kBf16>
 __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const float* __restrict__ g,
                           const float* __restrict__ beta, int* err) {
   volatile int* abort = &sh->abort;
-  const int t = threadIdx.x;
-  const uint32_t lane_base = (uint32_t)((t >> 5) * 32) << 16;
-  const uint32_t tG1 = tb + 256 + lane_base, tWT = tb + 320 + lane_base;
+  const int t = threadIdx.x, l = t & 127, hf = t >> 7;
+  const uint32_t lane_base = (uint32_t)((l >> 5) * 32) << 16;
+  const uint32_t tG1 = tb + 256 + lane_base + hf * 32, tWT = tb + 320 + lane_base + hf * 32;
   float* NM = reinterpret_cast<float*>(sm + OFF_NM);
   float* TM = reinterpret_cast<float*>(sm + OFF_TM);
   float* YM = reinterpret_cast<float*>(sm + OFF_YM);
   __shared__ float s_warp_total;
   const float scale = 0.08838834764831845f;
   const int N = it.count();
-  auto sync = [] { group_sync(BAR_PREP); };
-  // all threads wait, then agree (bounded, never leaves a thread behind a named barrier)
+  auto sync = [] { group_sync(BAR_PREP, kPrepThreads); };
   auto wait_all = [&](int b, uint32_t parity) -> bool {
     const bool ok = wait_bar(&sh->bar[b], parity, abort);
-    return !group_any(BAR_PREP, !ok);
+    return !group_any(BAR_PREP, kPrepThreads, !ok);
   };
+  auto load_gb = [&](int n, float& gv, float& bv) {
+    gv = 0.f;
+    bv = 0.f;
+    if (n < N && t < C) {
+      const int tok = it.chunk(n) * C + t;
+      if (tok < it.S) {
+        const size_t idx = (size_t)it.pair(n) * it.S + tok;
+        gv = g[idx];
+        bv = beta[idx];
+      }
+    }
+  };
+  float gnext, bnext;
+  load_gb(0, gnext, bnext);
 
   PROF_DECL
   for (int n = 0; n < N; ++n) {
-    const int s = n & 1, p = it.pair(n), c = it.chunk(n);
+    const int s = n & 1;
     uint8_t* qk = sm + OFF_QK + s * 32768;
-    // 1. g, beta -> cumulative g (two warps, shuffle scan)
-    float gv = 0.f, bv = 0.f;
+    // 1. cumulative g (shuffle scan over two warps); g/beta of n+1 prefetched
+    float gv = gnext, bv = bnext;
+    load_gb(n + 1, gnext, bnext);
     if (t < C) {
-      const int tok = c * C + t;
-      if (tok < it.S) {
-        gv = g[(size_t)p * it.S + tok];
-        bv = beta[(size_t)p * it.S + tok];
-      }
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const float y = __shfl_up_sync(0xffffffffu, gv, o);
@@ -300,6 +313,7 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     if (t < C) {
       if (t >= 32) gv += s_warp_total;
       sh->gc[s][t] = gv;
+      sh->gl[s][t] = gv * kLog2e;
       sh->beta[s][t] = bv;
       sh->eg[s][t] = ex2(gv * kLog2e);
     }
@@ -307,65 +321,69 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     // 2. q/k tile landed: convert, publish for G1
     if (!wait_all(QK_FULL0 + s, (n >> 1) & 1)) break;
     PROF_MARK(0, 1);
-    if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(qk), 32768 / 16, t, 128);
+    if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(qk), 32768 / 16, t, kPrepThreads);
     tc::fence_async_smem();
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_A], 0);
     PROF_MARK(0, 2);
-    // 3. G1 epilogue: P row (kept in registers) or N row
+    // 3. G1 epilogue on 32 columns: P row (kept in registers) or N row
     if (!wait_all(G1_DONE, n & 1)) break;
     PROF_MARK(0, 3);
     tc::tc_fence_after();
-    uint4 preg[8];
+    uint4 preg[4];
     {
-      float a[64];
-      tc::tmem_ld32(tG1, *reinterpret_cast<float(*)[32]>(&a[0]));
-      tc::tmem_ld32(tG1 + 32, *reinterpret_cast<float(*)[32]>(&a[32]));
-      const float* gc = sh->gc[s];
-      if (t < C) {
-        const float gi = gc[t];
+      float a[32];
+      tc::tmem_ld32(tG1, a);
+      const float* gl = sh->gl[s];
+      const int j0 = hf * 32;
+      if (l < C) {
+        const float gi = gl[l];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           float x[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const int j = q * 8 + k;
-            x[k] = (j <= t) ? (a[j] * scale) * ex2((gi - gc[j]) * kLog2e) : 0.f;
+            const int j = j0 + q * 8 + k;
+            x[k] = (j <= l) ? (a[q * 8 + k] * scale) * ex2(gi - gl[j]) : 0.f;
           }
           preg[q] = pack8(x);
         }
       } else {
-        const int i = t - C;
-        const float gi = gc[i], bi = sh->beta[s][i];
+        const int i = l - C;
+        const float gi = gl[i], nb = -sh->beta[s][i];
 #pragma unroll
-        for (int j = 0; j < C; ++j) NM[i * LDN + j] = (j < i) ? -(bi * a[j]) * ex2((gi - gc[j]) * kLog2e) : 0.f;
+        for (int k = 0; k < 32; ++k) {
+          const int j = j0 + k;
+          NM[i * LDN + j] = (j < i) ? (nb * a[k]) * ex2(gi - gl[j]) : 0.f;
+        }
       }
     }
     tc::tc_fence_before();
     sync();
     PROF_MARK(0, 4);
     // 4. T = (I - N)^-1
-    chunk::solve_unit_lower_fast(NM, TM, YM, t, sync);
+    chunk::solve_unit_lower_fast<kPrepThreads>(NM, TM, YM, t, sync);
     PROF_MARK(0, 5);
     // 5. T diag(beta e^gc) -> TBE (for W^T); T diag(beta) kept in registers
-    uint4 tbreg[4];
+    uint4 tbreg[2];
     {
-      const int i = t >> 1, jh = (t & 1) * 32;
+      const int i = t >> 2;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
+        const int ch = (t & 3) * 2 + q, j0 = ch * 8;
         float x[8], y[8];
-        const float4 t0 = *reinterpret_cast<const float4*>(TM + i * chunk::LDT + jh + q * 8);
-        const float4 t1 = *reinterpret_cast<const float4*>(TM + i * chunk::LDT + jh + q * 8 + 4);
+        const float4 t0 = *reinterpret_cast<const float4*>(TM + i * chunk::LDT + j0);
+        const float4 t1 = *reinterpret_cast<const float4*>(TM + i * chunk::LDT + j0 + 4);
         const float tr[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const int j = jh + q * 8 + k;
+          const int j = j0 + k;
           const float tv = (j <= i) ? tr[k] : 0.f;
           x[k] = tv * sh->beta[s][j];
           y[k] = x[k] * sh->eg[s][j];
         }
         tbreg[q] = pack8(x);
-        *reinterpret_cast<uint4*>(sm + OFF_TBE + sw128(i, (jh >> 3) + q)) = pack8(y);
+        *reinterpret_cast<uint4*>(sm + OFF_TBE + sw128(i, ch)) = pack8(y);
       }
     }
     tc::fence_async_smem();
@@ -376,13 +394,14 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     if (n > 0 && !wait_all(M1_DONE, (n - 1) & 1)) break;
     PROF_MARK(0, 7);
     {
-      const int i = t >> 1, jh = (t & 1) * 32;
+      const int i = t >> 2;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(sm + OFF_TB + sw128(i, (jh >> 3) + q)) = tbreg[q];
-      const int row = t & 63, h = t >> 6;
+      for (int q = 0; q < 2; ++q) *reinterpret_cast<uint4*>(sm + OFF_TB + sw128(i, (t & 3) * 2 + q)) = tbreg[q];
+      const int row = t & 63, h = (t >> 6) & 1, c0 = (t >> 7) * 4;
       const float f = scale * sh->eg[s][row];
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
+      for (int cc = 0; cc < 4; ++cc) {
+        const int ch = c0 + cc;
         float x[8];
         unpack8(*reinterpret_cast<const uint4*>(qk + h * 16384 + sw128(row, ch)), x);
 #pragma unroll
@@ -391,33 +410,34 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
       }
     }
     PROF_MARK(0, 8);
-    // 7. -W -> AW rows 0..63 (thread t holds column kd = t of W)
+    // 7. -W -> AW rows 0..63 (lane l holds column kd = l of W, rows hf*32 ..)
     if (!wait_all(WT_DONE, n & 1)) break;
     PROF_MARK(0, 9);
     tc::tc_fence_after();
     {
-      float w[64];
-      tc::tmem_ld32(tWT, *reinterpret_cast<float(*)[32]>(&w[0]));
-      tc::tmem_ld32(tWT + 32, *reinterpret_cast<float(*)[32]>(&w[32]));
-      const int h = t >> 6, cc = t & 63, ch = cc >> 3, e = cc & 7;
+      float w[32];
+      tc::tmem_ld32(tWT, w);
+      const int h = l >> 6, cc = l & 63, ch = cc >> 3, e = cc & 7;
       uint8_t* base = sm + OFF_AW + h * 16384 + e * 2;
 #pragma unroll
-      for (int i = 0; i < C; ++i) *reinterpret_cast<__half*>(base + sw128(i, ch)) = __float2half_rn(-w[i]);
+      for (int k = 0; k < 32; ++k)
+        *reinterpret_cast<__half*>(base + sw128(hf * 32 + k, ch)) = __float2half_rn(-w[k]);
     }
     tc::tc_fence_before();
     PROF_MARK(0, 10);
     // 8. once the previous item's output MMA has read it: P
     if (n > 0 && !wait_all(M2_DONE, (n - 1) & 1)) break;
     PROF_MARK(0, 11);
-    if (t < C) {
+    if (l < C) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(sm + OFF_TB + 16384 + sw128(t, q)) = preg[q];
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(sm + OFF_TB + 16384 + sw128(l, hf * 4 + q)) = preg[q];
     }
     PROF_MARK(0, 12);
     // 9. V of this item
     if (!wait_all(V_FULL, n & 1)) break;
     PROF_MARK(0, 13);
-    if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(sm + OFF_V), 16384 / 16, t, 128);
+    if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(sm + OFF_V), 16384 / 16, t, kPrepThreads);
     tc::fence_async_smem();
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_DONE], 0);
@@ -431,14 +451,14 @@ template <int kOut>
 __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const float* __restrict__ init,
                          void* __restrict__ out, float* __restrict__ final_state, int* err) {
   volatile int* abort = &sh->abort;
-  const int rt = threadIdx.x - 128;
+  const int rt = threadIdx.x - kRecBase;
   const uint32_t lane_base = (uint32_t)((rt >> 5) * 32) << 16;
   const uint32_t tS = tb + lane_base, tD1 = tb + 128 + lane_base;
   const int N = it.count();
-  auto sync = [] { group_sync(BAR_REC); };
+  auto sync = [] { group_sync(BAR_REC, 128); };
   auto wait_all = [&](int b, uint32_t parity) -> bool {
     const bool ok = wait_bar(&sh->bar[b], parity, abort);
-    return !group_any(BAR_REC, !ok);
+    return !group_any(BAR_REC, 128, !ok);
   };
 
   PROF_DECL
@@ -561,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::prefetch_tmap(&tmk);
     tc::prefetch_tmap(&tmv);
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc::tmem_alloc(&sh->tmem_base, 512);
     tc::tmem_relinquish();
   }
@@ -573,18 +593,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::tc_fence_after();
   const uint32_t tb = sh->tmem_base;
   const Items it{(S + C - 1) / C, pairs, S};
-  if (warp < 4) {
+  if (warp < kRecBase / 32) {
     prep_role<kBf16>(sm, sh, tb, it, g, beta, err_flag);
-  } else if (warp < 8) {
+  } else if (warp < kTmaWarp) {
     rec_role<kOut>(sm, sh, tb, it, init, out, final_state, err_flag);
-  } else if (warp == 8) {
+  } else if (warp == kTmaWarp) {
     if (lane == 0) tma_role(sm, sh, &tmq, &tmk, &tmv, it, err_flag);
   } else if (lane == 0) {
     mma_role(sm, sh, tb, it, err_flag);
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 9) tc::tmem_dealloc(tb, 512);
+  if (warp == kMmaWarp) tc::tmem_dealloc(tb, 512);
 }
 
 }  // namespace
