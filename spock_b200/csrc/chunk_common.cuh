@@ -87,28 +87,26 @@ template <int kNT, int kD, class Sync>
 __device__ __forceinline__ void solve_level(const float* __restrict__ N, float* __restrict__ T,
                                             float* __restrict__ Y, int t, Sync sync) {
   constexpr int nb = 4 - kD;
-  // Y_ij = sum_{k=j}^{i-1} N_ik T_kj   (i = j + kD)
-  for (int e = t; e < nb * 64; e += kNT) {
-    const int jb = e >> 6, r = (e >> 2) & 15, c0 = (e & 3) * 4, ib = jb + kD;
+  // Partial products, split over the kD source blocks so every thread runs at
+  // most one 16-step chain:  Y[jb][kb] = N_{ib, jb+kb} T_{jb+kb, jb}   (ib = jb + kD)
+  for (int e = t; e < nb * kD * 64; e += kNT) {
+    const int jb = e / (kD * 64), rem = e % (kD * 64), kb = rem >> 6;
+    const int r = (rem >> 2) & 15, c0 = (rem & 3) * 4, ib = jb + kD, col0 = 16 * (jb + kb);
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    const float* nrow = N + (16 * ib + r) * LDN;
+    const float* nrow = N + (16 * ib + r) * LDN + col0;
 #pragma unroll
-    for (int kb = 0; kb < kD; ++kb) {
-      const int col0 = 16 * (jb + kb);
-#pragma unroll
-      for (int m = 0; m < 16; ++m) {
-        const float nv = nrow[col0 + m];
-        const float4 tv = *reinterpret_cast<const float4*>(T + (col0 + m) * LDT + 16 * jb + c0);
-        a0 = fmaf(nv, tv.x, a0);
-        a1 = fmaf(nv, tv.y, a1);
-        a2 = fmaf(nv, tv.z, a2);
-        a3 = fmaf(nv, tv.w, a3);
-      }
+    for (int m = 0; m < 16; ++m) {
+      const float nv = nrow[m];
+      const float4 tv = *reinterpret_cast<const float4*>(T + (col0 + m) * LDT + 16 * jb + c0);
+      a0 = fmaf(nv, tv.x, a0);
+      a1 = fmaf(nv, tv.y, a1);
+      a2 = fmaf(nv, tv.z, a2);
+      a3 = fmaf(nv, tv.w, a3);
     }
-    *reinterpret_cast<float4*>(Y + jb * 256 + r * 16 + c0) = make_float4(a0, a1, a2, a3);
+    *reinterpret_cast<float4*>(Y + (jb * kD + kb) * 256 + r * 16 + c0) = make_float4(a0, a1, a2, a3);
   }
   sync();
-  // T_ij = T_ii Y_ij  (T_ii lower triangular, zeros above its diagonal)
+  // T_ij = T_ii sum_kb Y[jb][kb]  (T_ii lower triangular, zeros above its diagonal)
   for (int e = t; e < nb * 64; e += kNT) {
     const int jb = e >> 6, r = (e >> 2) & 15, c0 = (e & 3) * 4, ib = jb + kD;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
@@ -116,7 +114,15 @@ __device__ __forceinline__ void solve_level(const float* __restrict__ N, float* 
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
       const float tv = trow[m];
-      const float4 y = *reinterpret_cast<const float4*>(Y + jb * 256 + m * 16 + c0);
+      float4 y = *reinterpret_cast<const float4*>(Y + (jb * kD) * 256 + m * 16 + c0);
+#pragma unroll
+      for (int kb = 1; kb < kD; ++kb) {
+        const float4 z = *reinterpret_cast<const float4*>(Y + (jb * kD + kb) * 256 + m * 16 + c0);
+        y.x += z.x;
+        y.y += z.y;
+        y.z += z.z;
+        y.w += z.w;
+      }
       a0 = fmaf(tv, y.x, a0);
       a1 = fmaf(tv, y.y, a1);
       a2 = fmaf(tv, y.z, a2);
@@ -128,7 +134,9 @@ __device__ __forceinline__ void solve_level(const float* __restrict__ N, float* 
 }
 
 // N: row stride LDN; T: row stride LDT (only the lower triangle incl. the
-// diagonal is written; callers mask j > i); Y: 768 floats, 16-byte aligned.
+// diagonal is written; callers mask j > i); Y: 1024 floats, 16-byte aligned.
+// Diagonal 16x16 blocks by right-looking substitution: once x_m is final it
+// updates every later row at once (15 independent FMAs per step, not a chain).
 template <int kNT, class Sync>
 __device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ N, float* __restrict__ T,
                                                       float* __restrict__ Y, int t, Sync sync) {
@@ -136,14 +144,14 @@ __device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ 
     const int o = (t >> 4) * 16, j = t & 15;
     float x[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float acc = (i == j) ? 1.f : 0.f;
+    for (int i = 0; i < 16; ++i) x[i] = (i == j) ? 1.f : 0.f;
 #pragma unroll
-      for (int m = 0; m < i; ++m) acc = fmaf(N[(o + i) * LDN + o + m], x[m], acc);
-      x[i] = (i < j) ? 0.f : acc;
+    for (int m = 0; m < 15; ++m) {
+#pragma unroll
+      for (int i = m + 1; i < 16; ++i) x[i] = fmaf(N[(o + i) * LDN + o + m], x[m], x[i]);
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) T[(o + i) * LDT + o + j] = x[i];
+    for (int i = 0; i < 16; ++i) T[(o + i) * LDT + o + j] = (i < j) ? 0.f : x[i];
   }
   sync();
   solve_level<kNT, 1>(N, T, Y, t, sync);

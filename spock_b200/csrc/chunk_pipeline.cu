@@ -59,13 +59,13 @@ constexpr int OFF_VS = OFF_SB + 16 * 1024;
 constexpr int OFF_NM = 176 * 1024;
 constexpr int OFF_TM = OFF_NM + 16896;          // N: 64 x 65 fp32 (16640 B), padded to 16 B
 constexpr int OFF_YM = OFF_TM + C * chunk::LDT * 4;
-constexpr int OFF_SMALL = OFF_YM + 3 * 256 * 4;
+constexpr int OFF_SMALL = OFF_YM + 4 * 256 * 4;
 constexpr int SMALL_BYTES = 4096;
 constexpr int SMEM_BYTES = OFF_SMALL + SMALL_BYTES + 1024;
 
 enum Bar {
   QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE, TBE_READY, WT_DONE,
-  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, DRAIN, NUM_BARS
+  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, DRAIN, NUM_BARS
 };
 
 struct Small {
@@ -73,6 +73,8 @@ struct Small {
   float beta[2][C];
   float eg[2][C];    // exp(gc)
   float gl[2][C];    // gc * log2(e)
+  float graw[2][C];  // g, beta of an item, prefetched by cp.async one item ahead
+  float braw[2][C];
   uint64_t bar[NUM_BARS];
   uint32_t tmem_base;
   int abort;
@@ -102,6 +104,15 @@ __device__ __forceinline__ void group_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// 4-byte asynchronous global->shared copy; src_bytes 0 writes a zero.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(tc::smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Bounded wait that also gives up early once another role has aborted.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
@@ -115,18 +126,27 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 // in the shipped library): one row of 32 counters per CTA and role.
 #ifdef SPOCK_PHASE_PROF
 __device__ unsigned long long g_phase_prof[148 * 4 * 32];
-#define PROF_DECL long long _pt = clock64();
-#define PROF_MARK(role, k)                                                                   \
-  do {                                                                                       \
-    long long _now = clock64();                                                              \
-    if ((threadIdx.x & 127) == 0 && blockIdx.x < 148)                                        \
-      g_phase_prof[(blockIdx.x * 4 + (role)) * 32 + (k)] += (unsigned long long)(_now - _pt); \
-    _pt = _now;                                                                              \
+#define PROF_DECL                       \
+  long long _pt = clock64();            \
+  unsigned long long _acc[16] = {};
+#define PROF_MARK(role, k)                                  \
+  do {                                                      \
+    long long _now = clock64();                             \
+    _acc[k] += (unsigned long long)(_now - _pt);            \
+    _pt = _now;                                             \
+  } while (0)
+#define PROF_FLUSH(role)                                                        \
+  do {                                                                          \
+    if ((threadIdx.x & 127) == 0 && blockIdx.x < 148)                           \
+      for (int _k = 0; _k < 16; ++_k) g_phase_prof[(blockIdx.x * 4 + (role)) * 32 + _k] += _acc[_k]; \
   } while (0)
 #else
 #define PROF_DECL
 #define PROF_MARK(role, k) \
   do {                     \
+  } while (0)
+#define PROF_FLUSH(role) \
+  do {                   \
   } while (0)
 #endif
 
@@ -170,11 +190,13 @@ fail:
 }
 
 // ---- MMA issuer (one thread) -----------------------------------------------------
+template <bool kBf16>
 __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err) {
   volatile int* abort = &sh->abort;
   const uint32_t sbase = tc::smem_u32(sm);
   const uint32_t mS = tb, mD1 = tb + 128, mG1 = tb + 256, mWT = tb + 320;
-  constexpr uint32_t ID_G1 = tc::idesc_f16(128, 64, false, false);
+  // G1 reads the raw input tiles (bf16 or fp16); every other product is fp16
+  constexpr uint32_t ID_G1 = tc::idesc_f16(128, 64, false, false) | (kBf16 ? (1u << 7) | (1u << 10) : 0u);
   constexpr uint32_t ID_U = tc::idesc_f16(128, 128, false, true);
   constexpr uint32_t ID_WT = tc::idesc_f16(128, 64, true, false);
   constexpr uint32_t ID_2A = tc::idesc_f16(128, 128, true, true);
@@ -279,28 +301,30 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     const bool ok = wait_bar(&sh->bar[b], parity, abort);
     return !group_any(BAR_PREP, kPrepThreads, !ok);
   };
-  auto load_gb = [&](int n, float& gv, float& bv) {
-    gv = 0.f;
-    bv = 0.f;
+  auto prefetch_gb = [&](int n) {  // cp.async: not waited for by the barriers in between
     if (n < N && t < C) {
       const int tok = it.chunk(n) * C + t;
-      if (tok < it.S) {
-        const size_t idx = (size_t)it.pair(n) * it.S + tok;
-        gv = g[idx];
-        bv = beta[idx];
-      }
+      const bool in = tok < it.S;
+      const size_t idx = in ? (size_t)it.pair(n) * it.S + tok : 0;
+      cp_async4(&sh->graw[n & 1][t], g + idx, in ? 4u : 0u);
+      cp_async4(&sh->braw[n & 1][t], beta + idx, in ? 4u : 0u);
     }
+    cp_async_commit();
   };
-  float gnext, bnext;
-  load_gb(0, gnext, bnext);
+  prefetch_gb(0);
 
   PROF_DECL
   for (int n = 0; n < N; ++n) {
     const int s = n & 1;
     uint8_t* qk = sm + OFF_QK + s * 32768;
     // 1. cumulative g (shuffle scan over two warps); g/beta of n+1 prefetched
-    float gv = gnext, bv = bnext;
-    load_gb(n + 1, gnext, bnext);
+    cp_async_wait_all();
+    float gv = 0.f, bv = 0.f;
+    if (t < C) {
+      gv = sh->graw[s][t];
+      bv = sh->braw[s][t];
+    }
+    prefetch_gb(n + 1);
     if (t < C) {
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -321,8 +345,6 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     // 2. q/k tile landed: convert, publish for G1
     if (!wait_all(QK_FULL0 + s, (n >> 1) & 1)) break;
     PROF_MARK(0, 1);
-    if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(qk), 32768 / 16, t, kPrepThreads);
-    tc::fence_async_smem();
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_A], 0);
     PROF_MARK(0, 2);
@@ -357,6 +379,11 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
           NM[i * LDN + j] = (j < i) ? (nb * a[k]) * ex2(gi - gl[j]) : 0.f;
         }
       }
+    }
+    if constexpr (kBf16) {  // K -> fp16 in place (G1, the only bf16 reader, is done)
+      bf16_to_f16_inplace(reinterpret_cast<uint4*>(qk + 8192), 8192 / 16, t, kPrepThreads);
+      bf16_to_f16_inplace(reinterpret_cast<uint4*>(qk + 16384 + 8192), 8192 / 16, t, kPrepThreads);
+      tc::fence_async_smem();
     }
     tc::tc_fence_before();
     sync();
@@ -403,7 +430,18 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
       for (int cc = 0; cc < 4; ++cc) {
         const int ch = c0 + cc;
         float x[8];
-        unpack8(*reinterpret_cast<const uint4*>(qk + h * 16384 + sw128(row, ch)), x);
+        const uint4 raw = *reinterpret_cast<const uint4*>(qk + h * 16384 + sw128(row, ch));
+        if constexpr (kBf16) {
+          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f2 = __bfloat1622float2(b2[k]);
+            x[2 * k] = f2.x;
+            x[2 * k + 1] = f2.y;
+          }
+        } else {
+          unpack8(raw, x);
+        }
 #pragma unroll
         for (int k = 0; k < 8; ++k) x[k] *= f;
         *reinterpret_cast<uint4*>(sm + OFF_AW + h * 16384 + sw128(64 + row, ch)) = pack8(x);
@@ -434,32 +472,46 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
         *reinterpret_cast<uint4*>(sm + OFF_TB + 16384 + sw128(l, hf * 4 + q)) = preg[q];
     }
     PROF_MARK(0, 12);
-    // 9. V of this item
-    if (!wait_all(V_FULL, n & 1)) break;
+    // 9. V of this item (converted to fp16 by the REC warpgroup)
+    if (!wait_all(V_CONV, n & 1)) break;
     PROF_MARK(0, 13);
-    if constexpr (kBf16) bf16_to_f16_inplace(reinterpret_cast<uint4*>(sm + OFF_V), 16384 / 16, t, kPrepThreads);
     tc::fence_async_smem();
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_DONE], 0);
     PROF_MARK(0, 14);
   }
+  cp_async_wait_all();
+  PROF_FLUSH(0);
   if (*abort && t == 0) atomicExch(err, 2);
 }
 
 // ---- REC warpgroup (warps 4-7; rt <-> TMEM lane rt) --------------------------------------
-template <int kOut>
+template <bool kBf16, int kOut>
 __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const float* __restrict__ init,
                          void* __restrict__ out, float* __restrict__ final_state, int* err) {
   volatile int* abort = &sh->abort;
   const int rt = threadIdx.x - kRecBase;
   const uint32_t lane_base = (uint32_t)((rt >> 5) * 32) << 16;
   const uint32_t tS = tb + lane_base, tD1 = tb + 128 + lane_base;
-  const int N = it.count();
+  int N = it.count();
   auto sync = [] { group_sync(BAR_REC, 128); };
   auto wait_all = [&](int b, uint32_t parity) -> bool {
     const bool ok = wait_bar(&sh->bar[b], parity, abort);
     return !group_any(BAR_REC, 128, !ok);
   };
+
+  // V of item m -> fp16 in place, then published to PREP as V_CONV
+  auto convert_v = [&](int m) -> bool {
+    if (!wait_all(V_FULL, m & 1)) return false;
+    if constexpr (kBf16) {
+      bf16_to_f16_inplace(reinterpret_cast<uint4*>(sm + OFF_V), 16384 / 16, rt, 128);
+      tc::fence_async_smem();
+    }
+    sync();
+    if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[V_CONV], 0);
+    return true;
+  };
+  if (N > 0 && !convert_v(0)) N = 0;
 
   PROF_DECL
   for (int n = 0; n < N; ++n) {
@@ -533,6 +585,7 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     tc::tc_fence_before();
     sync();
     if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[VN_READY], 0);
+    if (n + 1 < N && !convert_v(n + 1)) break;
     PROF_MARK(1, 4);
     // 4. output rows (lanes 64..127); final state after a pair's last chunk
     if (!wait_all(M2_DONE, n & 1)) break;
@@ -560,6 +613,7 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     tc::tc_fence_before();
     PROF_MARK(1, 6);
   }
+  PROF_FLUSH(1);
   if (*abort && rt == 0) atomicExch(err, 2);
 }
 
@@ -596,11 +650,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < kRecBase / 32) {
     prep_role<kBf16>(sm, sh, tb, it, g, beta, err_flag);
   } else if (warp < kTmaWarp) {
-    rec_role<kOut>(sm, sh, tb, it, init, out, final_state, err_flag);
+    rec_role<kBf16, kOut>(sm, sh, tb, it, init, out, final_state, err_flag);
   } else if (warp == kTmaWarp) {
     if (lane == 0) tma_role(sm, sh, &tmq, &tmk, &tmv, it, err_flag);
   } else if (lane == 0) {
-    mma_role(sm, sh, tb, it, err_flag);
+    mma_role<kBf16>(sm, sh, tb, it, err_flag);
   }
   tc::tc_fence_before();
   __syncthreads();
