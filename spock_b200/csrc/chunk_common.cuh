@@ -159,6 +159,133 @@ __device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ 
   solve_level<kNT, 3>(N, T, Y, t, sync);
 }
 
+// ---- warp-level 16x16 products for the triangular inverse --------------------
+// mma.sync m16n8k16 (fp16 in, fp32 accumulate) with every fp32 operand split
+// as hi + lo fp16 and three products (hi*hi + hi*lo + lo*hi), which keeps the
+// result close to fp32 accuracy. Fragment layouts of m16n8k16 (g = lane/4,
+// q = lane%4): A rows g, g+8 x cols 2q, 2q+1, 2q+8, 2q+9; B rows 2q, 2q+1,
+// 2q+8, 2q+9 x col g; C rows g, g+8 x cols 2q, 2q+1.
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// c[nt][.] += A(16x16, stride lda) * B(16x16, stride ldb), both fp32 in shared memory.
+__device__ __forceinline__ void mm16_acc(const float* __restrict__ A, int lda, const float* __restrict__ B,
+                                         int ldb, float (&c)[2][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  uint32_t ah[4], al[4];
+  split2(A[g * lda + 2 * q], A[g * lda + 2 * q + 1], ah[0], al[0]);
+  split2(A[(g + 8) * lda + 2 * q], A[(g + 8) * lda + 2 * q + 1], ah[1], al[1]);
+  split2(A[g * lda + 2 * q + 8], A[g * lda + 2 * q + 9], ah[2], al[2]);
+  split2(A[(g + 8) * lda + 2 * q + 8], A[(g + 8) * lda + 2 * q + 9], ah[3], al[3]);
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int col = nt * 8 + g;
+    uint32_t bh0, bl0, bh1, bl1;
+    split2(B[(2 * q) * ldb + col], B[(2 * q + 1) * ldb + col], bh0, bl0);
+    split2(B[(2 * q + 8) * ldb + col], B[(2 * q + 9) * ldb + col], bh1, bl1);
+    mma16816(c[nt], ah, bh0, bh1);
+    mma16816(c[nt], ah, bl0, bl1);
+    mma16816(c[nt], al, bh0, bh1);
+  }
+}
+
+__device__ __forceinline__ void frag_zero(float (&c)[2][4]) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) c[nt][k] = 0.f;
+}
+
+// D(16x16, stride ldd) = c (+ D when add).
+__device__ __forceinline__ void frag_store(float* D, int ldd, const float (&c)[2][4], bool add) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int col = nt * 8 + 2 * q;
+    float* r0 = D + g * ldd + col;
+    float* r1 = D + (g + 8) * ldd + col;
+    if (add) {
+      r0[0] += c[nt][0];
+      r0[1] += c[nt][1];
+      r1[0] += c[nt][2];
+      r1[1] += c[nt][3];
+    } else {
+      r0[0] = c[nt][0];
+      r0[1] = c[nt][1];
+      r1[0] = c[nt][2];
+      r1[1] = c[nt][3];
+    }
+  }
+}
+
+// T = (I - N)^-1 on tensor cores. Warp w < 4 inverts diagonal block w as
+// (I+N)(I+N^2)(I+N^4)(I+N^8) (N_ww^16 = 0); then block diagonals d = 1..3,
+// one warp per block: T_ij = T_ii * sum_k N_ik T_kj. Y: 4 x 256 fp32 scratch
+// (one 16x16 per warp). `sync()` synchronises all participating warps.
+template <class Sync>
+__device__ __forceinline__ void solve_unit_lower_tc(const float* __restrict__ N, float* __restrict__ T,
+                                                    float* __restrict__ Y, int warp, Sync sync) {
+  const int lane = threadIdx.x & 31;
+  if (warp < 4) {
+    const int o = warp * 16;
+    float* Tb = T + o * LDT + o;
+    const float* Nb = N + o * LDN + o;
+    float* Pw = Y + warp * 256;  // powers of N_ww, stride 16
+    for (int e = lane; e < 256; e += 32) {
+      const int i = e >> 4, j = e & 15;
+      const float nv = Nb[i * LDN + j];
+      Tb[i * LDT + j] = (i == j ? 1.f : 0.f) + nv;  // R = I + N
+      Pw[e] = nv;
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (int step = 0; step < 3; ++step) {
+      float c[2][4];
+      frag_zero(c);
+      mm16_acc(Pw, 16, Pw, 16, c);  // P <- P^2   (N^2, N^4, N^8)
+      __syncwarp();
+      frag_store(Pw, 16, c, false);
+      __syncwarp();
+      frag_zero(c);
+      mm16_acc(Tb, LDT, Pw, 16, c);  // R <- R + R P
+      __syncwarp();
+      frag_store(Tb, LDT, c, true);
+      __syncwarp();
+    }
+  }
+  sync();
+#pragma unroll 1
+  for (int d = 1; d < 4; ++d) {
+    if (warp < 4 - d) {
+      const int jb = warp, ib = jb + d;
+      float c[2][4];
+      frag_zero(c);
+      for (int kb = 0; kb < d; ++kb)
+        mm16_acc(N + (16 * ib) * LDN + 16 * (jb + kb), LDN, T + (16 * (jb + kb)) * LDT + 16 * jb, LDT, c);
+      float* Yw = Y + warp * 256;
+      frag_store(Yw, 16, c, false);
+      __syncwarp();
+      frag_zero(c);
+      mm16_acc(T + (16 * ib) * LDT + 16 * ib, LDT, Yw, 16, c);
+      frag_store(T + (16 * ib) * LDT + 16 * jb, LDT, c, false);
+    }
+    sync();
+  }
+}
+
 template <int kOut>
 __device__ __forceinline__ void store_row32(void* out, size_t idx, const float (&v)[32]) {
   if constexpr (kOut == SPOCK_F32) {

@@ -128,7 +128,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 __device__ unsigned long long g_phase_prof[148 * 4 * 32];
 #define PROF_DECL                       \
   long long _pt = clock64();            \
-  unsigned long long _acc[16] = {};
+  unsigned long long _acc[32] = {};
 #define PROF_MARK(role, k)                                  \
   do {                                                      \
     long long _now = clock64();                             \
@@ -138,7 +138,7 @@ __device__ unsigned long long g_phase_prof[148 * 4 * 32];
 #define PROF_FLUSH(role)                                                        \
   do {                                                                          \
     if ((threadIdx.x & 127) == 0 && blockIdx.x < 148)                           \
-      for (int _k = 0; _k < 16; ++_k) g_phase_prof[(blockIdx.x * 4 + (role)) * 32 + _k] += _acc[_k]; \
+      for (int _k = 0; _k < 32; ++_k) g_phase_prof[(blockIdx.x * 4 + (role)) * 32 + _k] += _acc[_k]; \
   } while (0)
 #else
 #define PROF_DECL
@@ -389,7 +389,21 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     sync();
     PROF_MARK(0, 4);
     // 4. T = (I - N)^-1
-    chunk::solve_unit_lower_fast<kPrepThreads>(NM, TM, YM, t, sync);
+#ifdef SPOCK_PHASE_PROF
+    {
+      int kk = 16;
+      auto sync_prof = [&] {
+        PROF_MARK(0, kk);
+        ++kk;
+        sync();
+        PROF_MARK(0, kk);
+        ++kk;
+      };
+      chunk::solve_unit_lower_tc(NM, TM, YM, t >> 5, sync_prof);
+    }
+#else
+    chunk::solve_unit_lower_tc(NM, TM, YM, t >> 5, sync);
+#endif
     PROF_MARK(0, 5);
     // 5. T diag(beta e^gc) -> TBE (for W^T); T diag(beta) kept in registers
     uint4 tbreg[2];
