@@ -45,7 +45,7 @@ constexpr int kPrepThreads = 256;  // warps 0-7
 constexpr int kRecBase = 256;      // warps 8-11
 constexpr int kTmaWarp = 12, kMmaWarp = 13;
 constexpr int kThreads = 448;
-constexpr uint32_t kWaitLimit = 1u << 24;
+constexpr uint32_t kWaitLimit = 1u << 25;  // >= ~4 s of polling with back-off
 
 // Shared memory (offsets from a 1024-aligned base).
 constexpr int OFF_QK = 0;                    // 2 stages x 32K: per column half [Q 8K | K 8K]
@@ -114,9 +114,12 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // Bounded wait that also gives up early once another role has aborted.
+// Polls back off with __nanosleep so waiting warps do not take issue slots
+// from the warps they wait for (they share the SM's schedulers).
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (tc::mbar_try_wait(bar, parity)) return true;
+    if (i >= 4) __nanosleep(i < 64 ? 32 : 128);
     if ((i & 255u) == 255u && *abort) return false;
   }
   return false;
@@ -399,10 +402,10 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
         PROF_MARK(0, kk);
         ++kk;
       };
-      chunk::solve_unit_lower_tc(NM, TM, YM, t >> 5, sync_prof);
+      chunk::solve_unit_lower_fast<kPrepThreads>(NM, TM, YM, t, sync_prof);
     }
 #else
-    chunk::solve_unit_lower_tc(NM, TM, YM, t >> 5, sync);
+    chunk::solve_unit_lower_fast<kPrepThreads>(NM, TM, YM, t, sync);
 #endif
     PROF_MARK(0, 5);
     // 5. T diag(beta e^gc) -> TBE (for W^T); T diag(beta) kept in registers
