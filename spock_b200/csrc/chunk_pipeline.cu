@@ -641,7 +641,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const float* __restrict__ beta, const float* __restrict__ init, void* __restrict__ out,
                       float* __restrict__ final_state, int S, int pairs, int* __restrict__ err_flag) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment by pointer arithmetic on the __shared__ array keeps the
+  // shared address space visible to the compiler (LDS/STS, not generic loads).
+  uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   Small* sh = reinterpret_cast<Small*>(sm + OFF_SMALL);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {

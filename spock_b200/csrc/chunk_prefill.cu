@@ -83,7 +83,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                       void* __restrict__ out, float* __restrict__ final_state, int S,
                       int* __restrict__ err_flag) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment by pointer arithmetic on the __shared__ array keeps the
+  // shared address space visible to the compiler (LDS/STS, not generic loads).
+  uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   float* NM = reinterpret_cast<float*>(sm + OFF_NM);
   float* TM = reinterpret_cast<float*>(sm + OFF_TM);
   float* YM = reinterpret_cast<float*>(sm + OFF_YM);
