@@ -140,8 +140,10 @@ __device__ __forceinline__ void solve_level(const float* __restrict__ N, float* 
 template <int kNT, class Sync>
 __device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ N, float* __restrict__ T,
                                                       float* __restrict__ Y, int t, Sync sync) {
-  if (t < 64) {
-    const int o = (t >> 4) * 16, j = t & 15;
+  // diagonal block w on warp w (lanes 0..15 = its columns): no bank conflict
+  // between blocks, four schedulers busy
+  if ((t >> 5) < 4 && (t & 31) < 16) {
+    const int o = (t >> 5) * 16, j = t & 15;
     float x[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) x[i] = (i == j) ? 1.f : 0.f;

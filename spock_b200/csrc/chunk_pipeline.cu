@@ -361,6 +361,15 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
       tc::tmem_ld32(tG1, a);
       const float* gl = sh->gl[s];
       const int j0 = hf * 32;
+      float glj[32];  // broadcast float4 loads of this half's exponents
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 v4 = *reinterpret_cast<const float4*>(gl + j0 + 4 * q);
+        glj[4 * q] = v4.x;
+        glj[4 * q + 1] = v4.y;
+        glj[4 * q + 2] = v4.z;
+        glj[4 * q + 3] = v4.w;
+      }
       if (l < C) {
         const float gi = gl[l];
 #pragma unroll
@@ -369,7 +378,7 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const int j = j0 + q * 8 + k;
-            x[k] = (j <= l) ? (a[q * 8 + k] * scale) * ex2(gi - gl[j]) : 0.f;
+            x[k] = (j <= l) ? (a[q * 8 + k] * scale) * ex2(gi - glj[q * 8 + k]) : 0.f;
           }
           preg[q] = pack8(x);
         }
@@ -379,7 +388,7 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
 #pragma unroll
         for (int k = 0; k < 32; ++k) {
           const int j = j0 + k;
-          NM[i * LDN + j] = (j < i) ? (nb * a[k]) * ex2(gi - gl[j]) : 0.f;
+          NM[i * LDN + j] = (j < i) ? (nb * a[k]) * ex2(gi - glj[k]) : 0.f;
         }
       }
     }
@@ -472,11 +481,18 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     {
       float w[32];
       tc::tmem_ld32(tWT, w);
-      const int h = l >> 6, cc = l & 63, ch = cc >> 3, e = cc & 7;
+      // lanes kd, kd^1 hold adjacent columns: exchange so that each stores one
+      // 32-bit pair (even lane: even rows, odd lane: odd rows)
+      const int h = l >> 6, cc = l & 63, ch = cc >> 3, e = cc & 6, odd = l & 1;
       uint8_t* base = sm + OFF_AW + h * 16384 + e * 2;
 #pragma unroll
-      for (int k = 0; k < 32; ++k)
-        *reinterpret_cast<__half*>(base + sw128(hf * 32 + k, ch)) = __float2half_rn(-w[k]);
+      for (int k = 0; k < 32; k += 2) {
+        const float mine = odd ? w[k] : w[k + 1];      // value the partner needs
+        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+        const int row = hf * 32 + k + odd;
+        const float lo = odd ? other : w[k], hi = odd ? w[k + 1] : other;
+        *reinterpret_cast<uint32_t*>(base + sw128(row, ch)) = pack_h2(-lo, -hi);
+      }
     }
     tc::tc_fence_before();
     PROF_MARK(0, 10);
