@@ -180,6 +180,45 @@ int spock_deltanet_recurrent(spock_ctx* ctx, int64_t batch, int32_t num_heads, i
                              const float* g, const float* beta, float* state, void* out,
                              void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Full-model decode (Qwen3.5-0.8B layout): the decode glue around the mixer. */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces DecodeSession (src/runtime/vk_session.hpp:22-46) for batched,
+ * independent sequences; one instance per GPU. */
+typedef struct spock_model spock_model;
+
+typedef struct {
+  int32_t num_layers; /* multiple of 4; layer i is attention iff i % 4 == 3 (24) */
+  int32_t vocab;      /* 248320 (LM head tied to the embedding) */
+  int32_t max_batch;  /* sequences per step, <= 256 */
+  int32_t max_seq;    /* KV-cache capacity, MAX_SEQ (2048) in the reference */
+  float rms_eps;      /* 1e-6 */
+  float rope_theta;   /* 1e7 (vk_session.cpp:335) */
+} spock_model_desc;
+
+int spock_model_create(spock_ctx* ctx, const spock_model_desc* desc, spock_model** out);
+int spock_model_destroy(spock_model* m);
+const char* spock_model_last_error(const spock_model* m);
+/* Uploads one tensor by the reference artifact's role name (weight_loader.hpp
+ * find_by_role: "embedding", "final_norm", "layer.N.delta_in_proj_qkv", ...);
+ * host pointer, fp16 unless the role is fp32 in the artifact. */
+int spock_model_set_weight(spock_model* m, const char* role, const void* host, size_t bytes);
+/* Zeroes DeltaNet/conv/KV state and positions for `batch` sequences
+ * (DecodeSession::reset, vk_session.cpp:980). */
+int spock_model_reset(spock_model* m, int32_t batch);
+/* One token per sequence through all layers, final norm, LM head and argmax.
+ * tokens_in/out: device int32 [batch]; hidden_out (nullable): device fp16
+ * [batch][1024], the final-normed hidden. Replaces one iteration of the decode
+ * loop (vk_session.cpp:2298-4190). */
+int spock_model_step(spock_model* m, const int32_t* tokens_in, int32_t* tokens_out, void* hidden_out,
+                     void* stream);
+/* Token-serial prefill of prompt [batch][len] (layer_major_prefill semantics,
+ * vk_session.cpp:1003-2018) then n_new greedy tokens into out_tokens
+ * [batch][n_new] (device int32). Requires a non-default stream (graph replay). */
+int spock_model_generate(spock_model* m, const int32_t* prompt, int32_t len, int32_t n_new,
+                         int32_t* out_tokens, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

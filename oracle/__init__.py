@@ -45,6 +45,13 @@ def lib():
         _LIB.oracle_conv_l2_qk.argtypes = [ctypes.c_int] * 5 + [_u16p, _u16p, _u16p, ctypes.c_int]
         _LIB.oracle_rec_norm_gate.argtypes = [ctypes.c_int] * 4 + [ctypes.c_float] * 2 + [
             _u16p, _u16p, _f32p, _u16p, _f32p, _u16p, _f32p, _u16p, ctypes.c_int]
+        vp = ctypes.c_void_p
+        _LIB.oracle_model_create.restype = vp
+        _LIB.oracle_model_create.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float] * 2
+        _LIB.oracle_model_destroy.argtypes = [vp]
+        _LIB.oracle_model_set.argtypes = [vp, ctypes.c_char_p, vp]
+        _LIB.oracle_model_reset.argtypes = [vp, ctypes.c_int]
+        _LIB.oracle_model_step.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int]
         _LIB.oracle_recurrent_raw.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float] + [
             _u16p, _u16p, _u16p, _f32p, _u16p]
     return _LIB
@@ -139,3 +146,37 @@ def recurrent_raw(q, k, v, state_with_tail, num_heads=16, k_dim=128, v_dim=128):
                                _ptr(q, _u16p), _ptr(k, _u16p), _ptr(v, _u16p), _ptr(st, _f32p),
                                _ptr(out, _u16p))
     return out, st
+
+
+class Model:
+    """CPU restatement of one full-model decode step (oracle/model.cpp).
+    `weights` maps reference role names to numpy arrays (kept alive here)."""
+
+    def __init__(self, weights, layers, vocab, max_seq, eps=1e-6, theta=1e7):
+        self.L = lib()
+        self.h = self.L.oracle_model_create(layers, vocab, max_seq, eps, theta)
+        self.keep = {}
+        for role, arr in weights.items():
+            arr = np.ascontiguousarray(arr)
+            self.keep[role] = arr
+            self.L.oracle_model_set(self.h, role.encode(), arr.ctypes.data)
+
+    def reset(self, batch):
+        self.batch = batch
+        self.L.oracle_model_reset(self.h, batch)
+
+    def step(self, tokens, threads=8):
+        tok = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros(self.batch, np.int32)
+        hid = np.zeros((self.batch, 1024), np.uint16)
+        margin = np.zeros(self.batch, np.float32)
+        rc = self.L.oracle_model_step(self.h, tok.ctypes.data, out.ctypes.data, hid.ctypes.data,
+                                      margin.ctypes.data, threads)
+        assert rc == 0
+        return out, hid, margin
+
+    def __del__(self):
+        try:
+            self.L.oracle_model_destroy(self.h)
+        except Exception:
+            pass

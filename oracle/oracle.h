@@ -20,6 +20,13 @@ int oracle_rec_norm_gate(int batch, int num_heads, int k_dim, int v_dim, float q
 int oracle_recurrent_raw(int num_heads, int k_dim, int v_dim, float q_scale, const uint16_t* q,
                          const uint16_t* k, const uint16_t* v, float* state_with_tail,
                          uint16_t* out);
+typedef struct oracle_model oracle_model;
+oracle_model* oracle_model_create(int layers, int vocab, int max_seq, float eps, float theta);
+void oracle_model_destroy(oracle_model* m);
+void oracle_model_set(oracle_model* m, const char* role, const void* ptr);
+void oracle_model_reset(oracle_model* m, int batch);
+int oracle_model_step(oracle_model* m, const int* tokens, int* out_tokens, uint16_t* hidden_out,
+                      float* margin, int threads);
 void oracle_f32_to_f16(const float* x, uint16_t* y, int64_t n);
 void oracle_f16_to_f32(const uint16_t* x, float* y, int64_t n);
 #ifdef __cplusplus

@@ -35,7 +35,9 @@ F32, F16, BF16 = 0, 1, 2
 
 EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
             "spock_kernel_launch_count", "spock_chunk_prefill", "spock_chunk_last_to_fp16",
-            "spock_deltanet_decode_step", "spock_deltanet_recurrent", "spock_chunk_prefill_noalloc"]
+            "spock_deltanet_decode_step", "spock_deltanet_recurrent", "spock_chunk_prefill_noalloc",
+            "spock_model_create", "spock_model_destroy", "spock_model_last_error", "spock_model_set_weight",
+            "spock_model_reset", "spock_model_step", "spock_model_generate"]
 
 
 class SpockError(RuntimeError):
@@ -282,3 +284,79 @@ def run_deltanet_chunk_rule(config: DeltaNetChunkConfig, inputs: DeltaNetChunkIn
     out, st = chunk_prefill(q, k, v, g, b, initial_state=init, out_dtype=torch.float32,
                             use_qk_l2norm=c.use_qk_l2norm, chunk_size=c.chunk_size)
     return DeltaNetChunkOutputs(out.reshape(-1).cpu().numpy(), st.reshape(-1).cpu().numpy())
+
+
+# ---- full-model decode session ------------------------------------------------
+
+class ModelDesc(ctypes.Structure):
+    _fields_ = [("num_layers", ctypes.c_int32), ("vocab", ctypes.c_int32), ("max_batch", ctypes.c_int32),
+                ("max_seq", ctypes.c_int32), ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float)]
+
+
+def _model_lib():
+    L = lib()
+    if not getattr(L, "_model_types", False):
+        vp = ctypes.c_void_p
+        L.spock_model_create.argtypes = [vp, ctypes.POINTER(ModelDesc), ctypes.POINTER(vp)]
+        L.spock_model_destroy.argtypes = [vp]
+        L.spock_model_last_error.argtypes = [vp]
+        L.spock_model_last_error.restype = ctypes.c_char_p
+        L.spock_model_set_weight.argtypes = [vp, ctypes.c_char_p, vp, ctypes.c_size_t]
+        L.spock_model_reset.argtypes = [vp, ctypes.c_int32]
+        L.spock_model_step.argtypes = [vp, vp, vp, vp, vp]
+        L.spock_model_generate.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, vp, vp]
+        L._model_types = True
+    return L
+
+
+class Model:
+    """Qwen3.5-0.8B-layout decode session on one GPU (spock_model): the B200
+    form of DecodeSession (src/runtime/vk_session.hpp:22-46) for a batch of
+    independent sequences. Weights are uploaded by the reference's role names."""
+
+    def __init__(self, num_layers=24, vocab=248320, max_batch=1, max_seq=2048, eps=1e-6, theta=1e7,
+                 ctx=None, device=0):
+        self.L = _model_lib()
+        self.ctx = ctx or Context.get(device)
+        self.device = device
+        d = ModelDesc(num_layers, vocab, max_batch, max_seq, eps, theta)
+        h = ctypes.c_void_p()
+        rc = self.L.spock_model_create(self.ctx.h, ctypes.byref(d), ctypes.byref(h))
+        if rc != SPOCK_OK:
+            raise SpockError(rc, "spock_model_create failed")
+        self.h = h
+        self.max_batch = max_batch
+
+    def _check(self, rc):
+        if rc != SPOCK_OK:
+            raise SpockError(rc, self.L.spock_model_last_error(self.h).decode())
+
+    def set_weights(self, weights):
+        for role, arr in weights.items():
+            arr = np.ascontiguousarray(arr)
+            self._check(self.L.spock_model_set_weight(self.h, role.encode(), arr.ctypes.data, arr.nbytes))
+
+    def reset(self, batch):
+        self.batch = batch
+        self._check(self.L.spock_model_reset(self.h, batch))
+
+    def step(self, tokens, stream=None):
+        """tokens: int32 CUDA tensor [batch] -> (next tokens [batch], final-normed hidden fp16 [batch,1024])."""
+        import torch
+        out = torch.empty_like(tokens)
+        hid = torch.empty((tokens.shape[0], 1024), dtype=torch.float16, device=tokens.device)
+        self._check(self.L.spock_model_step(self.h, _ptr(tokens), _ptr(out), _ptr(hid), _stream(stream)))
+        return out, hid
+
+    def generate(self, prompt, n_new, stream=None):
+        """prompt: int32 CUDA tensor [batch, len] -> greedy tokens [batch, n_new] (token-serial prefill)."""
+        import torch
+        out = torch.empty((prompt.shape[0], n_new), dtype=torch.int32, device=prompt.device)
+        self._check(self.L.spock_model_generate(self.h, _ptr(prompt), prompt.shape[1], n_new, _ptr(out),
+                                                _stream(stream)))
+        return out
+
+    def close(self):
+        if self.h:
+            self.L.spock_model_destroy(self.h)
+            self.h = None

@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                      const uint16_t* __restrict__ k_raw, const uint16_t* __restrict__ v_raw,
                      const float* __restrict__ g_in, const float* __restrict__ beta_in,
                      float* __restrict__ state, uint16_t* __restrict__ out,
-                     uint16_t* __restrict__ core_raw) {
+                     uint16_t* __restrict__ core_raw, int qkv_ld, int ab_ld, int z_ld, int out_ld) {
   const int h = blockIdx.x;
   const int s = blockIdx.y;
   const int t = threadIdx.x;
@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // 2. Prologue: q, k, v for this head, g and beta.
   if constexpr (kFused) {
     const int conv_dim = H * 3 * kDim;
-    uint16_t* x = qkv + (size_t)s * conv_dim;
+    uint16_t* x = qkv + (size_t)s * qkv_ld;
     uint16_t* cs = conv_state + (size_t)s * conv_dim * 4;
     for (int c = t; c < 3 * kDim; c += kThreads) {
       const int blk = c / kDim, off = c % kDim;
@@ -102,8 +102,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     if (t == 0) {
-      const float a_val = h2f(a_in[(size_t)s * H + h]);
-      const float b_val = h2f(b_in[(size_t)s * H + h]);
+      const float a_val = h2f(a_in[(size_t)s * ab_ld + h]);
+      const float b_val = h2f(b_in[(size_t)s * ab_ld + h]);
       const float a_log = a_log_bias[h * 2 + 0], dt_bias = a_log_bias[h * 2 + 1];
       const float sp = logf(add_rn(1.0f, expf(add_rn(a_val, dt_bias))));
       s_g = mul_rn(-expf(a_log), sp);
@@ -200,18 +200,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (t < kDim) {
     const float nf = __fdiv_rn(1.0f, __fsqrt_rn(add_rn(__fdiv_rn(ss, (float)kDim), eps)));
     const float normed = mul_rn(ov, nf);
-    const float zz = h2f(z_in[((size_t)s * H + h) * kDim + t]);
+    const float zz = h2f(z_in[(size_t)s * z_ld + h * kDim + t]);
     const float silu = __fdiv_rn(zz, add_rn(1.0f, expf(-zz)));
     const float weighted = h2f(f2h(mul_rn(norm_w[t], normed)));
-    out[((size_t)s * H + h) * kDim + t] = f2h(mul_rn(weighted, silu));
+    out[(size_t)s * out_ld + h * kDim + t] = f2h(mul_rn(weighted, silu));
   }
 }
 
 }  // namespace
 
-Status launch_decode_step(const spock_dn_layer& L, int64_t batch, void* qkv, void* conv_state,
-                          float* state, const void* a, const void* b, const void* z, void* out,
-                          void* core_raw, cudaStream_t stream) {
+Status launch_decode_step_strided(const spock_dn_layer& L, int64_t batch, void* qkv, int qkv_ld,
+                                  void* conv_state, float* state, const void* a, const void* b, int ab_ld,
+                                  const void* z, int z_ld, void* out, int out_ld, void* core_raw,
+                                  cudaStream_t stream) {
   if (L.key_dim != kDim || L.value_dim != kDim || L.conv_kernel != 4)
     return Status::err(SPOCK_ERR_UNSUPPORTED,
                        "decode step: CUDA path implements key_dim=value_dim=128, conv_kernel=4");
@@ -225,9 +226,18 @@ Status launch_decode_step(const spock_dn_layer& L, int64_t batch, void* qkv, voi
       L.num_heads, 1.0f / sqrtf((float)kDim), L.eps, (uint16_t*)qkv, (uint16_t*)conv_state,
       (const uint16_t*)L.conv_weight, L.a_log_bias, L.norm_weight, (const uint16_t*)a,
       (const uint16_t*)b, (const uint16_t*)z, nullptr, nullptr, nullptr, nullptr, nullptr, state,
-      (uint16_t*)out, (uint16_t*)core_raw);
+      (uint16_t*)out, (uint16_t*)core_raw, qkv_ld, ab_ld, z_ld, out_ld);
   SPOCK_LAUNCH_CHECK("dn_decode_kernel<fused>");
   return Status::ok();
+}
+
+Status launch_decode_step(const spock_dn_layer& L, int64_t batch, void* qkv, void* conv_state,
+                          float* state, const void* a, const void* b, const void* z, void* out,
+                          void* core_raw, cudaStream_t stream) {
+  const int conv_dim = L.num_heads * (L.key_dim * 2 + L.value_dim);
+  return launch_decode_step_strided(L, batch, qkv, conv_dim, conv_state, state, a, b, L.num_heads, z,
+                                    L.num_heads * L.value_dim, out, L.num_heads * L.value_dim, core_raw,
+                                    stream);
 }
 
 Status launch_recurrent(int64_t batch, int H, int kd, int vd, const void* q, const void* k,
@@ -242,7 +252,7 @@ Status launch_recurrent(int64_t batch, int H, int kd, int vd, const void* q, con
   dn_decode_kernel<false><<<grid, kThreads, 0, stream>>>(
       H, 1.0f / sqrtf((float)kDim), 0.f, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
       nullptr, nullptr, (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, g, beta, state,
-      nullptr, (uint16_t*)out);
+      nullptr, (uint16_t*)out, 0, 0, 0, 0);
   SPOCK_LAUNCH_CHECK("dn_decode_kernel<raw>");
   return Status::ok();
 }

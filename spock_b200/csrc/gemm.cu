@@ -1,0 +1,402 @@
+// Weight-streaming projection for the decode glue: y[b][n] = sum_k x[b][k] W[n][k]
+// (fp16 in, fp32 accumulate), the batched form of spock's matvec / matvec_tiled /
+// lm_head_tiled shaders (shaders/matvec.comp:28-41, matvec_tiled.comp:41-83,
+// lm_head_tiled.comp:40-86). Their outputs are fp16-rounded; so are these.
+//
+// Swap-AB tcgen05 GEMM: a 128-row slab of W is the M=128 operand (K-major, TMA,
+// 128B swizzle) and the batch of activation rows is the N operand (16..256), so
+// one pass over the weights serves the whole batch; decode is HBM-bound on W.
+// Accumulators live in TMEM (lane = weight row, column = batch row).
+//
+// Grid: (row tiles, K splits). With K splits, every CTA writes its fp32 partial
+// tile to a workspace; the last CTA of a tile (atomic ticket) sums the
+// partials in split order (deterministic) and runs the epilogue.
+//
+// Epilogues (fused):
+//   F16      y = fp16(acc)
+//   RESIDUAL y = fp16(fp32(fp16(acc)) + res)          (matvec + residual_add.comp)
+//   SWIGLU   W rows interleaved in 16-row groups [gate g..g+15 | up g..g+15]:
+//            m = fp16(silu(fp16(gate)) * fp16(up))     (2 matvecs + silu_gate.comp)
+//   ARGMAX   logits = fp16(acc); per batch row the tile's (max, lowest index)
+//            goes to a partials array, reduced by argmax_finish (argmax.comp)
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace spock {
+
+enum GemmEpi { EPI_F16 = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+struct GemmArgs {
+  int n_out;        // weight rows
+  int k;            // inner dim, multiple of 64
+  int batch;        // real batch rows
+  int bpad;         // padded batch (MMA N), multiple of 16, <= 256
+  int kb_per_split; // 64-wide k blocks per split
+  int nsplit;
+  __half* y;        // [batch][ldy]
+  int ldy;
+  const __half* res;    // RESIDUAL: [batch][ldy]
+  float* ws;            // split partials [nsplit][n_tiles*128][bpad]
+  int* tickets;         // [n_tiles], zero before launch, left zero after
+  float* amax_val;      // ARGMAX partials [n_tiles][batch]
+  int* amax_idx;
+  int* err;
+};
+
+namespace {
+
+constexpr int kStages = 4;
+constexpr uint32_t kWaitLimit = 1u << 25;
+
+__device__ __forceinline__ bool wait_spin(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (tc::mbar_try_wait(bar, parity)) return true;
+    if (i >= 8) __nanosleep(64);
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          tc::smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(128, 1)
+    gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                       GemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int a_bytes = 128 * 128, b_bytes = a.bpad * 128, stage_bytes = a_bytes + b_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * stage_bytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* done = empty + kStages;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(done + 1);
+  int* s_last = reinterpret_cast<int*>(s_tmem + 1);
+  float* s_red = reinterpret_cast<float*>(s_last + 1);  // ARGMAX: [4 warps][256] vals, then idx
+  int* s_redi = reinterpret_cast<int*>(s_red + 4 * 256);
+
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int kb0 = split * a.kb_per_split;
+  const int nkb = min(a.kb_per_split, a.k / 64 - kb0);
+  uint32_t ncols = 32;
+  while ((int)ncols < a.bpad) ncols <<= 1;
+
+  if (t == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(done, 1);
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmw);
+    tc::prefetch_tmap(&tmx);
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(s_tmem, ncols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tb = *s_tmem;
+  bool ok = true;
+
+  if (warp == 0 && lane == 0) {  // TMA producer
+    for (int i = 0; i < nkb && ok; ++i) {
+      const int s = i % kStages;
+      if (i >= kStages) ok = wait_spin(&empty[s], ((i / kStages) - 1) & 1);
+      if (!ok) break;
+      uint8_t* st = sm + s * stage_bytes;
+      tc::mbar_arrive_expect_tx(&full[s], stage_bytes);
+      tma_load_2d(st, &tmw, &full[s], (kb0 + i) * 64, tile * 128);
+      tma_load_2d(st + a_bytes, &tmx, &full[s], (kb0 + i) * 64, 0);
+    }
+  } else if (warp == 1 && lane == 0) {  // MMA issuer
+    const uint32_t idesc = tc::idesc_f16(128, a.bpad, false, false);
+    const uint32_t sbase = tc::smem_u32(sm);
+    for (int i = 0; i < nkb && ok; ++i) {
+      const int s = i % kStages;
+      ok = wait_spin(&full[s], (i / kStages) & 1);
+      if (!ok) break;
+      tc::tc_fence_after();
+      const uint32_t st = sbase + s * stage_bytes;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        tc::mma_f16(tb, tc::sdesc(st + kk * 32, 16, 1024), tc::sdesc(st + a_bytes + kk * 32, 16, 1024), idesc,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+      tc::mma_commit(&empty[s]);
+    }
+    tc::mma_commit(done);
+  }
+  __syncwarp();
+  // epilogue: all 128 threads; thread t <-> weight row tile*128 + t
+  if (!wait_spin(done, 0)) ok = false;
+  if (__syncthreads_or(!ok)) {
+    if (t == 0) atomicExch(a.err, 3);
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tb, ncols);
+    return;
+  }
+  tc::tc_fence_after();
+  const int row = tile * 128 + t;
+  const uint32_t taddr = tb + ((uint32_t)(warp * 32) << 16);
+  const size_t tile_stride = (size_t)gridDim.x * 128 * a.bpad;
+
+  bool finisher = true;
+  if (a.nsplit > 1) {
+    // partial tile -> workspace [split][row][col]
+    float* wsp = a.ws + split * tile_stride + (size_t)row * a.bpad;
+    for (int c0 = 0; c0 < a.bpad; c0 += 32) {
+      float v[32];
+      tc::tmem_ld32(taddr + c0, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (c0 + 4 * q < a.bpad)
+          reinterpret_cast<float4*>(wsp + c0)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (t == 0) {
+      const int ticket = atomicAdd(&a.tickets[tile], 1);
+      *s_last = (ticket == a.nsplit - 1);
+      if (*s_last) a.tickets[tile] = 0;  // ready for the next launch
+    }
+    __syncthreads();
+    finisher = *s_last != 0;
+    __threadfence();
+  }
+
+  if (finisher) {
+    for (int c0 = 0; c0 < a.bpad; c0 += 32) {
+      float v[32];
+      if (a.nsplit > 1) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = 0.f;
+        for (int s = 0; s < a.nsplit; ++s) {  // fixed order: deterministic
+          const float* p = a.ws + s * tile_stride + (size_t)row * a.bpad + c0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (c0 + 4 * q < a.bpad) {
+              const float4 x = __ldcg(reinterpret_cast<const float4*>(p) + q);
+              v[4 * q] += x.x;
+              v[4 * q + 1] += x.y;
+              v[4 * q + 2] += x.z;
+              v[4 * q + 3] += x.w;
+            }
+          }
+        }
+      } else {
+        tc::tmem_ld32(taddr + c0, v);
+      }
+      if constexpr (kEpi == EPI_F16 || kEpi == EPI_RESIDUAL) {
+        if (row < a.n_out) {
+#pragma unroll 4
+          for (int k = 0; k < 32; ++k) {
+            const int b = c0 + k;
+            if (b < a.batch) {
+              float o = __half2float(__float2half_rn(v[k]));
+              if constexpr (kEpi == EPI_RESIDUAL) o = o + __half2float(a.res[(size_t)b * a.ldy + row]);
+              a.y[(size_t)b * a.ldy + row] = __float2half_rn(o);
+            }
+          }
+        }
+      } else if constexpr (kEpi == EPI_SWIGLU) {
+        const int grp = row >> 5, j = row & 31, feat = grp * 16 + (j & 15);
+#pragma unroll 4
+        for (int k = 0; k < 32; ++k) {
+          const float u = __shfl_xor_sync(0xffffffffu, v[k], 16);
+          const int b = c0 + k;
+          if (j < 16 && b < a.batch && row < a.n_out) {
+            const float g16 = __half2float(__float2half_rn(v[k]));
+            const float u16 = __half2float(__float2half_rn(u));
+            const float silu = __fdiv_rn(g16, __fadd_rn(1.0f, expf(-g16)));
+            a.y[(size_t)b * a.ldy + feat] = __float2half_rn(__fmul_rn(silu, u16));
+          }
+        }
+      } else {  // EPI_ARGMAX: per batch column, max fp16 logit over the tile's rows, lowest index on ties
+        for (int k = 0; k < 32; ++k) {
+          const int b = c0 + k;
+          float val = (row < a.n_out) ? __half2float(__float2half_rn(v[k])) : -INFINITY;
+          int idx = (row < a.n_out) ? row : 0x7fffffff;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, val, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (ov > val || (ov == val && oi < idx)) {
+              val = ov;
+              idx = oi;
+            }
+          }
+          if (lane == 0) {
+            s_red[warp * 256 + b] = val;
+            s_redi[warp * 256 + b] = idx;
+          }
+        }
+      }
+    }
+    if constexpr (kEpi == EPI_ARGMAX) {
+      __syncthreads();
+      for (int b = t; b < a.batch; b += 128) {
+        float val = s_red[b];
+        int idx = s_redi[b];
+        for (int w = 1; w < 4; ++w) {
+          const float ov = s_red[w * 256 + b];
+          const int oi = s_redi[w * 256 + b];
+          if (ov > val || (ov == val && oi < idx)) {
+            val = ov;
+            idx = oi;
+          }
+        }
+        a.amax_val[(size_t)tile * a.batch + b] = val;
+        a.amax_idx[(size_t)tile * a.batch + b] = idx;
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tb, ncols);
+}
+
+// token[b] = index of the largest fp16 logit, lowest index among equals.
+__global__ void argmax_finish_kernel(const float* __restrict__ val, const int* __restrict__ idx, int ntiles,
+                                     int batch, int* __restrict__ token) {
+  const int b = blockIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
+    const float v = val[(size_t)i * batch + b];
+    const int x = idx[(size_t)i * batch + b];
+    if (v > bv || (v == bv && x < bi)) {
+      bv = v;
+      bi = x;
+    }
+  }
+  __shared__ float sv[256];
+  __shared__ int si[256];
+  sv[threadIdx.x] = bv;
+  si[threadIdx.x] = bi;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if ((int)threadIdx.x < s) {
+      const float ov = sv[threadIdx.x + s];
+      const int oi = si[threadIdx.x + s];
+      if (ov > sv[threadIdx.x] || (ov == sv[threadIdx.x] && oi < si[threadIdx.x])) {
+        sv[threadIdx.x] = ov;
+        si[threadIdx.x] = oi;
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) token[b] = si[0];
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn2() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+Status map2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn2();
+  if (!fn) return Status::err(SPOCK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return Status::err(SPOCK_ERR_CUDA, "cuTensorMapEncodeTiled failed (gemm)");
+  return Status::ok();
+}
+
+}  // namespace
+
+Status gemm_prepare();
+
+// x: [bpad][k] fp16 (rows >= batch may hold anything), W: [n_out][k] fp16.
+// Workspace needs nsplit * ceil(n_out/128) * 128 * bpad floats when nsplit > 1,
+// tickets ceil(n_out/128) ints (zero), ARGMAX partials ceil(n_out/128) * batch.
+Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, cudaStream_t st) {
+  if (a.k % 64 || a.bpad % 16 || a.bpad < 16 || a.bpad > 256 || a.batch > a.bpad || a.batch < 1)
+    return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: k % 64, 16 <= bpad <= 256 (multiple of 16), batch <= bpad");
+  if (((uintptr_t)x & 15) || ((uintptr_t)w & 15))
+    return Status::err(SPOCK_ERR_INVALID, "gemm: operands must be 16-byte aligned");
+  CUtensorMap mw, mx;
+  Status s = map2d(&mw, w, a.n_out, a.k, 128);
+  if (s.code) return s;
+  s = map2d(&mx, x, a.bpad, a.k, a.bpad);
+  if (s.code) return s;
+  const int ntiles = (a.n_out + 127) / 128, kbs = a.k / 64;
+  if (a.nsplit < 1) {  // enough CTAs to stream the weights from every SM
+    int want = (sms + ntiles - 1) / ntiles;
+    want = want < 1 ? 1 : want;
+    a.nsplit = want > kbs ? kbs : want;
+  }
+  a.kb_per_split = (kbs + a.nsplit - 1) / a.nsplit;
+  a.nsplit = (kbs + a.kb_per_split - 1) / a.kb_per_split;
+  if (a.nsplit > 1 && (!a.ws || !a.tickets)) return Status::err(SPOCK_ERR_INVALID, "gemm: split-K needs a workspace");
+  const int smem = kStages * (128 * 128 + a.bpad * 128) + 64 + 8 * 256 * 4 + 1024;
+  dim3 grid(ntiles, a.nsplit);
+  {
+    static std::once_flag once;
+    static Status prep;
+    std::call_once(once, [] { prep = gemm_prepare(); });
+    if (prep.code) return prep;
+  }
+#define SPOCK_GEMM_CASE(E)                                                                          \
+  case E: {                                                                                         \
+    gemm_swapab_kernel<E><<<grid, 128, smem, st>>>(mw, mx, a);                                      \
+    break;                                                                                          \
+  }
+  switch (epi) {
+    SPOCK_GEMM_CASE(EPI_F16)
+    SPOCK_GEMM_CASE(EPI_RESIDUAL)
+    SPOCK_GEMM_CASE(EPI_SWIGLU)
+    SPOCK_GEMM_CASE(EPI_ARGMAX)
+    default:
+      return Status::err(SPOCK_ERR_INVALID, "gemm: unknown epilogue");
+  }
+#undef SPOCK_GEMM_CASE
+  SPOCK_LAUNCH_CHECK("gemm_swapab_kernel");
+  return Status::ok();
+}
+
+// Sets every GEMM variant's shared-memory limit once (before any graph capture).
+Status gemm_prepare() {
+  const int smem = kStages * (128 * 128 + 256 * 128) + 64 + 8 * 256 * 4 + 1024;
+  cudaError_t e = cudaSuccess;
+  e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return cuda_status(e, "gemm_prepare");
+}
+
+Status launch_argmax_finish(const float* val, const int* idx, int ntiles, int batch, int* token, cudaStream_t st) {
+  argmax_finish_kernel<<<batch, 256, 0, st>>>(val, idx, ntiles, batch, token);
+  SPOCK_LAUNCH_CHECK("argmax_finish_kernel");
+  return Status::ok();
+}
+
+}  // namespace spock

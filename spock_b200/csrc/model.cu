@@ -1,0 +1,474 @@
+// Full-model decode session for the Qwen3.5-0.8B layout (the B200 form of
+// spock's DecodeSession, src/runtime/vk_session.{hpp,cpp}), batched over
+// independent sequences. Per token and layer it follows the reference's
+// default (all fast gates on) order (vk_session.cpp:2658-3370):
+//   x = rmsnorm(h, input_norm)
+//   DeltaNet: [qkv|z|a|b] = W_in x ; conv+L2+g/beta+recurrence+gated norm ;
+//             h += W_out (mixer out)
+//   attention: [q,gate|k|v] = W_qkv x ; q/k norm, RoPE, KV store ; GQA decode,
+//             sigmoid gate ; h += W_o (gated)
+//   x = rmsnorm(h, post_norm) ; m = silu(W_gate x) * (W_up x) ; h += W_down m
+// then final rmsnorm, tied LM head and argmax (lowest index on ties). Layer i
+// is attention iff i % 4 == 3 (src/model/qwen35_config.cpp:5-13).
+//
+// All weights stay resident (1.5 GB fp16); state per sequence: DeltaNet
+// state 18 x 16 x 128 x 128 fp32, conv cache 18 x 6144 x 4 fp16, KV cache
+// 6 x max_seq x 2 x 2 x 256 fp16. A step is captured once into a CUDA graph and
+// replayed per token.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace {
+constexpr int HID = 1024, INTER = 3584, DNH = 16, DND = 128, CONV = 6144, DN_IN = 6144 + 2048 + 32;
+constexpr int QH = 8, KVH = 2, HD = 256, ATT_IN = QH * HD * 2 + 2 * KVH * HD;  // 5120
+}  // namespace
+
+namespace spock {
+struct GemmArgs {
+  int n_out, k, batch, bpad, kb_per_split, nsplit;
+  __half* y;
+  int ldy;
+  const __half* res;
+  float* ws;
+  int* tickets;
+  float* amax_val;
+  int* amax_idx;
+  int* err;
+};
+Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, cudaStream_t st);
+Status launch_argmax_finish(const float* val, const int* idx, int ntiles, int batch, int* token, cudaStream_t st);
+Status launch_embed(const int* tokens, const void* emb, void* h, int batch, cudaStream_t st);
+Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batch, cudaStream_t st);
+Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* kn_w, const float* rope,
+                        const int* pos, void* q_out, void* gate_out, void* kv, int64_t kv_seq_stride,
+                        int64_t kv_layer_off, float eps, int batch, cudaStream_t st);
+Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
+                          int64_t kv_layer_off, const int* pos, float scale, void* out, int batch,
+                          cudaStream_t st);
+Status launch_decode_step_strided(const spock_dn_layer& L, int64_t batch, void* qkv, int qkv_ld,
+                                  void* conv_state, float* state, const void* a, const void* b, int ab_ld,
+                                  const void* z, int z_ld, void* out, int out_ld, void* core_raw,
+                                  cudaStream_t stream);
+enum { EPI_F16 = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+namespace {
+
+__global__ void advance_kernel(int* pos, const int* tok_out, int* tok_in, int batch) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) {
+    pos[b] += 1;
+    tok_in[b] = tok_out[b];
+  }
+}
+// dst[b * dst_stride + dst_off] = src[b * src_stride + src_off]
+__global__ void copy_col_kernel(int* dst, int dst_stride, int dst_off, const int* src, int src_stride, int src_off,
+                                int batch) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) dst[(size_t)b * dst_stride + dst_off] = src[(size_t)b * src_stride + src_off];
+}
+}  // namespace
+
+Status gemm_prepare();
+
+struct ModelLayer {
+  bool attn = false;
+  void *input_norm = nullptr, *post_norm = nullptr;
+  void *w_in = nullptr, *w_out = nullptr;      // DN: [8224][1024], [1024][2048]; attn: [5120][1024], [1024][2048]
+  void *conv_w = nullptr;                      // DN fp16 [6144][4]
+  float *a_log_bias = nullptr, *dn_norm = nullptr;
+  void *q_norm = nullptr, *k_norm = nullptr;
+  void *w_gu = nullptr, *w_down = nullptr;     // [7168][1024] (gate/up interleaved by 16 rows), [1024][3584]
+  int dn_idx = -1, attn_idx = -1;
+};
+
+}  // namespace spock
+
+struct spock_model {
+  int device = 0, sms = 148;
+  spock_model_desc d{};
+  std::string err;
+  std::vector<spock::ModelLayer> L;
+  std::vector<void*> allocs;
+  void *emb = nullptr, *final_norm = nullptr;
+  float* rope = nullptr;  // [max_seq][64]
+  // activations (bpad rows)
+  int bpad = 16, batch = 0;
+  void *h = nullptr, *x = nullptr, *proj = nullptr, *mix = nullptr, *mlp = nullptr, *q = nullptr, *gate = nullptr;
+  float *ws = nullptr;
+  int* tickets = nullptr;
+  float* amax_val = nullptr;
+  int* amax_idx = nullptr;
+  int *tok_in = nullptr, *tok_out = nullptr, *pos = nullptr, *err_flag = nullptr;
+  // state
+  float* dn_state = nullptr;
+  void* conv_state = nullptr;
+  void* kv = nullptr;
+  int64_t kv_seq_stride = 0;
+  cudaGraphExec_t graph = nullptr;
+  int graph_batch = -1;
+  cudaStream_t graph_stream = nullptr;
+};
+
+namespace {
+using spock::Status;
+
+int mfail(spock_model* m, int code, const std::string& msg) {
+  m->err = msg;
+  return code;
+}
+
+template <class T>
+cudaError_t dalloc(spock_model* m, T** p, size_t bytes) {
+  void* v = nullptr;
+  cudaError_t e = cudaMalloc(&v, bytes);
+  if (e == cudaSuccess) {
+    m->allocs.push_back(v);
+    cudaMemset(v, 0, bytes);
+  }
+  *p = static_cast<T*>(v);
+  return e;
+}
+
+int n_dn(const spock_model* m) { return (int)(m->d.num_layers - m->d.num_layers / 4); }
+int n_attn(const spock_model* m) { return (int)(m->d.num_layers / 4); }
+
+Status gemm(spock_model* m, int epi, const void* x, const void* w, int n_out, int k, void* y, int ldy,
+            const void* res, cudaStream_t st) {
+  spock::GemmArgs a{};
+  a.n_out = n_out;
+  a.k = k;
+  a.batch = m->batch;
+  a.bpad = m->bpad;
+  a.nsplit = 0;
+  a.y = (__half*)y;
+  a.ldy = ldy;
+  a.res = (const __half*)res;
+  a.ws = m->ws;
+  a.tickets = m->tickets;
+  a.amax_val = m->amax_val;
+  a.amax_idx = m->amax_idx;
+  a.err = m->err_flag;
+  return spock::launch_gemm(epi, x, w, a, m->sms, st);
+}
+
+#define TRY(expr)                  \
+  do {                             \
+    Status _s = (expr);            \
+    if (_s.code) return _s;        \
+  } while (0)
+
+// One decode token for every sequence: tok_in -> tok_out, h holds the final normed hidden in x.
+Status record_step(spock_model* m, cudaStream_t st) {
+  const int B = m->batch;
+  TRY(spock::launch_embed(m->tok_in, m->emb, m->h, B, st));
+  const float eps = m->d.rms_eps;
+  for (const auto& l : m->L) {
+    TRY(spock::launch_rmsnorm(m->h, l.input_norm, m->x, eps, B, st));
+    if (!l.attn) {
+      TRY(gemm(m, spock::EPI_F16, m->x, l.w_in, DN_IN, HID, m->proj, DN_IN, nullptr, st));
+      spock_dn_layer dl{DNH, DND, DND, 4, l.conv_w, l.a_log_bias, l.dn_norm, eps, 0};
+      __half* p = (__half*)m->proj;  // [batch][qkv 6144 | z 2048 | a 16 | b 16]
+      // state and conv caches are [dn layer][sequence][...]
+      TRY(spock::launch_decode_step_strided(
+          dl, B, p, DN_IN, (uint16_t*)m->conv_state + (size_t)l.dn_idx * B * CONV * 4,
+          m->dn_state + (size_t)l.dn_idx * B * DNH * DND * DND, p + CONV + 2048, p + CONV + 2048 + DNH, DN_IN,
+          p + CONV, DN_IN, m->mix, DNH * DND, nullptr, st));
+      TRY(gemm(m, spock::EPI_RESIDUAL, m->mix, l.w_out, HID, DNH * DND, m->h, HID, m->h, st));
+    } else {
+      TRY(gemm(m, spock::EPI_F16, m->x, l.w_in, ATT_IN, HID, m->proj, ATT_IN, nullptr, st));
+      const int64_t layer_off = (int64_t)l.attn_idx * m->d.max_seq * 2 * KVH * HD;
+      TRY(spock::launch_attn_prep(m->proj, ATT_IN, l.q_norm, l.k_norm, m->rope, m->pos, m->q, m->gate, m->kv,
+                                  m->kv_seq_stride, layer_off, eps, B, st));
+      TRY(spock::launch_attn_decode(m->q, m->gate, m->kv, m->kv_seq_stride, layer_off, m->pos, 1.0f / 16.0f,
+                                    m->mix, B, st));
+      TRY(gemm(m, spock::EPI_RESIDUAL, m->mix, l.w_out, HID, QH * HD, m->h, HID, m->h, st));
+    }
+    TRY(spock::launch_rmsnorm(m->h, l.post_norm, m->x, eps, B, st));
+    TRY(gemm(m, spock::EPI_SWIGLU, m->x, l.w_gu, 2 * INTER, HID, m->mlp, INTER, nullptr, st));
+    TRY(gemm(m, spock::EPI_RESIDUAL, m->mlp, l.w_down, HID, INTER, m->h, HID, m->h, st));
+  }
+  TRY(spock::launch_rmsnorm(m->h, m->final_norm, m->x, eps, B, st));
+  TRY(gemm(m, spock::EPI_ARGMAX, m->x, m->emb, m->d.vocab, HID, nullptr, 0, nullptr, st));
+  TRY(spock::launch_argmax_finish(m->amax_val, m->amax_idx, (m->d.vocab + 127) / 128, B, m->tok_out, st));
+  spock::advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(m->pos, m->tok_out, m->tok_in, B);
+  SPOCK_LAUNCH_CHECK("advance_kernel");
+  return Status::ok();
+}
+
+Status ensure_graph(spock_model* m, cudaStream_t st) {
+  if (m->graph && m->graph_batch == m->batch && m->graph_stream == st) return Status::ok();
+  if (m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  cudaGraph_t g;
+  Status prep = spock::gemm_prepare();
+  if (prep.code) return prep;
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
+  if (e != cudaSuccess) return spock::cuda_status(e, "model: begin capture");
+  Status s = record_step(m, st);
+  e = cudaStreamEndCapture(st, &g);
+  if (s.code) return s;
+  if (e != cudaSuccess) return spock::cuda_status(e, "model: end capture");
+  e = cudaGraphInstantiate(&m->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return spock::cuda_status(e, "model: graph instantiate");
+  m->graph_batch = m->batch;
+  m->graph_stream = st;
+  return Status::ok();
+}
+
+struct Guard {
+  int prev = -1;
+  explicit Guard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~Guard() {
+    int cur;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+}  // namespace
+
+extern "C" {
+
+__attribute__((visibility("default"))) int spock_model_create(spock_ctx* ctx, const spock_model_desc* d,
+                                                              spock_model** out) {
+  (void)ctx;
+  if (!out || !d) return SPOCK_ERR_INVALID;
+  *out = nullptr;
+  if (d->num_layers <= 0 || d->num_layers % 4 || d->vocab <= 0 || d->max_batch <= 0 || d->max_batch > 256 ||
+      d->max_seq <= 0)
+    return SPOCK_ERR_INVALID;
+  spock_model* m = new spock_model();
+  m->d = *d;
+  cudaGetDevice(&m->device);
+  cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device);
+  m->bpad = ((d->max_batch + 15) / 16) * 16;
+  const int B = m->bpad;
+  bool ok = true;
+  auto A = [&](auto** p, size_t bytes) { ok = ok && dalloc(m, p, bytes) == cudaSuccess; };
+  A(&m->emb, (size_t)d->vocab * HID * 2);
+  A(&m->final_norm, HID * 2);
+  A(&m->rope, (size_t)d->max_seq * 64 * 4);
+  A(&m->h, (size_t)B * HID * 2);
+  A(&m->x, (size_t)B * HID * 2);
+  A(&m->proj, (size_t)B * DN_IN * 2);
+  A(&m->mix, (size_t)B * 2048 * 2);
+  A(&m->mlp, (size_t)B * INTER * 2);
+  A(&m->q, (size_t)B * QH * HD * 2);
+  A(&m->gate, (size_t)B * QH * HD * 2);
+  // split-K workspace: up to 148 CTAs per GEMM of 128 x bpad fp32 partials, twice for slack
+  A(&m->ws, (size_t)2 * m->sms * 128 * B * 4 + (size_t)((DN_IN + 127) / 128) * 128 * B * 4 * 2);
+  A(&m->tickets, (size_t)((d->vocab + 127) / 128 + 64) * 4);
+  A(&m->amax_val, (size_t)((d->vocab + 127) / 128) * B * 4);
+  A(&m->amax_idx, (size_t)((d->vocab + 127) / 128) * B * 4);
+  A(&m->tok_in, (size_t)B * 4);
+  A(&m->tok_out, (size_t)B * 4);
+  A(&m->pos, (size_t)B * 4);
+  A(&m->err_flag, 4);
+  const int ndn = n_dn(m), nat = n_attn(m);
+  A(&m->dn_state, (size_t)ndn * B * DNH * DND * DND * 4);
+  A(&m->conv_state, (size_t)ndn * B * CONV * 4 * 2);
+  m->kv_seq_stride = (int64_t)nat * d->max_seq * 2 * KVH * HD;
+  A(&m->kv, (size_t)B * m->kv_seq_stride * 2);
+  m->L.resize(d->num_layers);
+  int di = 0, ai = 0;
+  for (int i = 0; i < d->num_layers; ++i) {
+    auto& l = m->L[i];
+    l.attn = (i % 4) == 3;
+    A(&l.input_norm, HID * 2);
+    A(&l.post_norm, HID * 2);
+    A(&l.w_gu, (size_t)2 * INTER * HID * 2);
+    A(&l.w_down, (size_t)HID * INTER * 2);
+    if (l.attn) {
+      l.attn_idx = ai++;
+      A(&l.w_in, (size_t)ATT_IN * HID * 2);
+      A(&l.w_out, (size_t)HID * QH * HD * 2);
+      A(&l.q_norm, HD * 2);
+      A(&l.k_norm, HD * 2);
+    } else {
+      l.dn_idx = di++;
+      A(&l.w_in, (size_t)DN_IN * HID * 2);
+      A(&l.w_out, (size_t)HID * 2048 * 2);
+      A(&l.conv_w, (size_t)CONV * 4 * 2);
+      A(&l.a_log_bias, DNH * 2 * 4);
+      A(&l.dn_norm, DND * 4);
+    }
+  }
+  if (!ok) {
+    spock_model_destroy(m);
+    return SPOCK_ERR_ALLOC;
+  }
+  // RoPE table exactly as DecodeSession builds it (vk_session.cpp:333-346): host fp32
+  std::vector<float> rope((size_t)d->max_seq * 64);
+  const float theta = d->rope_theta;
+  for (int p = 0; p < d->max_seq; ++p)
+    for (int i = 0; i < 32; ++i) {
+      const float inv_freq = 1.0f / std::pow(theta, 2.0f * (float)i / 64.0f);
+      const float ang = (float)p * inv_freq;
+      rope[(size_t)p * 64 + 2 * i] = std::cos(ang);
+      rope[(size_t)p * 64 + 2 * i + 1] = std::sin(ang);
+    }
+  cudaMemcpy(m->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice);
+  *out = m;
+  return SPOCK_OK;
+}
+
+__attribute__((visibility("default"))) int spock_model_destroy(spock_model* m) {
+  if (!m) return SPOCK_OK;
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+  return SPOCK_OK;
+}
+
+__attribute__((visibility("default"))) const char* spock_model_last_error(const spock_model* m) {
+  return m ? m->err.c_str() : "";
+}
+
+// Roles as in spock's artifact (weight_loader / vk_session.cpp): "embedding",
+// "final_norm", "layer.N.<input_norm|post_norm|mlp_gate|mlp_up|mlp_down|
+// delta_in_proj_qkv|delta_in_proj_z|delta_in_proj_a|delta_in_proj_b|delta_conv|
+// delta_norm|delta_a_log|delta_dt_bias|delta_out_proj|attn_q|attn_k|attn_v|
+// attn_q_norm|attn_k_norm|attn_o>". fp16 unless noted: delta_norm and
+// delta_a_log are fp32, delta_dt_bias fp16 (kept as fp32 on device).
+__attribute__((visibility("default"))) int spock_model_set_weight(spock_model* m, const char* role,
+                                                                  const void* host, size_t bytes) {
+  if (!m || !role || !host) return SPOCK_ERR_INVALID;
+  Guard g(m->device);
+  const std::string r(role);
+  auto put = [&](void* dst, size_t expect, size_t off = 0) -> int {
+    if (bytes != expect) return mfail(m, SPOCK_ERR_INVALID, r + ": expected " + std::to_string(expect) + " bytes");
+    return cudaMemcpy((char*)dst + off, host, bytes, cudaMemcpyHostToDevice) == cudaSuccess ? SPOCK_OK
+                                                                                            : mfail(m, SPOCK_ERR_CUDA, "copy failed");
+  };
+  if (r == "embedding") return put(m->emb, (size_t)m->d.vocab * HID * 2);
+  if (r == "final_norm") return put(m->final_norm, HID * 2);
+  if (r.rfind("layer.", 0) != 0) return mfail(m, SPOCK_ERR_INVALID, "unknown role " + r);
+  const size_t dot = r.find('.', 6);
+  const int li = std::atoi(r.substr(6, dot - 6).c_str());
+  if (dot == std::string::npos || li < 0 || li >= m->d.num_layers) return mfail(m, SPOCK_ERR_INVALID, "bad layer in " + r);
+  const std::string n = r.substr(dot + 1);
+  auto& l = m->L[li];
+  if (n == "input_norm") return put(l.input_norm, HID * 2);
+  if (n == "post_norm") return put(l.post_norm, HID * 2);
+  if (n == "mlp_down") return put(l.w_down, (size_t)HID * INTER * 2);
+  if (n == "mlp_gate" || n == "mlp_up") {
+    // interleave gate/up rows in groups of 16 for the fused SwiGLU epilogue
+    if (bytes != (size_t)INTER * HID * 2) return mfail(m, SPOCK_ERR_INVALID, r + ": bad size");
+    std::vector<uint16_t> buf((size_t)INTER * HID);
+    std::memcpy(buf.data(), host, bytes);
+    const int half = n == "mlp_up" ? 16 : 0;
+    for (int gidx = 0; gidx < INTER / 16; ++gidx)
+      if (cudaMemcpy((char*)l.w_gu + ((size_t)(gidx * 32 + half) * HID) * 2, buf.data() + (size_t)gidx * 16 * HID,
+                     (size_t)16 * HID * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+        return mfail(m, SPOCK_ERR_CUDA, "copy failed");
+    return SPOCK_OK;
+  }
+  if (!l.attn) {
+    if (n == "delta_in_proj_qkv") return put(l.w_in, (size_t)CONV * HID * 2, 0);
+    if (n == "delta_in_proj_z") return put(l.w_in, (size_t)2048 * HID * 2, (size_t)CONV * HID * 2);
+    if (n == "delta_in_proj_a") return put(l.w_in, (size_t)DNH * HID * 2, (size_t)(CONV + 2048) * HID * 2);
+    if (n == "delta_in_proj_b") return put(l.w_in, (size_t)DNH * HID * 2, (size_t)(CONV + 2048 + DNH) * HID * 2);
+    if (n == "delta_out_proj") return put(l.w_out, (size_t)HID * 2048 * 2);
+    if (n == "delta_conv") return put(l.conv_w, (size_t)CONV * 4 * 2);
+    if (n == "delta_norm") return put(l.dn_norm, DND * 4);
+    if (n == "delta_a_log" || n == "delta_dt_bias") {
+      std::vector<float> ab(DNH * 2);
+      cudaMemcpy(ab.data(), l.a_log_bias, DNH * 2 * 4, cudaMemcpyDeviceToHost);
+      if (n == "delta_a_log") {
+        if (bytes != DNH * 4) return mfail(m, SPOCK_ERR_INVALID, r + ": bad size");
+        for (int h = 0; h < DNH; ++h) ab[h * 2] = static_cast<const float*>(host)[h];
+      } else {
+        if (bytes != DNH * 2) return mfail(m, SPOCK_ERR_INVALID, r + ": bad size");
+        for (int h = 0; h < DNH; ++h) {
+          __half hv;
+          std::memcpy(&hv, static_cast<const uint16_t*>(host) + h, 2);
+          ab[h * 2 + 1] = __half2float(hv);
+        }
+      }
+      return cudaMemcpy(l.a_log_bias, ab.data(), DNH * 2 * 4, cudaMemcpyHostToDevice) == cudaSuccess ? SPOCK_OK : SPOCK_ERR_CUDA;
+    }
+  } else {
+    if (n == "attn_q") return put(l.w_in, (size_t)QH * HD * 2 * HID * 2, 0);
+    if (n == "attn_k") return put(l.w_in, (size_t)KVH * HD * HID * 2, (size_t)QH * HD * 2 * HID * 2);
+    if (n == "attn_v") return put(l.w_in, (size_t)KVH * HD * HID * 2, (size_t)(QH * HD * 2 + KVH * HD) * HID * 2);
+    if (n == "attn_q_norm") return put(l.q_norm, HD * 2);
+    if (n == "attn_k_norm") return put(l.k_norm, HD * 2);
+    if (n == "attn_o") return put(l.w_out, (size_t)HID * QH * HD * 2);
+  }
+  return mfail(m, SPOCK_ERR_INVALID, "unknown role " + r);
+}
+
+// Zeroes recurrent state, conv and KV caches and positions for `batch` sequences.
+__attribute__((visibility("default"))) int spock_model_reset(spock_model* m, int32_t batch) {
+  if (!m || batch < 1 || batch > m->d.max_batch) return SPOCK_ERR_INVALID;
+  Guard g(m->device);
+  m->batch = batch;
+  const int B = m->bpad;
+  cudaMemset(m->dn_state, 0, (size_t)n_dn(m) * B * DNH * DND * DND * 4);
+  cudaMemset(m->conv_state, 0, (size_t)n_dn(m) * B * CONV * 4 * 2);
+  cudaMemset(m->pos, 0, (size_t)B * 4);
+  cudaError_t e = cudaMemset(m->kv, 0, (size_t)B * m->kv_seq_stride * 2);
+  return e == cudaSuccess ? SPOCK_OK : mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));
+}
+
+// One token per sequence. tokens_in / tokens_out: device int32 [batch];
+// hidden_out (nullable): device fp16 [batch][1024], the final-normed hidden.
+__attribute__((visibility("default"))) int spock_model_step(spock_model* m, const int32_t* tokens_in,
+                                                            int32_t* tokens_out, void* hidden_out, void* stream) {
+  if (!m || !tokens_in || m->batch < 1) return SPOCK_ERR_INVALID;
+  Guard g(m->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaMemcpyAsync(m->tok_in, tokens_in, (size_t)m->batch * 4, cudaMemcpyDeviceToDevice, st);
+  Status s = st ? ensure_graph(m, st) : Status::ok();
+  if (s.code) return mfail(m, s.code, s.msg);
+  if (st) {
+    cudaError_t e = cudaGraphLaunch(m->graph, st);
+    if (e != cudaSuccess) return mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));
+  } else {
+    s = record_step(m, st);
+    if (s.code) return mfail(m, s.code, s.msg);
+  }
+  if (tokens_out) cudaMemcpyAsync(tokens_out, m->tok_out, (size_t)m->batch * 4, cudaMemcpyDeviceToDevice, st);
+  if (hidden_out) cudaMemcpyAsync(hidden_out, m->x, (size_t)m->batch * HID * 2, cudaMemcpyDeviceToDevice, st);
+  return SPOCK_OK;
+}
+
+// Token-serial prefill of prompt[batch][len] (device int32), the reference's
+// own layer_major_prefill semantics (each prompt token through the decode
+// kernels), then `n_new` greedy tokens. out_tokens: device int32 [batch][n_new]
+// (the first entry is the prompt's greedy continuation).
+__attribute__((visibility("default"))) int spock_model_generate(spock_model* m, const int32_t* prompt, int32_t len,
+                                                                int32_t n_new, int32_t* out_tokens, void* stream) {
+  if (!m || !prompt || len < 1 || n_new < 0 || m->batch < 1 || len + n_new > m->d.max_seq) return SPOCK_ERR_INVALID;
+  Guard g(m->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!st) return mfail(m, SPOCK_ERR_INVALID, "spock_model_generate needs a non-default stream (graph replay)");
+  Status s = ensure_graph(m, st);
+  if (s.code) return mfail(m, s.code, s.msg);
+  const int B = m->batch;
+  std::vector<int32_t> col(B);
+  const unsigned nb = (unsigned)((B + 127) / 128);
+  for (int t = 0; t < len; ++t) {
+    spock::copy_col_kernel<<<nb, 128, 0, st>>>(m->tok_in, 1, 0, prompt, len, t, B);  // prompt column t
+    if (cudaGraphLaunch(m->graph, st) != cudaSuccess) return mfail(m, SPOCK_ERR_CUDA, "graph launch failed");
+  }
+  for (int i = 0; i < n_new; ++i) {
+    // the step left its argmax in tok_in: record it, then feed it back
+    spock::copy_col_kernel<<<nb, 128, 0, st>>>(out_tokens, n_new, i, m->tok_in, 1, 0, B);
+    if (i + 1 < n_new && cudaGraphLaunch(m->graph, st) != cudaSuccess) return mfail(m, SPOCK_ERR_CUDA, "graph launch failed");
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SPOCK_OK : mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));
+}
+
+}  // extern "C"

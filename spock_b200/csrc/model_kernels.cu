@@ -1,0 +1,240 @@
+// Decode glue around the DeltaNet mixer for the Qwen3.5-0.8B layout, batched
+// over independent sequences (one row per sequence). Each kernel restates a
+// reference shader's arithmetic, including its fp16 storage points:
+//   embed_kernel       shaders/embedding_lookup.comp
+//   rmsnorm_kernel     shaders/rms_norm.comp:31-70 (x * rsqrt(mean(x^2)+eps) * (1+w);
+//                      4 consecutive elements per lane, then a stride-128..1 tree)
+//   attn_prep_kernel   split_q_gate.comp + rms_norm_per_head.comp (q_norm, k_norm)
+//                      + rope_apply.comp (rotary 64 of 256, pairs d / d+32, host
+//                      cos/sin table) + kv_cache_store.comp, fused per head
+//   attn_decode_kernel attention_decode.comp (GQA 8 q / 2 kv heads, head 256,
+//                      softmax over positions 0..pos) + sigmoid_gate.comp, fused
+#include "common.cuh"
+
+namespace spock {
+namespace {
+
+constexpr int HID = 1024;
+constexpr int HD = 256;       // attention head dim
+constexpr int QH = 8, KVH = 2;
+constexpr int ROT = 64;
+
+__global__ void embed_kernel(const int* __restrict__ tokens, const uint4* __restrict__ emb, uint4* __restrict__ h,
+                             int batch) {
+  const int b = blockIdx.x;
+  if (b >= batch) return;
+  const int tok = tokens[b];
+  for (int i = threadIdx.x; i < HID / 8; i += blockDim.x) h[(size_t)b * (HID / 8) + i] = emb[(size_t)tok * (HID / 8) + i];
+}
+
+// One CTA (256 threads) per row.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__ x, const __half* __restrict__ w,
+                                                      __half* __restrict__ y, float eps, int batch) {
+  const int b = blockIdx.x, t = threadIdx.x;
+  if (b >= batch) return;
+  __shared__ float s[256];
+  const __half* xr = x + (size_t)b * HID;
+  float v[4], acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = __half2float(xr[t * 4 + i]);
+    acc = __fadd_rn(acc, __fmul_rn(v[i], v[i]));
+  }
+  s[t] = acc;
+  __syncthreads();
+  for (int stride = 128; stride > 0; stride >>= 1) {
+    if (t < stride) s[t] = __fadd_rn(s[t], s[t + stride]);
+    __syncthreads();
+  }
+  const float nf = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s[0], (float)HID), eps)));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float wv = __fadd_rn(1.0f, __half2float(w[t * 4 + i]));
+    y[(size_t)b * HID + t * 4 + i] = __float2half_rn(__fmul_rn(__fmul_rn(v[i], nf), wv));
+  }
+}
+
+// grid (QH + KVH, batch), 256 threads (thread d = head dimension d).
+// qkv: [batch][ld] with [q0 (256) | gate0 (256) | q1 | gate1 | ... | k (2x256) | v (2x256)].
+__global__ void __launch_bounds__(256)
+    attn_prep_kernel(const __half* __restrict__ qkv, int ld, const __half* __restrict__ qn_w,
+                     const __half* __restrict__ kn_w, const float* __restrict__ rope /*[max_seq][64] cos,sin*/,
+                     const int* __restrict__ pos, __half* __restrict__ q_out /*[batch][QH][HD]*/,
+                     __half* __restrict__ gate_out, __half* __restrict__ kv /*[batch][layers][max_seq][2][KVH][HD]*/,
+                     int64_t kv_seq_stride /*elements per sequence*/, int64_t kv_layer_off, float eps, float scale_unused) {
+  const int hh = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const __half* row = qkv + (size_t)b * ld;
+  __shared__ float s[256];
+  __shared__ float sn[256];
+  const bool is_q = hh < QH;
+  const int kvh = hh - QH;
+  const float x = __half2float(is_q ? row[hh * 2 * HD + d] : row[QH * 2 * HD + kvh * HD + d]);
+  if (is_q) gate_out[((size_t)b * QH + hh) * HD + d] = row[hh * 2 * HD + HD + d];
+  // per-head RMSNorm (rms_norm_per_head.comp: one element per lane, stride-128..1 tree)
+  s[d] = __fmul_rn(x, x);
+  __syncthreads();
+  for (int stride = 128; stride > 0; stride >>= 1) {
+    if (d < stride) s[d] = __fadd_rn(s[d], s[d + stride]);
+    __syncthreads();
+  }
+  const float nf = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s[0], (float)HD), eps)));
+  const float wv = __fadd_rn(1.0f, __half2float(is_q ? qn_w[d] : kn_w[d]));
+  const float xn = __half2float(__float2half_rn(__fmul_rn(__fmul_rn(x, nf), wv)));
+  sn[d] = xn;
+  __syncthreads();
+  // partial RoPE: pairs (d, d+32) for d < 32 of the first 64 dims
+  float o = xn;
+  const int p = pos[b];
+  if (d < ROT) {
+    const int i = d & 31;
+    const float c = rope[(size_t)p * ROT + 2 * i], sn_ = rope[(size_t)p * ROT + 2 * i + 1];
+    if (d < 32) o = __fsub_rn(__fmul_rn(xn, c), __fmul_rn(sn[d + 32], sn_));
+    else o = __fadd_rn(__fmul_rn(xn, c), __fmul_rn(sn[d - 32], sn_));
+  }
+  const __half oh = __float2half_rn(o);
+  if (is_q) {
+    q_out[((size_t)b * QH + hh) * HD + d] = oh;
+  } else {
+    __half* base = kv + (size_t)b * kv_seq_stride + kv_layer_off + (size_t)p * (2 * KVH * HD);
+    base[kvh * HD + d] = oh;                                          // K
+    base[KVH * HD + kvh * HD + d] = row[QH * 2 * HD + KVH * HD + kvh * HD + d];  // V (no norm, no rope)
+  }
+}
+
+// grid (KVH, batch), 256 threads = 8 warps. Warp w takes positions w, w+8, ...;
+// lane l owns dims 8l..8l+7 of the 4 query heads of this kv head (GQA group).
+// Online softmax per warp, merged across warps in shared memory; the output is
+// fp16(acc / (sum + 1e-30)) and then fp16(out * sigmoid(gate)).
+__global__ void __launch_bounds__(256)
+    attn_decode_kernel(const __half* __restrict__ q /*[batch][QH][HD]*/, const __half* __restrict__ gate,
+                       const __half* __restrict__ kv, int64_t kv_seq_stride, int64_t kv_layer_off,
+                       const int* __restrict__ pos, float scale, __half* __restrict__ out /*[batch][QH*HD]*/) {
+  const int kvh = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int G = QH / KVH;  // 4
+  const int L = pos[b] + 1;
+  float qv[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const uint4 u = *reinterpret_cast<const uint4*>(q + ((size_t)b * QH + kvh * G + g) * HD + lane * 8);
+    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(h2[k]);
+      qv[g][2 * k] = f.x;
+      qv[g][2 * k + 1] = f.y;
+    }
+  }
+  float m[G], l[G], acc[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[g][k] = 0.f;
+  }
+  const __half* base = kv + (size_t)b * kv_seq_stride + kv_layer_off;
+  for (int p = warp; p < L; p += 8) {
+    const __half* kr = base + (size_t)p * (2 * KVH * HD) + kvh * HD + lane * 8;
+    const __half* vr = base + (size_t)p * (2 * KVH * HD) + KVH * HD + kvh * HD + lane * 8;
+    const uint4 ku = *reinterpret_cast<const uint4*>(kr);
+    const uint4 vu = *reinterpret_cast<const uint4*>(vr);
+    float kf[8], vf[8];
+    const __half2* k2 = reinterpret_cast<const __half2*>(&ku);
+    const __half2* v2 = reinterpret_cast<const __half2*>(&vu);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 a = __half22float2(k2[k]), c = __half22float2(v2[k]);
+      kf[2 * k] = a.x;
+      kf[2 * k + 1] = a.y;
+      vf[2 * k] = c.x;
+      vf[2 * k + 1] = c.y;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float dot = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) dot = fmaf(qv[g][k], kf[k], dot);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      const float sc = dot * scale;
+      const float mn = fmaxf(m[g], sc);
+      const float corr = expf(m[g] - mn), w = expf(sc - mn);
+      l[g] = l[g] * corr + w;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[g][k] = fmaf(w, vf[k], acc[g][k] * corr);
+      m[g] = mn;
+    }
+  }
+  __shared__ float sm_m[8][G], sm_l[8][G];
+  __shared__ float sm_acc[8][G][HD];
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      sm_m[warp][g] = m[g];
+      sm_l[warp][g] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sm_acc[warp][g][lane * 8 + k] = acc[g][k];
+  __syncthreads();
+  // thread t -> (g = t / 64, dims 4*(t%64)..+3)
+  const int g = threadIdx.x >> 6, d0 = (threadIdx.x & 63) * 4;
+  float mt = -INFINITY;
+  for (int w = 0; w < 8; ++w) mt = fmaxf(mt, sm_m[w][g]);
+  float lt = 0.f, at[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int w = 0; w < 8; ++w) {
+    if (sm_m[w][g] == -INFINITY) continue;
+    const float c = expf(sm_m[w][g] - mt);
+    lt += sm_l[w][g] * c;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) at[k] += sm_acc[w][g][d0 + k] * c;
+  }
+  const float inv = 1.0f / (lt + 1e-30f);
+  const int qh = kvh * G + g;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float a16 = __half2float(__float2half_rn(at[k] * inv));
+    const float gt = __half2float(gate[((size_t)b * QH + qh) * HD + d0 + k]);
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gt)));
+    out[((size_t)b * QH + qh) * HD + d0 + k] = __float2half_rn(__fmul_rn(a16, sig));
+  }
+}
+
+}  // namespace
+
+Status launch_embed(const int* tokens, const void* emb, void* h, int batch, cudaStream_t st) {
+  embed_kernel<<<batch, 128, 0, st>>>(tokens, (const uint4*)emb, (uint4*)h, batch);
+  SPOCK_LAUNCH_CHECK("embed_kernel");
+  return Status::ok();
+}
+
+Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batch, cudaStream_t st) {
+  rmsnorm_kernel<<<batch, 256, 0, st>>>((const __half*)x, (const __half*)w, (__half*)y, eps, batch);
+  SPOCK_LAUNCH_CHECK("rmsnorm_kernel");
+  return Status::ok();
+}
+
+Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* kn_w, const float* rope,
+                        const int* pos, void* q_out, void* gate_out, void* kv, int64_t kv_seq_stride,
+                        int64_t kv_layer_off, float eps, int batch, cudaStream_t st) {
+  attn_prep_kernel<<<dim3(QH + KVH, batch), 256, 0, st>>>((const __half*)qkv, ld, (const __half*)qn_w,
+                                                           (const __half*)kn_w, rope, pos, (__half*)q_out,
+                                                           (__half*)gate_out, (__half*)kv, kv_seq_stride,
+                                                           kv_layer_off, eps, 0.f);
+  SPOCK_LAUNCH_CHECK("attn_prep_kernel");
+  return Status::ok();
+}
+
+Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
+                          int64_t kv_layer_off, const int* pos, float scale, void* out, int batch,
+                          cudaStream_t st) {
+  attn_decode_kernel<<<dim3(KVH, batch), 256, 0, st>>>((const __half*)q, (const __half*)gate, (const __half*)kv,
+                                                        kv_seq_stride, kv_layer_off, pos, scale, (__half*)out);
+  SPOCK_LAUNCH_CHECK("attn_decode_kernel");
+  return Status::ok();
+}
+
+}  // namespace spock

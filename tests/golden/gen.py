@@ -86,3 +86,45 @@ def decode_inputs(batch, heads=16, k_dim=128, v_dim=128, ks=4, seed=0):
     dt = np.float16(rng.standard_normal(heads, dtype=np.float32) * 0.1).astype(np.float32)
     d["a_log_bias"] = np.stack([a_log, dt], 1).astype(np.float32)
     return d
+
+
+def model_weights(layers=24, vocab=248320, seed=0):
+    """Random-init weights in the Qwen3.5-0.8B layout under the reference's role
+    names: fp16 matrices ~ N(0, 0.02), (1+w) RMSNorm weights
+    w ~ N(0, 0.1) fp16, A_log ~ U(-2, 1) fp32, dt_bias ~ N(0, 0.1) fp16, conv
+    weight ~ N(0, 0.02) fp16, gated-norm weight 1 + N(0, 0.1) fp32. Matrices as
+    uint16 fp16 bits [out][in]."""
+    rng = np.random.default_rng(seed)
+
+    def mat(o, i, sd=0.02):
+        return (rng.standard_normal((o, i), dtype=np.float32) * sd).astype(np.float16).view(np.uint16)
+
+    def vec16(n, sd=0.1):
+        return (rng.standard_normal(n, dtype=np.float32) * sd).astype(np.float16).view(np.uint16)
+
+    w = {"embedding": mat(vocab, 1024), "final_norm": vec16(1024)}
+    for i in range(layers):
+        p = f"layer.{i}."
+        w[p + "input_norm"] = vec16(1024)
+        w[p + "post_norm"] = vec16(1024)
+        w[p + "mlp_gate"] = mat(3584, 1024)
+        w[p + "mlp_up"] = mat(3584, 1024)
+        w[p + "mlp_down"] = mat(1024, 3584)
+        if i % 4 == 3:
+            w[p + "attn_q"] = mat(4096, 1024)
+            w[p + "attn_k"] = mat(512, 1024)
+            w[p + "attn_v"] = mat(512, 1024)
+            w[p + "attn_q_norm"] = vec16(256)
+            w[p + "attn_k_norm"] = vec16(256)
+            w[p + "attn_o"] = mat(1024, 2048)
+        else:
+            w[p + "delta_in_proj_qkv"] = mat(6144, 1024)
+            w[p + "delta_in_proj_z"] = mat(2048, 1024)
+            w[p + "delta_in_proj_a"] = mat(16, 1024)
+            w[p + "delta_in_proj_b"] = mat(16, 1024)
+            w[p + "delta_conv"] = mat(6144, 4)
+            w[p + "delta_norm"] = (1.0 + 0.1 * rng.standard_normal(128, dtype=np.float32)).astype(np.float32)
+            w[p + "delta_a_log"] = rng.uniform(-2, 1, 16).astype(np.float32)
+            w[p + "delta_dt_bias"] = vec16(16)
+            w[p + "delta_out_proj"] = mat(1024, 2048)
+    return w
