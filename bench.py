@@ -316,13 +316,143 @@ def bench_decode(args, ws, rank, local):
     }
 
 
+# ------------------------------------------------------------ configs 3 / 4 ---
+
+def model_weights_gpu(layers, vocab, seed, dev):
+    """Random-init Qwen3.5-0.8B-layout weights (config 3 distributions), drawn on
+    the GPU for speed and returned as host arrays for spock_model_set_weight."""
+    import numpy as np
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    def mat(o, i, sd=0.02):
+        return (torch.randn(o, i, device=dev, generator=g) * sd).half().view(torch.int16).cpu().numpy().view(np.uint16)
+    def vec16(n, sd=0.1):
+        return (torch.randn(n, device=dev, generator=g) * sd).half().view(torch.int16).cpu().numpy().view(np.uint16)
+    w = {"embedding": mat(vocab, 1024), "final_norm": vec16(1024)}
+    for i in range(layers):
+        p = f"layer.{i}."
+        w[p + "input_norm"] = vec16(1024)
+        w[p + "post_norm"] = vec16(1024)
+        w[p + "mlp_gate"] = mat(3584, 1024)
+        w[p + "mlp_up"] = mat(3584, 1024)
+        w[p + "mlp_down"] = mat(1024, 3584)
+        if i % 4 == 3:
+            w[p + "attn_q"] = mat(4096, 1024)
+            w[p + "attn_k"] = mat(512, 1024)
+            w[p + "attn_v"] = mat(512, 1024)
+            w[p + "attn_q_norm"] = vec16(256)
+            w[p + "attn_k_norm"] = vec16(256)
+            w[p + "attn_o"] = mat(1024, 2048)
+        else:
+            w[p + "delta_in_proj_qkv"] = mat(6144, 1024)
+            w[p + "delta_in_proj_z"] = mat(2048, 1024)
+            w[p + "delta_in_proj_a"] = mat(16, 1024)
+            w[p + "delta_in_proj_b"] = mat(16, 1024)
+            w[p + "delta_conv"] = mat(6144, 4)
+            w[p + "delta_norm"] = (1.0 + 0.1 * torch.randn(128, device=dev, generator=g)).float().cpu().numpy()
+            w[p + "delta_a_log"] = (torch.rand(16, device=dev, generator=g) * 3 - 2).float().cpu().numpy()
+            w[p + "delta_dt_bias"] = vec16(16)
+            w[p + "delta_out_proj"] = mat(1024, 2048)
+    return w
+
+
+def bench_model(args, ws, rank, local):
+    """Config 4 (greedy decode after a 512-token prompt) or config 3 (prompt
+    prefill). A step is one token for every sequence of this GPU's batch."""
+    import numpy as np
+    import torch
+    import spock_b200
+    dev = torch.device("cuda", local)
+    B, P, layers, vocab = args.batch, args.prompt, 24, 248320
+    w = model_weights_gpu(layers, vocab, 7, dev)
+    m = spock_b200.Model(layers, vocab, max_batch=B, max_seq=P + args.steps + args.warmup + 8, device=local)
+    m.set_weights(w)
+    del w
+    m.reset(B)
+    stream = torch.cuda.Stream(device=dev)
+    prompt = torch.randint(0, vocab, (B, P), generator=torch.Generator().manual_seed(rank), dtype=torch.int32).to(dev)
+    cnt = spock_b200.lib().spock_kernel_launch_count
+    with torch.cuda.stream(stream):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0 = cnt()
+        m.generate(prompt[:, :1], 1, stream=stream)  # captures the step graph: counts its kernels once
+        per_step = cnt() - c0
+        m.reset(B)
+        stream.synchronize()
+        if args.config == 3:
+            # prefill: P prompt tokens (token-serial, graph replayed), timed as a whole
+            m.generate(prompt[:, :8], 1, stream=stream)  # warm-up + graph capture
+            m.reset(B)
+            stream.synchronize()
+            barrier(ws)
+            with ClockSampler(local) as clk:
+                t0.record(stream)
+                m.generate(prompt, 1, stream=stream)
+                t1.record(stream)
+                stream.synchronize()
+            steps = P
+        else:
+            m.generate(prompt, 1 + args.warmup, stream=stream)  # prefill + graph capture + warm-up
+            stream.synchronize()
+            tok = torch.zeros(B, dtype=torch.int32, device=dev)
+            barrier(ws)
+            with ClockSampler(local) as clk:
+                t0.record(stream)
+                for _ in range(args.steps):
+                    tok, _h = m.step(tok, stream=stream)
+                t1.record(stream)
+                stream.synchronize()
+            steps = args.steps
+    launches = per_step * steps  # graph replays: kernels per step x timed steps
+    ms = max_over_ranks(t0.elapsed_time(t1), ws) / steps
+    value = B * ws / (ms / 1e3)
+    hbm, tf, pk = peaks()
+    w_bytes = 752.4e6 * 2
+    state_bytes = B * 18 * (16 * 128 * 128 * 4 * 2 + 6144 * 4 * 2 * 2)
+    kv_bytes = B * 6 * 2 * 2 * 256 * 2 * (P + steps // 2)
+    alg = w_bytes + state_bytes + kv_bytes
+    gbs = alg / (ms / 1e3) / 1e9
+    # end to end through the public API: host prompt -> device, generate, tokens -> host
+    hp = prompt[:, : min(P, 16)].cpu().pin_memory()
+    n_e2e = 16
+    m.reset(B)
+    with torch.cuda.stream(stream):
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        dp = hp.to(dev, non_blocking=True)
+        out = m.generate(dp, n_e2e, stream=stream)
+        ho = out.to("cpu", non_blocking=True)
+        a1.record(stream)
+        stream.synchronize()
+    e2e_ms = max_over_ranks(a0.elapsed_time(a1), ws)
+    e2e_val = B * ws * (hp.shape[1] + n_e2e - 1) / (e2e_ms / 1e3)
+    m.close()
+    name = "full-model greedy decode tok/s" if args.config == 4 else "full-model token-serial prefill tok/s"
+    return {
+        "metric": name, "value": round(value, 1), "unit": "tok/s", "n_gpus": ws, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 weights/activations, fp32 accumulation and DeltaNet state",
+        "data": "synthetic (random-init Qwen3.5-0.8B layout, seeded random prompt)",
+        "config": {"workload": f"config {args.config}", "sequences_per_gpu": B, "prompt": P, "layers": layers,
+                   "vocab": vocab, "parallelism": f"dp{ws} over sequences",
+                   "l2": "weights (1.5 GB) larger than L2"},
+        "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "h2d_bytes_per_step": int(hp.numel() * 4 / (hp.shape[1] + n_e2e - 1)),
+                "d2h_bytes_per_step": int(B * 4), "note": f"{hp.shape[1]}-token prompt + {n_e2e} new tokens via spock_model_generate"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                     "traffic": None, "peak_source": pk, "alg_bytes_per_step": int(alg)},
+        "clocks": clk.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="spock_b200", choices=["spock_b200", "reference"])
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4])
+    ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--layers", type=int, default=18)
@@ -330,7 +460,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.batch is None:
-        args.batch = 64
+        args.batch = {1: 64, 2: 64, 3: 1, 4: 1}[args.config]
     args.warmup = max(args.warmup, 3) if args.impl != "reference" else args.warmup
     ws, rank, local = dist_init(args)
 
@@ -355,7 +485,12 @@ def main():
                 flush=True)
         return
 
-    res = bench_chunk(args, ws, rank, local) if args.config == 2 else bench_decode(args, ws, rank, local)
+    if args.config == 2:
+        res = bench_chunk(args, ws, rank, local)
+    elif args.config == 1:
+        res = bench_decode(args, ws, rank, local)
+    else:
+        res = bench_model(args, ws, rank, local)
     if rank == 0:
         if ws == 1 and not args.no_cpu_baseline and args.config == 2:
             threads = os.cpu_count() or 1
