@@ -375,13 +375,13 @@ def bench_model(args, ws, rank, local):
     with torch.cuda.stream(stream):
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c0 = cnt()
-        m.generate(prompt[:, :1], 1, stream=stream)  # captures the step graph: counts its kernels once
+        m.generate(prompt[:, :1].contiguous(), 1, stream=stream)  # captures the step graph: counts its kernels once
         per_step = cnt() - c0
         m.reset(B)
         stream.synchronize()
         if args.config == 3:
             # prefill: P prompt tokens (token-serial, graph replayed), timed as a whole
-            m.generate(prompt[:, :8], 1, stream=stream)  # warm-up + graph capture
+            m.generate(prompt[:, :8].contiguous(), 1, stream=stream)  # warm-up + graph capture
             m.reset(B)
             stream.synchronize()
             barrier(ws)
@@ -413,7 +413,7 @@ def bench_model(args, ws, rank, local):
     alg = w_bytes + state_bytes + kv_bytes
     gbs = alg / (ms / 1e3) / 1e9
     # end to end through the public API: host prompt -> device, generate, tokens -> host
-    hp = prompt[:, : min(P, 16)].cpu().pin_memory()
+    hp = prompt[:, : min(P, 16)].contiguous().cpu().pin_memory()
     n_e2e = 16
     m.reset(B)
     with torch.cuda.stream(stream):
