@@ -365,7 +365,7 @@ def bench_model(args, ws, rank, local):
     dev = torch.device("cuda", local)
     B, P, layers, vocab = args.batch, args.prompt, 24, 248320
     w = model_weights_gpu(layers, vocab, 7, dev)
-    m = spock_b200.Model(layers, vocab, max_batch=B, max_seq=P + args.steps + args.warmup + 8, device=local)
+    m = spock_b200.Model(layers, vocab, max_batch=B, max_seq=P + args.steps + args.warmup + 48, device=local)
     m.set_weights(w)
     del w
     m.reset(B)
