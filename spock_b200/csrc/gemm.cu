@@ -8,9 +8,11 @@
 // one pass over the weights serves the whole batch; decode is HBM-bound on W.
 // Accumulators live in TMEM (lane = weight row, column = batch row).
 //
-// Grid: (row tiles, K splits). With K splits, every CTA writes its fp32 partial
-// tile to a workspace; the last CTA of a tile (atomic ticket) sums the
-// partials in split order (deterministic) and runs the epilogue.
+// Grid: (row tiles, K splits). With K splits, every CTA adds its fp32 partial
+// tile into an accumulator with vector atomics (L2-side, all splits in
+// parallel); the last CTA of a tile (atomic ticket) reads the sum once, clears
+// it for the next launch and runs the epilogue. The split count is capped so
+// partial traffic stays below the weight traffic it parallelises.
 //
 // Epilogues (fused):
 //   F16      y = fp16(acc)
@@ -40,7 +42,7 @@ struct GemmArgs {
   __half* y;        // [batch][ldy]
   int ldy;
   const __half* res;    // RESIDUAL: [batch][ldy]
-  float* ws;            // split partials [nsplit][n_tiles*128][bpad]
+  float* ws;            // split accumulator [n_tiles*128][bpad], zero between launches
   int* tickets;         // [n_tiles], zero before launch, left zero after
   float* amax_val;      // ARGMAX partials [n_tiles][batch]
   int* amax_idx;
@@ -153,16 +155,17 @@ __global__ void __launch_bounds__(128, 1)
   const size_t tile_stride = (size_t)gridDim.x * 128 * a.bpad;
 
   bool finisher = true;
+  (void)tile_stride;
   if (a.nsplit > 1) {
-    // partial tile -> workspace [split][row][col]
-    float* wsp = a.ws + split * tile_stride + (size_t)row * a.bpad;
+    // partial tile -> accumulator [row][col] (vector atomics, resolved in L2)
+    float* wsp = a.ws + (size_t)row * a.bpad;
     for (int c0 = 0; c0 < a.bpad; c0 += 32) {
       float v[32];
       tc::tmem_ld32(taddr + c0, v);
 #pragma unroll
       for (int q = 0; q < 8; ++q)
         if (c0 + 4 * q < a.bpad)
-          reinterpret_cast<float4*>(wsp + c0)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          atomicAdd(reinterpret_cast<float4*>(wsp + c0) + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
     }
     __threadfence();
     __syncthreads();
@@ -180,19 +183,18 @@ __global__ void __launch_bounds__(128, 1)
     for (int c0 = 0; c0 < a.bpad; c0 += 32) {
       float v[32];
       if (a.nsplit > 1) {
+        float4* p = reinterpret_cast<float4*>(a.ws + (size_t)row * a.bpad + c0);
 #pragma unroll
-        for (int k = 0; k < 32; ++k) v[k] = 0.f;
-        for (int s = 0; s < a.nsplit; ++s) {  // fixed order: deterministic
-          const float* p = a.ws + s * tile_stride + (size_t)row * a.bpad + c0;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            if (c0 + 4 * q < a.bpad) {
-              const float4 x = __ldcg(reinterpret_cast<const float4*>(p) + q);
-              v[4 * q] += x.x;
-              v[4 * q + 1] += x.y;
-              v[4 * q + 2] += x.z;
-              v[4 * q + 3] += x.w;
-            }
+        for (int q = 0; q < 8; ++q) {
+          if (c0 + 4 * q < a.bpad) {
+            const float4 x = __ldcg(p + q);
+            v[4 * q] = x.x;
+            v[4 * q + 1] = x.y;
+            v[4 * q + 2] = x.z;
+            v[4 * q + 3] = x.w;
+            __stcg(p + q, make_float4(0.f, 0.f, 0.f, 0.f));  // cleared for the next launch
+          } else {
+            v[4 * q] = v[4 * q + 1] = v[4 * q + 2] = v[4 * q + 3] = 0.f;
           }
         }
       } else {
@@ -348,8 +350,11 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   s = map2d(&mx, x, a.bpad, a.k, a.bpad);
   if (s.code) return s;
   const int ntiles = (a.n_out + 127) / 128, kbs = a.k / 64;
-  if (a.nsplit < 1) {  // enough CTAs to stream the weights from every SM
+  if (a.nsplit < 1) {  // enough CTAs to stream the weights from every SM ...
     int want = (sms + ntiles - 1) / ntiles;
+    // ... but no more partial-tile traffic (128 x bpad fp32) than weight traffic
+    const int cap = a.k / (2 * a.bpad);
+    want = want > cap ? cap : want;
     want = want < 1 ? 1 : want;
     a.nsplit = want > kbs ? kbs : want;
   }

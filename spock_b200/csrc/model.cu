@@ -265,8 +265,8 @@ __attribute__((visibility("default"))) int spock_model_create(spock_ctx* ctx, co
   A(&m->mlp, (size_t)B * INTER * 2);
   A(&m->q, (size_t)B * QH * HD * 2);
   A(&m->gate, (size_t)B * QH * HD * 2);
-  // split-K workspace: up to 148 CTAs per GEMM of 128 x bpad fp32 partials, twice for slack
-  A(&m->ws, (size_t)2 * m->sms * 128 * B * 4 + (size_t)((DN_IN + 127) / 128) * 128 * B * 4 * 2);
+  // split-K accumulator: one 128 x bpad fp32 tile per weight-row tile of the largest split GEMM
+  A(&m->ws, (size_t)((2 * INTER + 127) / 128 + (DN_IN + 127) / 128) * 128 * B * 4);
   A(&m->tickets, (size_t)((d->vocab + 127) / 128 + 64) * 4);
   A(&m->amax_val, (size_t)((d->vocab + 127) / 128) * B * 4);
   A(&m->amax_idx, (size_t)((d->vocab + 127) / 128) * B * 4);
