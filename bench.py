@@ -95,7 +95,7 @@ def dist_init(args):
         backend = "nccl" if args.impl != "reference" else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
-        dist.init_process_group(backend)
+        dist.init_process_group(backend, device_id=torch.device("cuda", local) if backend == "nccl" else None)
     elif args.impl != "reference":
         torch.cuda.set_device(0)
     return ws, rank, local
