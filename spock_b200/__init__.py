@@ -65,7 +65,9 @@ _LIB = None
 
 def build(force=False):
     from . import build as _b
-    return _b.build(force=force)
+    lib_path = _b.build(force=force)
+    _b.build_apps(force=force)
+    return lib_path
 
 
 def lib():

@@ -43,5 +43,29 @@ def build(force=False, verbose=False):
     return LIB
 
 
+APPS = {"spock-deltanet-chunk": "spock_deltanet_chunk.cpp", "spock-decode": "spock_decode.cpp",
+        "spock-bench": "spock_bench.cpp"}
+BIN = os.path.join(HERE, "bin")
+
+
+def build_apps(force=False, verbose=False):
+    """The reference's CLIs over the C ABI, linked against libspock_b200.so."""
+    os.makedirs(BIN, exist_ok=True)
+    for name, src in APPS.items():
+        out = os.path.join(BIN, name)
+        srcp = os.path.join(HERE, "apps", src)
+        deps = [srcp, LIB] + [os.path.join(HERE, "apps", f) for f in os.listdir(os.path.join(HERE, "apps"))]
+        if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out) for d in deps):
+            continue
+        cmd = [NVCC, "-O2", "-std=c++17", "-x", "cu", srcp, "-o", out, "-L" + HERE, "-lspock_b200",
+               "-Xlinker", "-rpath,$ORIGIN/..", "-gencode", "arch=compute_100a,code=sm_100a"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if verbose or r.returncode:
+            sys.stderr.write(r.stdout + r.stderr)
+        if r.returncode:
+            raise RuntimeError("nvcc failed on " + src)
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    build_apps(force="--force" in sys.argv, verbose="-v" in sys.argv)
