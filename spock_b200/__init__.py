@@ -64,7 +64,7 @@ _LIB = None
 
 
 def build(force=False):
-    from . import build as _b
+    from . import builder as _b
     lib_path = _b.build(force=force)
     _b.build_apps(force=force)
     return lib_path
