@@ -65,7 +65,7 @@ constexpr int SMEM_BYTES = OFF_SMALL + SMALL_BYTES + 1024;
 
 enum Bar {
   QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE, TBE_READY, WT_DONE,
-  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, DRAIN, NUM_BARS
+  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, AW_READY, DRAIN, NUM_BARS
 };
 
 struct Small {
@@ -232,6 +232,7 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
     // (a) U + MMA1 of item n: D1 = [T diag(beta); 0] V ; D1 += [-W ; Q'] S16
     if (!wait_bar(&sh->bar[PREP_DONE], n & 1, abort)) goto fail;
     if (!wait_bar(&sh->bar[S16_READY], n & 1, abort)) goto fail;
+    if (!wait_bar(&sh->bar[AW_READY], n & 1, abort)) goto fail;
     tc::tc_fence_after();
     for (int ks = 0; ks < 4; ++ks)
       tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + ks * 32, 16, 1024),
@@ -292,7 +293,7 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
   volatile int* abort = &sh->abort;
   const int t = threadIdx.x, l = t & 127, hf = t >> 7;
   const uint32_t lane_base = (uint32_t)((l >> 5) * 32) << 16;
-  const uint32_t tG1 = tb + 256 + lane_base + hf * 32, tWT = tb + 320 + lane_base + hf * 32;
+  const uint32_t tG1 = tb + 256 + lane_base + hf * 32;
   float* NM = reinterpret_cast<float*>(sm + OFF_NM);
   float* TM = reinterpret_cast<float*>(sm + OFF_TM);
   float* YM = reinterpret_cast<float*>(sm + OFF_YM);
@@ -351,45 +352,43 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_A], 0);
     PROF_MARK(0, 2);
-    // 3. G1 epilogue on 32 columns: P row (kept in registers) or N row
-    if (!wait_all(G1_DONE, n & 1)) break;
-    PROF_MARK(0, 3);
-    tc::tc_fence_after();
+    // 3. G1 epilogue on 32 columns: P row (kept in registers) or N row. The
+    //    decay factors (and scale / -beta) are formed while G1 is in flight.
     uint4 preg[4];
     {
-      float a[32];
-      tc::tmem_ld32(tG1, a);
       const float* gl = sh->gl[s];
-      const int j0 = hf * 32;
-      float glj[32];  // broadcast float4 loads of this half's exponents
+      const int j0 = hf * 32, row = l & 63;
+      const float gi = gl[row];
+      const float f = (l < C) ? scale : -sh->beta[s][row];
+      float dec[32];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float4 v4 = *reinterpret_cast<const float4*>(gl + j0 + 4 * q);
-        glj[4 * q] = v4.x;
-        glj[4 * q + 1] = v4.y;
-        glj[4 * q + 2] = v4.z;
-        glj[4 * q + 3] = v4.w;
+        const float gj[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = j0 + 4 * q + k;
+          const bool keep = (l < C) ? (j <= row) : (j < row);
+          dec[4 * q + k] = keep ? f * ex2(gi - gj[k]) : 0.f;
+        }
       }
+      if (!wait_all(G1_DONE, n & 1)) break;
+      PROF_MARK(0, 3);
+      tc::tc_fence_after();
+      float a[32];
+      tc::tmem_ld32(tG1, a);
       if (l < C) {
-        const float gi = gl[l];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float x[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int j = j0 + q * 8 + k;
-            x[k] = (j <= l) ? (a[q * 8 + k] * scale) * ex2(gi - glj[q * 8 + k]) : 0.f;
-          }
+          for (int k = 0; k < 8; ++k) x[k] = a[q * 8 + k] * dec[q * 8 + k];
           preg[q] = pack8(x);
         }
       } else {
         const int i = l - C;
-        const float gi = gl[i], nb = -sh->beta[s][i];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const int j = j0 + k;
-          NM[i * LDN + j] = (j < i) ? (nb * a[k]) * ex2(gi - glj[k]) : 0.f;
-        }
+        for (int k = 0; k < 32; ++k) NM[i * LDN + j0 + k] = a[k] * dec[k];
       }
     }
     if constexpr (kBf16) {  // K -> fp16 in place (G1, the only bf16 reader, is done)
@@ -450,52 +449,8 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
       const int i = t >> 2;
 #pragma unroll
       for (int q = 0; q < 2; ++q) *reinterpret_cast<uint4*>(sm + OFF_TB + sw128(i, (t & 3) * 2 + q)) = tbreg[q];
-      const int row = t & 63, h = (t >> 6) & 1, c0 = (t >> 7) * 4;
-      const float f = scale * sh->eg[s][row];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const int ch = c0 + cc;
-        float x[8];
-        const uint4 raw = *reinterpret_cast<const uint4*>(qk + h * 16384 + sw128(row, ch));
-        if constexpr (kBf16) {
-          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f2 = __bfloat1622float2(b2[k]);
-            x[2 * k] = f2.x;
-            x[2 * k + 1] = f2.y;
-          }
-        } else {
-          unpack8(raw, x);
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] *= f;
-        *reinterpret_cast<uint4*>(sm + OFF_AW + h * 16384 + sw128(64 + row, ch)) = pack8(x);
-      }
     }
     PROF_MARK(0, 8);
-    // 7. -W -> AW rows 0..63 (lane l holds column kd = l of W, rows hf*32 ..)
-    if (!wait_all(WT_DONE, n & 1)) break;
-    PROF_MARK(0, 9);
-    tc::tc_fence_after();
-    {
-      float w[32];
-      tc::tmem_ld32(tWT, w);
-      // lanes kd, kd^1 hold adjacent columns: exchange so that each stores one
-      // 32-bit pair (even lane: even rows, odd lane: odd rows)
-      const int h = l >> 6, cc = l & 63, ch = cc >> 3, e = cc & 6, odd = l & 1;
-      uint8_t* base = sm + OFF_AW + h * 16384 + e * 2;
-#pragma unroll
-      for (int k = 0; k < 32; k += 2) {
-        const float mine = odd ? w[k] : w[k + 1];      // value the partner needs
-        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
-        const int row = hf * 32 + k + odd;
-        const float lo = odd ? other : w[k], hi = odd ? w[k + 1] : other;
-        *reinterpret_cast<uint32_t*>(base + sw128(row, ch)) = pack_h2(-lo, -hi);
-      }
-    }
-    tc::tc_fence_before();
-    PROF_MARK(0, 10);
     // 8. once the previous item's output MMA has read it: P
     if (n > 0 && !wait_all(M2_DONE, (n - 1) & 1)) break;
     PROF_MARK(0, 11);
@@ -525,7 +480,7 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
   volatile int* abort = &sh->abort;
   const int rt = threadIdx.x - kRecBase;
   const uint32_t lane_base = (uint32_t)((rt >> 5) * 32) << 16;
-  const uint32_t tS = tb + lane_base, tD1 = tb + 128 + lane_base;
+  const uint32_t tS = tb + lane_base, tD1 = tb + 128 + lane_base, tWT = tb + 320 + lane_base;
   int N = it.count();
   auto sync = [] { group_sync(BAR_REC, 128); };
   auto wait_all = [&](int b, uint32_t parity) -> bool {
@@ -591,6 +546,52 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     tc::tc_fence_before();
     sync();
     if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[S16_READY], 0);
+    // 2b. A operand of MMA1: -W (from W^T in TMEM) and Q' = diag(s e^gc) Q.
+    //     MMA1 of the previous item, the last reader of AW, has completed.
+    if (!wait_all(WT_DONE, n & 1)) break;
+    tc::tc_fence_after();
+    {
+      float w[64];
+      tc::tmem_ld32(tWT, *reinterpret_cast<float(*)[32]>(&w[0]));
+      tc::tmem_ld32(tWT + 32, *reinterpret_cast<float(*)[32]>(&w[32]));
+      // lanes kd, kd^1 hold adjacent columns: exchange so that each stores one
+      // 32-bit pair (even lane: even rows, odd lane: odd rows)
+      const int h = rt >> 6, cc = rt & 63, ch = cc >> 3, e = cc & 6, odd = rt & 1;
+      uint8_t* base = sm + OFF_AW + h * 16384 + e * 2;
+#pragma unroll
+      for (int k = 0; k < 64; k += 2) {
+        const float mine = odd ? w[k] : w[k + 1];
+        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+        const float lo = odd ? other : w[k], hi = odd ? w[k + 1] : other;
+        *reinterpret_cast<uint32_t*>(base + sw128(k + odd, ch)) = pack_h2(-lo, -hi);
+      }
+      const uint8_t* qk = sm + OFF_QK + s * 32768;
+      const int row = rt & 63, hq = rt >> 6;
+      const float f = 0.08838834764831845f * sh->eg[s][row];
+#pragma unroll
+      for (int ch2 = 0; ch2 < 8; ++ch2) {
+        float x[8];
+        const uint4 raw = *reinterpret_cast<const uint4*>(qk + hq * 16384 + sw128(row, ch2));
+        if constexpr (kBf16) {
+          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f2 = __bfloat1622float2(b2[k]);
+            x[2 * k] = f2.x;
+            x[2 * k + 1] = f2.y;
+          }
+        } else {
+          unpack8(raw, x);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] *= f;
+        *reinterpret_cast<uint4*>(sm + OFF_AW + hq * 16384 + sw128(64 + row, ch2)) = pack8(x);
+      }
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    sync();
+    if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[AW_READY], 0);
     PROF_MARK(1, 2);
     // 3. v_new rows (lanes 0..63) -> VN, VS
     if (!wait_all(M1_DONE, n & 1)) break;
