@@ -65,7 +65,7 @@ constexpr int SMEM_BYTES = OFF_SMALL + SMALL_BYTES + 1024;
 
 enum Bar {
   QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE, TBE_READY, WT_DONE,
-  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, AW_READY, DRAIN, NUM_BARS
+  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, AW_READY, GC_READY0, GC_READY1, DRAIN, NUM_BARS
 };
 
 struct Small {
@@ -350,7 +350,12 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     if (!wait_all(QK_FULL0 + s, (n >> 1) & 1)) break;
     PROF_MARK(0, 1);
     sync();
-    if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_A], 0);
+    if (t == 0) {
+      tc::mbar_arrive_expect_tx(&sh->bar[PREP_A], 0);
+      // per-stage copy for the REC warps: they may lag this prep by more than
+      // one item, which a single barrier's parity could not tell apart
+      tc::mbar_arrive_expect_tx(&sh->bar[GC_READY0 + s], 0);
+    }
     PROF_MARK(0, 2);
     // 3. G1 epilogue on 32 columns: P row (kept in registers) or N row. The
     //    decay factors (and scale / -beta) are formed while G1 is in flight.
@@ -416,7 +421,9 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     chunk::solve_unit_lower_fast<kPrepThreads>(NM, TM, YM, t, sync);
 #endif
     PROF_MARK(0, 5);
-    // 5. T diag(beta e^gc) -> TBE (for W^T); T diag(beta) kept in registers
+    // 5. T diag(beta e^gc) -> TBE (for W^T) once W^T of the previous item has
+    //    read it; T diag(beta) kept in registers
+    if (n > 0 && !wait_all(WT_DONE, (n - 1) & 1)) break;
     uint4 tbreg[2];
     {
       const int i = t >> 2;
@@ -526,7 +533,7 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     }
     PROF_MARK(1, 0);
     // 2. S16 <- S ; S <- e^{gL} S
-    if (!wait_all(PREP_A, n & 1)) break;
+    if (!wait_all(GC_READY0 + s, (n >> 1) & 1)) break;
     PROF_MARK(1, 1);
     const float egL = sh->eg[s][C - 1];
     tc::tc_fence_after();
