@@ -227,39 +227,72 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
     return true;
   };
 
-  if (N > 0 && (!issue_g1(0) || !issue_wt(0))) goto fail;
-  for (int n = 0; n < N; ++n) {
-    // (a) U + MMA1 of item n: D1 = [T diag(beta); 0] V ; D1 += [-W ; Q'] S16
-    if (!wait_bar(&sh->bar[PREP_DONE], n & 1, abort)) goto fail;
-    if (!wait_bar(&sh->bar[S16_READY], n & 1, abort)) goto fail;
-    if (!wait_bar(&sh->bar[AW_READY], n & 1, abort)) goto fail;
-    tc::tc_fence_after();
-    for (int ks = 0; ks < 4; ++ks)
-      tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + ks * 32, 16, 1024),
-                  tc::sdesc(sbase + OFF_V + ks * 2048, 8192, 1024), ID_U, ks > 0);
-    for (int ks = 0; ks < 8; ++ks)
-      tc::mma_f16(mD1, tc::sdesc(sbase + OFF_AW + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
-                  tc::sdesc(sbase + OFF_SB + ks * 2048, 16384, 1024), ID_U, 1);
-    tc::mma_commit(&sh->bar[M1_DONE]);
-    tc::mma_commit(&sh->bar[V_EMPTY]);
-    // (b) G1 of item n+1 (its prep overlaps this item's recurrence)
-    if (n + 1 < N && !issue_g1(n + 1)) goto fail;
-    // (c) state update + output of item n: S += K^T VS ; D1 += [0 ; P] VN
-    if (!wait_bar(&sh->bar[VN_READY], n & 1, abort)) goto fail;
-    tc::tc_fence_after();
-    {
-      const uint32_t k = sbase + OFF_QK + (n & 1) * 32768 + 8192;
-      for (int ks = 0; ks < 4; ++ks)
-        tc::mma_f16(mS, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_VS + ks * 2048, 8192, 1024),
-                    ID_2A, 1);
-      for (int ks = 0; ks < 4; ++ks)
-        tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + 8192 + ks * 32, 16, 1024),
-                    tc::sdesc(sbase + OFF_VN + ks * 2048, 8192, 1024), ID_U, 1);
+  {
+    // Greedy issue: each of the four MMA queues stays in item order, and
+    // whichever queue's next group is ready goes first, so the prep of item
+    // n+1 (G1, W^T) is not held behind the recurrence of item n.
+    int g1 = 0, wt = 0, um = 0, m2 = 0;
+    uint32_t idle = 0;
+    while (m2 < N) {
+      bool progressed = false;
+      if (m2 < um && tc::mbar_try_wait(&sh->bar[VN_READY], m2 & 1)) {
+        // state update + output of item m2: S += K^T VS ; D1 += [0 ; P] VN
+        tc::tc_fence_after();
+        const uint32_t k = sbase + OFF_QK + (m2 & 1) * 32768 + 8192;
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_f16(mS, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_VS + ks * 2048, 8192, 1024),
+                      ID_2A, 1);
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + 8192 + ks * 32, 16, 1024),
+                      tc::sdesc(sbase + OFF_VN + ks * 2048, 8192, 1024), ID_U, 1);
+        tc::mma_commit(&sh->bar[M2_DONE]);
+        tc::mma_commit(&sh->bar[QK_EMPTY0 + (m2 & 1)]);
+        ++m2;
+        progressed = true;
+      }
+      if (um < wt && um == m2 && tc::mbar_try_wait(&sh->bar[PREP_DONE], um & 1) &&
+          tc::mbar_try_wait(&sh->bar[S16_READY], um & 1) && tc::mbar_try_wait(&sh->bar[AW_READY], um & 1)) {
+        // U + MMA1 of item um: D1 = [T diag(beta); 0] V ; D1 += [-W ; Q'] S16
+        tc::tc_fence_after();
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + ks * 32, 16, 1024),
+                      tc::sdesc(sbase + OFF_V + ks * 2048, 8192, 1024), ID_U, ks > 0);
+        for (int ks = 0; ks < 8; ++ks)
+          tc::mma_f16(mD1, tc::sdesc(sbase + OFF_AW + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
+                      tc::sdesc(sbase + OFF_SB + ks * 2048, 16384, 1024), ID_U, 1);
+        tc::mma_commit(&sh->bar[M1_DONE]);
+        tc::mma_commit(&sh->bar[V_EMPTY]);
+        ++um;
+        progressed = true;
+      }
+      if (wt < g1 && tc::mbar_try_wait(&sh->bar[TBE_READY], wt & 1)) {
+        tc::tc_fence_after();
+        const uint32_t k = sbase + OFF_QK + (wt & 1) * 32768 + 8192;
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_f16(mWT, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_TBE + ks * 32, 16, 1024),
+                      ID_WT, ks > 0);
+        tc::mma_commit(&sh->bar[WT_DONE]);
+        ++wt;
+        progressed = true;
+      }
+      if (g1 < N && g1 <= m2 + 1 && tc::mbar_try_wait(&sh->bar[PREP_A], g1 & 1)) {
+        tc::tc_fence_after();
+        const uint32_t qk = sbase + OFF_QK + (g1 & 1) * 32768;
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
+          tc::mma_f16(mG1, tc::sdesc(qk + koff, 16, 1024), tc::sdesc(qk + 8192 + koff, 16, 1024), ID_G1, ks > 0);
+        }
+        tc::mma_commit(&sh->bar[G1_DONE]);
+        ++g1;
+        progressed = true;
+      }
+      if (progressed) {
+        idle = 0;
+      } else {
+        if (++idle > kWaitLimit || *abort) goto fail;
+        if (idle > 4) __nanosleep(idle < 64 ? 20 : 100);
+      }
     }
-    tc::mma_commit(&sh->bar[M2_DONE]);
-    tc::mma_commit(&sh->bar[QK_EMPTY0 + (n & 1)]);
-    // (d) W^T of item n+1
-    if (n + 1 < N && !issue_wt(n + 1)) goto fail;
   }
   return;
 fail:
