@@ -64,7 +64,7 @@ constexpr int SMALL_BYTES = 4096;
 constexpr int SMEM_BYTES = OFF_SMALL + SMALL_BYTES + 1024;
 
 enum Bar {
-  QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE, TBE_READY, WT_DONE,
+  QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE0, G1_DONE1, TBE_READY, WT_DONE,
   PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, AW_READY, GC_READY0, GC_READY1, DRAIN, NUM_BARS
 };
 
@@ -197,7 +197,8 @@ template <bool kBf16>
 __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err) {
   volatile int* abort = &sh->abort;
   const uint32_t sbase = tc::smem_u32(sm);
-  const uint32_t mS = tb, mD1 = tb + 128, mG1 = tb + 256, mWT = tb + 320;
+  // TMEM: S [0,128), D1 [128,256), G1 x2 [256,384), W^T [384,448)
+  const uint32_t mS = tb, mD1 = tb + 128, mG1 = tb + 256, mWT = tb + 384;
   // G1 reads the raw input tiles (bf16 or fp16); every other product is fp16
   constexpr uint32_t ID_G1 = tc::idesc_f16(128, 64, false, false) | (kBf16 ? (1u << 7) | (1u << 10) : 0u);
   constexpr uint32_t ID_U = tc::idesc_f16(128, 128, false, true);
@@ -205,33 +206,11 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
   constexpr uint32_t ID_2A = tc::idesc_f16(128, 128, true, true);
   const int N = it.count();
 
-  auto issue_g1 = [&](int n) -> bool {
-    if (!wait_bar(&sh->bar[PREP_A], n & 1, abort)) return false;
-    tc::tc_fence_after();
-    const uint32_t qk = sbase + OFF_QK + (n & 1) * 32768;
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
-      tc::mma_f16(mG1, tc::sdesc(qk + koff, 16, 1024), tc::sdesc(qk + 8192 + koff, 16, 1024), ID_G1, ks > 0);
-    }
-    tc::mma_commit(&sh->bar[G1_DONE]);
-    return true;
-  };
-  auto issue_wt = [&](int n) -> bool {
-    if (!wait_bar(&sh->bar[TBE_READY], n & 1, abort)) return false;
-    tc::tc_fence_after();
-    const uint32_t k = sbase + OFF_QK + (n & 1) * 32768 + 8192;
-    for (int ks = 0; ks < 4; ++ks)
-      tc::mma_f16(mWT, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_TBE + ks * 32, 16, 1024),
-                  ID_WT, ks > 0);
-    tc::mma_commit(&sh->bar[WT_DONE]);
-    return true;
-  };
-
   {
     // Greedy issue: each of the four MMA queues stays in item order, and
     // whichever queue's next group is ready goes first, so the prep of item
     // n+1 (G1, W^T) is not held behind the recurrence of item n.
-    int g1 = 0, wt = 0, um = 0, m2 = 0;
+    int g1 = 0, wt = 0, um = 0, m2 = 0, pa = 0;
     uint32_t idle = 0;
     while (m2 < N) {
       bool progressed = false;
@@ -275,14 +254,21 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
         ++wt;
         progressed = true;
       }
-      if (g1 < N && g1 <= m2 + 1 && tc::mbar_try_wait(&sh->bar[PREP_A], g1 & 1)) {
+      // prep has started item pa-1 (so it is done reading G1 of item pa-2)
+      if (pa < N && tc::mbar_try_wait(&sh->bar[PREP_A], pa & 1)) {
+        ++pa;
+        progressed = true;
+      }
+      // G1 straight from the landed q/k tile, into the TMEM buffer of g1 & 1
+      if (g1 < N && (g1 < 2 || pa >= g1 - 1) && tc::mbar_try_wait(&sh->bar[QK_FULL0 + (g1 & 1)], (g1 >> 1) & 1)) {
         tc::tc_fence_after();
         const uint32_t qk = sbase + OFF_QK + (g1 & 1) * 32768;
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
-          tc::mma_f16(mG1, tc::sdesc(qk + koff, 16, 1024), tc::sdesc(qk + 8192 + koff, 16, 1024), ID_G1, ks > 0);
+          tc::mma_f16(mG1 + (g1 & 1) * 64, tc::sdesc(qk + koff, 16, 1024), tc::sdesc(qk + 8192 + koff, 16, 1024),
+                      ID_G1, ks > 0);
         }
-        tc::mma_commit(&sh->bar[G1_DONE]);
+        tc::mma_commit(&sh->bar[G1_DONE0 + (g1 & 1)]);
         ++g1;
         progressed = true;
       }
@@ -326,7 +312,7 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
   volatile int* abort = &sh->abort;
   const int t = threadIdx.x, l = t & 127, hf = t >> 7;
   const uint32_t lane_base = (uint32_t)((l >> 5) * 32) << 16;
-  const uint32_t tG1 = tb + 256 + lane_base + hf * 32;
+  const uint32_t tG1 = tb + 256 + lane_base + hf * 32;  // + (n & 1) * 64: double buffer
   float* NM = reinterpret_cast<float*>(sm + OFF_NM);
   float* TM = reinterpret_cast<float*>(sm + OFF_TM);
   float* YM = reinterpret_cast<float*>(sm + OFF_YM);
@@ -410,11 +396,11 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
           dec[4 * q + k] = keep ? f * ex2(gi - gj[k]) : 0.f;
         }
       }
-      if (!wait_all(G1_DONE, n & 1)) break;
+      if (!wait_all(G1_DONE0 + (n & 1), (n >> 1) & 1)) break;
       PROF_MARK(0, 3);
       tc::tc_fence_after();
       float a[32];
-      tc::tmem_ld32(tG1, a);
+      tc::tmem_ld32(tG1 + (n & 1) * 64, a);
       if (l < C) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -520,7 +506,7 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
   volatile int* abort = &sh->abort;
   const int rt = threadIdx.x - kRecBase;
   const uint32_t lane_base = (uint32_t)((rt >> 5) * 32) << 16;
-  const uint32_t tS = tb + lane_base, tD1 = tb + 128 + lane_base, tWT = tb + 320 + lane_base;
+  const uint32_t tS = tb + lane_base, tD1 = tb + 128 + lane_base, tWT = tb + 384 + lane_base;
   int N = it.count();
   auto sync = [] { group_sync(BAR_REC, 128); };
   auto wait_all = [&](int b, uint32_t parity) -> bool {
