@@ -168,22 +168,35 @@ __device__ void tma_role(uint8_t* sm, Small* sh, const CUtensorMap* mq, const CU
                          const CUtensorMap* mv, Items it, int* err) {
   volatile int* abort = &sh->abort;
   const int N = it.count();
-  int nv = 0;  // next item whose V is to be loaded
-  for (int n = 0; n < N; ++n) {
-    const int s = n & 1, p = it.pair(n), c = it.chunk(n);
-    if (!wait_bar(&sh->bar[QK_EMPTY0 + s], ((n >> 1) & 1) ^ 1, abort)) goto fail;
-    tc::mbar_arrive_expect_tx(&sh->bar[QK_FULL0 + s], 4 * 64 * 64 * 2);
-    for (int h = 0; h < 2; ++h) {
-      uint8_t* base = sm + OFF_QK + s * 32768 + h * 16384;
-      tc::tma_load_3d(base, mq, &sh->bar[QK_FULL0 + s], h * 64, c * C, p);
-      tc::tma_load_3d(base + 8192, mk, &sh->bar[QK_FULL0 + s], h * 64, c * C, p);
+  // Greedy: the q/k ring and the single V buffer are refilled independently,
+  // each in item order, as soon as their consumers release them.
+  int nq = 0, nv = 0;
+  uint32_t idle = 0;
+  while (nq < N || nv < N) {
+    bool progressed = false;
+    if (nq < N && tc::mbar_try_wait(&sh->bar[QK_EMPTY0 + (nq & 1)], ((nq >> 1) & 1) ^ 1)) {
+      const int s = nq & 1, p = it.pair(nq), c = it.chunk(nq);
+      tc::mbar_arrive_expect_tx(&sh->bar[QK_FULL0 + s], 4 * 64 * 64 * 2);
+      for (int h = 0; h < 2; ++h) {
+        uint8_t* base = sm + OFF_QK + s * 32768 + h * 16384;
+        tc::tma_load_3d(base, mq, &sh->bar[QK_FULL0 + s], h * 64, c * C, p);
+        tc::tma_load_3d(base + 8192, mk, &sh->bar[QK_FULL0 + s], h * 64, c * C, p);
+      }
+      ++nq;
+      progressed = true;
     }
-    // V of the oldest item whose U product has released the single V buffer
-    for (; nv <= n; ++nv) {
-      if (!wait_bar(&sh->bar[V_EMPTY], (nv & 1) ^ 1, abort)) goto fail;
+    if (nv < N && tc::mbar_try_wait(&sh->bar[V_EMPTY], (nv & 1) ^ 1)) {
       tc::mbar_arrive_expect_tx(&sh->bar[V_FULL], 2 * 64 * 64 * 2);
       for (int h = 0; h < 2; ++h)
         tc::tma_load_3d(sm + OFF_V + h * 8192, mv, &sh->bar[V_FULL], h * 64, it.chunk(nv) * C, it.pair(nv));
+      ++nv;
+      progressed = true;
+    }
+    if (progressed) {
+      idle = 0;
+    } else {
+      if (++idle > kWaitLimit || *abort) goto fail;
+      if (idle > 4) __nanosleep(idle < 64 ? 20 : 100);
     }
   }
   return;
