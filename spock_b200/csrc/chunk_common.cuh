@@ -161,6 +161,107 @@ __device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ 
   solve_level<kNT, 3>(N, T, Y, t, sync);
 }
 
+// ---- 3xTF32 warp tiles (mma.sync m16n8k8) for the blocked inverse ----------
+// Each fp32 operand x is split as hi = tf32(x), lo = tf32(x - hi); the three
+// products lo*hi + hi*lo + hi*hi keep about 21 bits of every product, which is
+// ample next to the fp16 operands the chunk products use afterwards.
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_rna(x);
+  lo = tf32_rna(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// D(16x8, stride ldd) = A(16 x 8kSteps, stride lda) * B(8kSteps x 8, stride ldb), one warp.
+// Fragments (g = lane/4, q = lane%4): A (g|g+8, q|q+4), B (q|q+4, g), C (g|g+8, 2q|2q+1).
+template <int kSteps>
+__device__ __forceinline__ void tile16x8_3xtf32(const float* __restrict__ A, int lda, const float* __restrict__ B,
+                                                int ldb, float* __restrict__ Dst, int ldd) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  float c[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // hi*hi | correction terms
+#pragma unroll
+  for (int s = 0; s < kSteps; ++s) {
+    const float* a = A + s * 8;
+    const float* b = B + s * 8 * ldb;
+    uint32_t ah[4], al[4], bh0, bl0, bh1, bl1;
+    split_tf32(a[g * lda + q], ah[0], al[0]);
+    split_tf32(a[(g + 8) * lda + q], ah[1], al[1]);
+    split_tf32(a[g * lda + q + 4], ah[2], al[2]);
+    split_tf32(a[(g + 8) * lda + q + 4], ah[3], al[3]);
+    split_tf32(b[q * ldb + g], bh0, bl0);
+    split_tf32(b[(q + 4) * ldb + g], bh1, bl1);
+    mma_tf32(e, al, bh0, bh1);
+    mma_tf32(e, ah, bl0, bl1);
+    mma_tf32(c, ah, bh0, bh1);
+  }
+  *reinterpret_cast<float2*>(Dst + g * ldd + 2 * q) = make_float2(c[0] + e[0], c[1] + e[1]);
+  *reinterpret_cast<float2*>(Dst + (g + 8) * ldd + 2 * q) = make_float2(c[2] + e[2], c[3] + e[3]);
+}
+
+// T = (I - N)^-1 for 8 warps (256 threads) in five barrier-separated phases:
+//   1. the four 16x16 diagonal blocks by forward substitution, four threads
+//      per column (rows rg, rg+4, rg+8, rg+12); once x_m is final its owner
+//      broadcasts it with a 4-wide shuffle and every later row takes one FMA
+//      (the same FMA order as a scalar column solve);
+//   2/3. T10 = T11 (N10 T00) and T32 = T33 (N32 T22), which completes the two
+//      32x32 diagonal inverses A^-1 = T[0:32,0:32] and B^-1 = T[32:64,32:64];
+//   4/5. T[32:64,0:32] = B^-1 (N[32:64,0:32] A^-1).
+// Phases 2-5 are 16x8 warp tiles on the tensor cores (3xTF32).
+// N and T: row stride LDT (N's strictly lower part is read). The strictly
+// upper blocks T[0:16,16:32] and T[32:48,48:64] must hold zeros (nothing here
+// writes them). Y: 32 x kLDY floats of scratch.
+constexpr int kLDY = 40;
+template <class Sync>
+__device__ __forceinline__ void solve_unit_lower_blk(const float* __restrict__ N, float* __restrict__ T,
+                                                     float* __restrict__ Y, int t, Sync sync) {
+  {
+    const int o = (t >> 6) * 16, j = (t >> 2) & 15, rg = t & 3;
+    const float* nb = N + (o + rg) * LDT + o;
+    float x[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] = (rg + 4 * k == j) ? 1.f : 0.f;
+#pragma unroll
+    for (int m = 0; m < 15; ++m) {
+      const float xm = __shfl_sync(0xffffffffu, x[m >> 2], m & 3, 4);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (4 * k + 3 > m && rg + 4 * k > m) x[k] = fmaf(nb[4 * k * LDT + m], xm, x[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) T[(o + rg + 4 * k) * LDT + o + j] = x[k];
+  }
+  sync();
+  const int w = t >> 5;
+  if (w < 4) {  // Y_b = N_{ib,jb} T_jj  (b = w/2: (ib,jb) = (1,0) | (3,2); column half w&1)
+    const int jb = 2 * (w >> 1), ib = jb + 1, n8 = (w & 1) * 8;
+    tile16x8_3xtf32<2>(N + 16 * ib * LDT + 16 * jb, LDT, T + 16 * jb * LDT + 16 * jb + n8, LDT,
+                       Y + (w >> 1) * 16 + n8, kLDY);
+  }
+  sync();
+  if (w < 4) {  // T_{ib,jb} = T_ii Y_b
+    const int jb = 2 * (w >> 1), ib = jb + 1, n8 = (w & 1) * 8;
+    tile16x8_3xtf32<2>(T + 16 * ib * LDT + 16 * ib, LDT, Y + (w >> 1) * 16 + n8, kLDY,
+                       T + 16 * ib * LDT + 16 * jb + n8, LDT);
+  }
+  sync();
+  const int mi = w >> 2, n8 = (w & 3) * 8;
+  // X = N[32:64,0:32] A^-1
+  tile16x8_3xtf32<4>(N + (32 + 16 * mi) * LDT, LDT, T + n8, LDT, Y + 16 * mi * kLDY + n8, kLDY);
+  sync();
+  // T[32:64,0:32] = B^-1 X
+  tile16x8_3xtf32<4>(T + (32 + 16 * mi) * LDT + 32, LDT, Y + n8, kLDY, T + (32 + 16 * mi) * LDT + n8, LDT);
+  sync();
+}
+
 // ---- warp-level 16x16 products for the triangular inverse --------------------
 // mma.sync m16n8k16 (fp16 in, fp32 accumulate) with every fp32 operand split
 // as hi + lo fp16 and three products (hi*hi + hi*lo + lo*hi), which keeps the

@@ -34,7 +34,6 @@ namespace {
 
 using chunk::C;
 using chunk::D;
-using chunk::LDN;
 using chunk::pack8;
 using chunk::pack_h2;
 using chunk::store_row32;
@@ -57,11 +56,12 @@ constexpr int OFF_SB = 144 * 1024;           // S16 MN-major [kd][v]; later VN |
 constexpr int OFF_VN = OFF_SB;
 constexpr int OFF_VS = OFF_SB + 16 * 1024;
 constexpr int OFF_NM = 176 * 1024;
-constexpr int OFF_TM = OFF_NM + 16896;          // N: 64 x 65 fp32 (16640 B), padded to 16 B
-constexpr int OFF_YM = OFF_TM + C * chunk::LDT * 4;
-constexpr int OFF_SMALL = OFF_YM + 4 * 256 * 4;
+constexpr int OFF_TM = OFF_NM + C * chunk::LDT * 4;  // N and T: 64 x LDT fp32
+constexpr int OFF_YM = OFF_TM + C * chunk::LDT * 4;  // solve scratch: 32 x kLDY fp32
+constexpr int OFF_SMALL = OFF_YM + 32 * chunk::kLDY * 4;
 constexpr int SMALL_BYTES = 4096;
 constexpr int SMEM_BYTES = OFF_SMALL + SMALL_BYTES + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 
 enum Bar {
   QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE0, G1_DONE1, TBE_READY, WT_DONE,
@@ -348,6 +348,10 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     cp_async_commit();
   };
   prefetch_gb(0);
+  // the solve reads the strictly upper blocks T[0:16,16:32] and T[32:48,48:64]
+  // as zeros and never writes them
+  for (int i = t; i < C * chunk::LDT; i += kPrepThreads) TM[i] = 0.f;
+  sync();
 
   PROF_DECL
   for (int n = 0; n < N; ++n) {
@@ -425,7 +429,9 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
       } else {
         const int i = l - C;
 #pragma unroll
-        for (int k = 0; k < 32; ++k) NM[i * LDN + j0 + k] = a[k] * dec[k];
+        for (int k = 0; k < 32; k += 4)
+          *reinterpret_cast<float4*>(NM + i * chunk::LDT + j0 + k) =
+              make_float4(a[k] * dec[k], a[k + 1] * dec[k + 1], a[k + 2] * dec[k + 2], a[k + 3] * dec[k + 3]);
       }
     }
     if constexpr (kBf16) {  // K -> fp16 in place (G1, the only bf16 reader, is done)
@@ -447,10 +453,10 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
         PROF_MARK(0, kk);
         ++kk;
       };
-      chunk::solve_unit_lower_fast<kPrepThreads>(NM, TM, YM, t, sync_prof);
+      chunk::solve_unit_lower_blk(NM, TM, YM, t, sync_prof);
     }
 #else
-    chunk::solve_unit_lower_fast<kPrepThreads>(NM, TM, YM, t, sync);
+    chunk::solve_unit_lower_blk(NM, TM, YM, t, sync);
 #endif
     PROF_MARK(0, 5);
     // 5. T diag(beta e^gc) -> TBE (for W^T) once W^T of the previous item has
