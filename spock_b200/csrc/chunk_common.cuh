@@ -77,89 +77,10 @@ __device__ __forceinline__ void solve_unit_lower(const float* __restrict__ N, fl
   }
 }
 
-// Same inverse, register-blocked for kNT threads: T has row stride
-// LDT (16-byte aligned rows), every off-diagonal product is computed as 1x4
-// output tiles with fully unrolled 16-wide k loops (independent FMAs, float4
-// loads of T), so the solve is throughput- rather than latency-bound.
+// Row stride of the fp32 N and T matrices of the pipelined kernel (16-byte
+// aligned rows for float4 access; 68 = 4 mod 32 keeps the mma fragment loads
+// of consecutive rows on distinct banks).
 constexpr int LDT = 68;
-
-template <int kNT, int kD, class Sync>
-__device__ __forceinline__ void solve_level(const float* __restrict__ N, float* __restrict__ T,
-                                            float* __restrict__ Y, int t, Sync sync) {
-  constexpr int nb = 4 - kD;
-  // Partial products, split over the kD source blocks so every thread runs at
-  // most one 16-step chain:  Y[jb][kb] = N_{ib, jb+kb} T_{jb+kb, jb}   (ib = jb + kD)
-  for (int e = t; e < nb * kD * 64; e += kNT) {
-    const int jb = e / (kD * 64), rem = e % (kD * 64), kb = rem >> 6;
-    const int r = (rem >> 2) & 15, c0 = (rem & 3) * 4, ib = jb + kD, col0 = 16 * (jb + kb);
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    const float* nrow = N + (16 * ib + r) * LDN + col0;
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const float nv = nrow[m];
-      const float4 tv = *reinterpret_cast<const float4*>(T + (col0 + m) * LDT + 16 * jb + c0);
-      a0 = fmaf(nv, tv.x, a0);
-      a1 = fmaf(nv, tv.y, a1);
-      a2 = fmaf(nv, tv.z, a2);
-      a3 = fmaf(nv, tv.w, a3);
-    }
-    *reinterpret_cast<float4*>(Y + (jb * kD + kb) * 256 + r * 16 + c0) = make_float4(a0, a1, a2, a3);
-  }
-  sync();
-  // T_ij = T_ii sum_kb Y[jb][kb]  (T_ii lower triangular, zeros above its diagonal)
-  for (int e = t; e < nb * 64; e += kNT) {
-    const int jb = e >> 6, r = (e >> 2) & 15, c0 = (e & 3) * 4, ib = jb + kD;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    const float* trow = T + (16 * ib + r) * LDT + 16 * ib;
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const float tv = trow[m];
-      float4 y = *reinterpret_cast<const float4*>(Y + (jb * kD) * 256 + m * 16 + c0);
-#pragma unroll
-      for (int kb = 1; kb < kD; ++kb) {
-        const float4 z = *reinterpret_cast<const float4*>(Y + (jb * kD + kb) * 256 + m * 16 + c0);
-        y.x += z.x;
-        y.y += z.y;
-        y.z += z.z;
-        y.w += z.w;
-      }
-      a0 = fmaf(tv, y.x, a0);
-      a1 = fmaf(tv, y.y, a1);
-      a2 = fmaf(tv, y.z, a2);
-      a3 = fmaf(tv, y.w, a3);
-    }
-    *reinterpret_cast<float4*>(T + (16 * ib + r) * LDT + 16 * jb + c0) = make_float4(a0, a1, a2, a3);
-  }
-  sync();
-}
-
-// N: row stride LDN; T: row stride LDT (only the lower triangle incl. the
-// diagonal is written; callers mask j > i); Y: 1024 floats, 16-byte aligned.
-// Diagonal 16x16 blocks by right-looking substitution: once x_m is final it
-// updates every later row at once (15 independent FMAs per step, not a chain).
-template <int kNT, class Sync>
-__device__ __forceinline__ void solve_unit_lower_fast(const float* __restrict__ N, float* __restrict__ T,
-                                                      float* __restrict__ Y, int t, Sync sync) {
-  // diagonal block w on warp w (lanes 0..15 = its columns): no bank conflict
-  // between blocks, four schedulers busy
-  if ((t >> 5) < 4 && (t & 31) < 16) {
-    const int o = (t >> 5) * 16, j = t & 15;
-    float x[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = (i == j) ? 1.f : 0.f;
-#pragma unroll
-    for (int m = 0; m < 15; ++m) {
-#pragma unroll
-      for (int i = m + 1; i < 16; ++i) x[i] = fmaf(N[(o + i) * LDN + o + m], x[m], x[i]);
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) T[(o + i) * LDT + o + j] = (i < j) ? 0.f : x[i];
-  }
-  sync();
-  solve_level<kNT, 1>(N, T, Y, t, sync);
-  solve_level<kNT, 2>(N, T, Y, t, sync);
-  solve_level<kNT, 3>(N, T, Y, t, sync);
-}
 
 // ---- 3xTF32 warp tiles (mma.sync m16n8k8) for the blocked inverse ----------
 // Each fp32 operand x is split as hi = tf32(x), lo = tf32(x - hi); the three
@@ -208,10 +129,9 @@ __device__ __forceinline__ void tile16x8_3xtf32(const float* __restrict__ A, int
 }
 
 // T = (I - N)^-1 for 8 warps (256 threads) in five barrier-separated phases:
-//   1. the four 16x16 diagonal blocks by forward substitution, four threads
-//      per column (rows rg, rg+4, rg+8, rg+12); once x_m is final its owner
-//      broadcasts it with a 4-wide shuffle and every later row takes one FMA
-//      (the same FMA order as a scalar column solve);
+//   1. the four 16x16 diagonal blocks by forward substitution, one thread per
+//      column (warps 0-1): once x_m is final it updates every later row, so
+//      the dependent chain is 15 FMAs and the loads of N run ahead of it;
 //   2/3. T10 = T11 (N10 T00) and T32 = T33 (N32 T22), which completes the two
 //      32x32 diagonal inverses A^-1 = T[0:32,0:32] and B^-1 = T[32:64,32:64];
 //   4/5. T[32:64,0:32] = B^-1 (N[32:64,0:32] A^-1).
@@ -223,21 +143,22 @@ constexpr int kLDY = 40;
 template <class Sync>
 __device__ __forceinline__ void solve_unit_lower_blk(const float* __restrict__ N, float* __restrict__ T,
                                                      float* __restrict__ Y, int t, Sync sync) {
-  {
-    const int o = (t >> 6) * 16, j = (t >> 2) & 15, rg = t & 3;
-    const float* nb = N + (o + rg) * LDT + o;
-    float x[4];
+  if (t < 64) {
+    const int o = (t >> 4) * 16, j = t & 15;
+    const float* nb = N + o * LDT + o;
+    float x[16];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) x[k] = (rg + 4 * k == j) ? 1.f : 0.f;
+    for (int i = 0; i < 16; ++i) x[i] = (i == j) ? 1.f : 0.f;
 #pragma unroll
     for (int m = 0; m < 15; ++m) {
-      const float xm = __shfl_sync(0xffffffffu, x[m >> 2], m & 3, 4);
+      float c[16];
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (4 * k + 3 > m && rg + 4 * k > m) x[k] = fmaf(nb[4 * k * LDT + m], xm, x[k]);
+      for (int i = m + 1; i < 16; ++i) c[i] = nb[i * LDT + m];
+#pragma unroll
+      for (int i = m + 1; i < 16; ++i) x[i] = fmaf(c[i], x[m], x[i]);
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) T[(o + rg + 4 * k) * LDT + o + j] = x[k];
+    for (int i = 0; i < 16; ++i) T[(o + i) * LDT + o + j] = x[i];
   }
   sync();
   const int w = t >> 5;
@@ -260,133 +181,6 @@ __device__ __forceinline__ void solve_unit_lower_blk(const float* __restrict__ N
   // T[32:64,0:32] = B^-1 X
   tile16x8_3xtf32<4>(T + (32 + 16 * mi) * LDT + 32, LDT, Y + n8, kLDY, T + (32 + 16 * mi) * LDT + n8, LDT);
   sync();
-}
-
-// ---- warp-level 16x16 products for the triangular inverse --------------------
-// mma.sync m16n8k16 (fp16 in, fp32 accumulate) with every fp32 operand split
-// as hi + lo fp16 and three products (hi*hi + hi*lo + lo*hi), which keeps the
-// result close to fp32 accuracy. Fragment layouts of m16n8k16 (g = lane/4,
-// q = lane%4): A rows g, g+8 x cols 2q, 2q+1, 2q+8, 2q+9; B rows 2q, 2q+1,
-// 2q+8, 2q+9 x col g; C rows g, g+8 x cols 2q, 2q+1.
-__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  const __half2 h = __floats2half2_rn(x0, x1);
-  const float2 hf = __half22float2(h);
-  const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
-  hi = *reinterpret_cast<const uint32_t*>(&h);
-  lo = *reinterpret_cast<const uint32_t*>(&l);
-}
-
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// c[nt][.] += A(16x16, stride lda) * B(16x16, stride ldb), both fp32 in shared memory.
-__device__ __forceinline__ void mm16_acc(const float* __restrict__ A, int lda, const float* __restrict__ B,
-                                         int ldb, float (&c)[2][4]) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-  uint32_t ah[4], al[4];
-  split2(A[g * lda + 2 * q], A[g * lda + 2 * q + 1], ah[0], al[0]);
-  split2(A[(g + 8) * lda + 2 * q], A[(g + 8) * lda + 2 * q + 1], ah[1], al[1]);
-  split2(A[g * lda + 2 * q + 8], A[g * lda + 2 * q + 9], ah[2], al[2]);
-  split2(A[(g + 8) * lda + 2 * q + 8], A[(g + 8) * lda + 2 * q + 9], ah[3], al[3]);
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    const int col = nt * 8 + g;
-    uint32_t bh0, bl0, bh1, bl1;
-    split2(B[(2 * q) * ldb + col], B[(2 * q + 1) * ldb + col], bh0, bl0);
-    split2(B[(2 * q + 8) * ldb + col], B[(2 * q + 9) * ldb + col], bh1, bl1);
-    mma16816(c[nt], ah, bh0, bh1);
-    mma16816(c[nt], ah, bl0, bl1);
-    mma16816(c[nt], al, bh0, bh1);
-  }
-}
-
-__device__ __forceinline__ void frag_zero(float (&c)[2][4]) {
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) c[nt][k] = 0.f;
-}
-
-// D(16x16, stride ldd) = c (+ D when add).
-__device__ __forceinline__ void frag_store(float* D, int ldd, const float (&c)[2][4], bool add) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    const int col = nt * 8 + 2 * q;
-    float* r0 = D + g * ldd + col;
-    float* r1 = D + (g + 8) * ldd + col;
-    if (add) {
-      r0[0] += c[nt][0];
-      r0[1] += c[nt][1];
-      r1[0] += c[nt][2];
-      r1[1] += c[nt][3];
-    } else {
-      r0[0] = c[nt][0];
-      r0[1] = c[nt][1];
-      r1[0] = c[nt][2];
-      r1[1] = c[nt][3];
-    }
-  }
-}
-
-// T = (I - N)^-1 on tensor cores. Warp w < 4 inverts diagonal block w as
-// (I+N)(I+N^2)(I+N^4)(I+N^8) (N_ww^16 = 0); then block diagonals d = 1..3,
-// one warp per block: T_ij = T_ii * sum_k N_ik T_kj. Y: 4 x 256 fp32 scratch
-// (one 16x16 per warp). `sync()` synchronises all participating warps.
-template <class Sync>
-__device__ __forceinline__ void solve_unit_lower_tc(const float* __restrict__ N, float* __restrict__ T,
-                                                    float* __restrict__ Y, int warp, Sync sync) {
-  const int lane = threadIdx.x & 31;
-  if (warp < 4) {
-    const int o = warp * 16;
-    float* Tb = T + o * LDT + o;
-    const float* Nb = N + o * LDN + o;
-    float* Pw = Y + warp * 256;  // powers of N_ww, stride 16
-    for (int e = lane; e < 256; e += 32) {
-      const int i = e >> 4, j = e & 15;
-      const float nv = Nb[i * LDN + j];
-      Tb[i * LDT + j] = (i == j ? 1.f : 0.f) + nv;  // R = I + N
-      Pw[e] = nv;
-    }
-    __syncwarp();
-#pragma unroll 1
-    for (int step = 0; step < 3; ++step) {
-      float c[2][4];
-      frag_zero(c);
-      mm16_acc(Pw, 16, Pw, 16, c);  // P <- P^2   (N^2, N^4, N^8)
-      __syncwarp();
-      frag_store(Pw, 16, c, false);
-      __syncwarp();
-      frag_zero(c);
-      mm16_acc(Tb, LDT, Pw, 16, c);  // R <- R + R P
-      __syncwarp();
-      frag_store(Tb, LDT, c, true);
-      __syncwarp();
-    }
-  }
-  sync();
-#pragma unroll 1
-  for (int d = 1; d < 4; ++d) {
-    if (warp < 4 - d) {
-      const int jb = warp, ib = jb + d;
-      float c[2][4];
-      frag_zero(c);
-      for (int kb = 0; kb < d; ++kb)
-        mm16_acc(N + (16 * ib) * LDN + 16 * (jb + kb), LDN, T + (16 * (jb + kb)) * LDT + 16 * jb, LDT, c);
-      float* Yw = Y + warp * 256;
-      frag_store(Yw, 16, c, false);
-      __syncwarp();
-      frag_zero(c);
-      mm16_acc(T + (16 * ib) * LDT + 16 * ib, LDT, Yw, 16, c);
-      frag_store(T + (16 * ib) * LDT + 16 * jb, LDT, c, false);
-    }
-    sync();
-  }
 }
 
 template <int kOut>

@@ -114,12 +114,12 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // Bounded wait that also gives up early once another role has aborted.
-// Polls back off with __nanosleep so waiting warps do not take issue slots
-// from the warps they wait for (they share the SM's schedulers).
+// mbarrier.try_wait suspends the thread in hardware until the phase completes
+// or a short time limit passes, so the loop neither spins hot nor oversleeps.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (*abort) return false;
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (tc::mbar_try_wait(bar, parity)) return true;
-    if (i >= 4) __nanosleep(i < 64 ? 32 : 128);
     if ((i & 255u) == 255u && *abort) return false;
   }
   return false;
@@ -143,7 +143,15 @@ __device__ unsigned long long g_phase_prof[148 * 4 * 32];
     if ((threadIdx.x & 127) == 0 && blockIdx.x < 148)                           \
       for (int _k = 0; _k < 32; ++_k) g_phase_prof[(blockIdx.x * 4 + (role)) * 32 + _k] += _acc[_k]; \
   } while (0)
+__device__ long long g_trace[64 * 32];
+#define TRACE(ev, n)                                                                 \
+  do {                                                                               \
+    if (blockIdx.x == 0 && (n) < 64) g_trace[(n) * 32 + (ev)] = clock64();           \
+  } while (0)
 #else
+#define TRACE(ev, n) \
+  do {               \
+  } while (0)
 #define PROF_DECL
 #define PROF_MARK(role, k) \
   do {                     \
@@ -174,7 +182,7 @@ __device__ void tma_role(uint8_t* sm, Small* sh, const CUtensorMap* mq, const CU
   uint32_t idle = 0;
   while (nq < N || nv < N) {
     bool progressed = false;
-    if (nq < N && tc::mbar_try_wait(&sh->bar[QK_EMPTY0 + (nq & 1)], ((nq >> 1) & 1) ^ 1)) {
+    if (nq < N && tc::mbar_test_wait(&sh->bar[QK_EMPTY0 + (nq & 1)], ((nq >> 1) & 1) ^ 1)) {
       const int s = nq & 1, p = it.pair(nq), c = it.chunk(nq);
       tc::mbar_arrive_expect_tx(&sh->bar[QK_FULL0 + s], 4 * 64 * 64 * 2);
       for (int h = 0; h < 2; ++h) {
@@ -182,13 +190,15 @@ __device__ void tma_role(uint8_t* sm, Small* sh, const CUtensorMap* mq, const CU
         tc::tma_load_3d(base, mq, &sh->bar[QK_FULL0 + s], h * 64, c * C, p);
         tc::tma_load_3d(base + 8192, mk, &sh->bar[QK_FULL0 + s], h * 64, c * C, p);
       }
+      TRACE(0, nq);
       ++nq;
       progressed = true;
     }
-    if (nv < N && tc::mbar_try_wait(&sh->bar[V_EMPTY], (nv & 1) ^ 1)) {
+    if (nv < N && tc::mbar_test_wait(&sh->bar[V_EMPTY], (nv & 1) ^ 1)) {
       tc::mbar_arrive_expect_tx(&sh->bar[V_FULL], 2 * 64 * 64 * 2);
       for (int h = 0; h < 2; ++h)
         tc::tma_load_3d(sm + OFF_V + h * 8192, mv, &sh->bar[V_FULL], h * 64, it.chunk(nv) * C, it.pair(nv));
+      TRACE(1, nv);
       ++nv;
       progressed = true;
     }
@@ -196,7 +206,6 @@ __device__ void tma_role(uint8_t* sm, Small* sh, const CUtensorMap* mq, const CU
       idle = 0;
     } else {
       if (++idle > kWaitLimit || *abort) goto fail;
-      if (idle > 4) __nanosleep(idle < 64 ? 20 : 100);
     }
   }
   return;
@@ -225,9 +234,15 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
     // n+1 (G1, W^T) is not held behind the recurrence of item n.
     int g1 = 0, wt = 0, um = 0, m2 = 0, pa = 0;
     uint32_t idle = 0;
+#ifdef SPOCK_PHASE_PROF
+    long long iters = 0;
+#endif
     while (m2 < N) {
+#ifdef SPOCK_PHASE_PROF
+      ++iters;
+#endif
       bool progressed = false;
-      if (m2 < um && tc::mbar_try_wait(&sh->bar[VN_READY], m2 & 1)) {
+      if (m2 < um && tc::mbar_test_wait(&sh->bar[VN_READY], m2 & 1)) {
         // state update + output of item m2: S += K^T VS ; D1 += [0 ; P] VN
         tc::tc_fence_after();
         const uint32_t k = sbase + OFF_QK + (m2 & 1) * 32768 + 8192;
@@ -239,11 +254,15 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
                       tc::sdesc(sbase + OFF_VN + ks * 2048, 8192, 1024), ID_U, 1);
         tc::mma_commit(&sh->bar[M2_DONE]);
         tc::mma_commit(&sh->bar[QK_EMPTY0 + (m2 & 1)]);
+        TRACE(5, m2);
+#ifdef SPOCK_PHASE_PROF
+        if (blockIdx.x == 0 && m2 < 64) g_trace[m2 * 32 + 26] = iters;
+#endif
         ++m2;
         progressed = true;
       }
-      if (um < wt && um == m2 && tc::mbar_try_wait(&sh->bar[PREP_DONE], um & 1) &&
-          tc::mbar_try_wait(&sh->bar[S16_READY], um & 1) && tc::mbar_try_wait(&sh->bar[AW_READY], um & 1)) {
+      if (um < wt && um == m2 && tc::mbar_test_wait(&sh->bar[PREP_DONE], um & 1) &&
+          tc::mbar_test_wait(&sh->bar[S16_READY], um & 1) && tc::mbar_test_wait(&sh->bar[AW_READY], um & 1)) {
         // U + MMA1 of item um: D1 = [T diag(beta); 0] V ; D1 += [-W ; Q'] S16
         tc::tc_fence_after();
         for (int ks = 0; ks < 4; ++ks)
@@ -254,26 +273,31 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
                       tc::sdesc(sbase + OFF_SB + ks * 2048, 16384, 1024), ID_U, 1);
         tc::mma_commit(&sh->bar[M1_DONE]);
         tc::mma_commit(&sh->bar[V_EMPTY]);
+        TRACE(4, um);
         ++um;
         progressed = true;
       }
-      if (wt < g1 && tc::mbar_try_wait(&sh->bar[TBE_READY], wt & 1)) {
+      // W^T of item wt overwrites W^T of item wt-1 in TMEM: the REC warps
+      // must have read that one first (they did once MMA1 of wt-1 is issued,
+      // which waits for their AW_READY).
+      if (wt < g1 && wt <= um && tc::mbar_test_wait(&sh->bar[TBE_READY], wt & 1)) {
         tc::tc_fence_after();
         const uint32_t k = sbase + OFF_QK + (wt & 1) * 32768 + 8192;
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_f16(mWT, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_TBE + ks * 32, 16, 1024),
                       ID_WT, ks > 0);
         tc::mma_commit(&sh->bar[WT_DONE]);
+        TRACE(3, wt);
         ++wt;
         progressed = true;
       }
       // prep has started item pa-1 (so it is done reading G1 of item pa-2)
-      if (pa < N && tc::mbar_try_wait(&sh->bar[PREP_A], pa & 1)) {
+      if (pa < N && tc::mbar_test_wait(&sh->bar[PREP_A], pa & 1)) {
         ++pa;
         progressed = true;
       }
       // G1 straight from the landed q/k tile, into the TMEM buffer of g1 & 1
-      if (g1 < N && (g1 < 2 || pa >= g1 - 1) && tc::mbar_try_wait(&sh->bar[QK_FULL0 + (g1 & 1)], (g1 >> 1) & 1)) {
+      if (g1 < N && (g1 < 2 || pa >= g1 - 1) && tc::mbar_test_wait(&sh->bar[QK_FULL0 + (g1 & 1)], (g1 >> 1) & 1)) {
         tc::tc_fence_after();
         const uint32_t qk = sbase + OFF_QK + (g1 & 1) * 32768;
         for (int ks = 0; ks < 8; ++ks) {
@@ -282,6 +306,7 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
                       ID_G1, ks > 0);
         }
         tc::mma_commit(&sh->bar[G1_DONE0 + (g1 & 1)]);
+        TRACE(2, g1);
         ++g1;
         progressed = true;
       }
@@ -289,7 +314,6 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
         idle = 0;
       } else {
         if (++idle > kWaitLimit || *abort) goto fail;
-        if (idle > 4) __nanosleep(idle < 64 ? 20 : 100);
       }
     }
   }
@@ -299,7 +323,7 @@ fail:
   atomicExch(err, 2);
   // let MMAs already issued finish before TMEM is released (bounded)
   tc::mma_commit(&sh->bar[DRAIN]);
-  for (uint32_t i = 0; i < kWaitLimit && !tc::mbar_try_wait(&sh->bar[DRAIN], 0); ++i) {
+  for (uint32_t i = 0; i < kWaitLimit && !tc::mbar_test_wait(&sh->bar[DRAIN], 0); ++i) {
   }
 }
 
@@ -329,15 +353,15 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
   float* NM = reinterpret_cast<float*>(sm + OFF_NM);
   float* TM = reinterpret_cast<float*>(sm + OFF_TM);
   float* YM = reinterpret_cast<float*>(sm + OFF_YM);
-  __shared__ float s_warp_total;
   const float scale = 0.08838834764831845f;
   const int N = it.count();
   auto sync = [] { group_sync(BAR_PREP, kPrepThreads); };
-  auto wait_all = [&](int b, uint32_t parity) -> bool {
-    const bool ok = wait_bar(&sh->bar[b], parity, abort);
-    return !group_any(BAR_PREP, kPrepThreads, !ok);
-  };
-  auto prefetch_gb = [&](int n) {  // cp.async: not waited for by the barriers in between
+  // Waits are per thread (no barrier): a thread whose wait gives up sets the
+  // shared abort flag, later waits return at once, and every thread still
+  // runs the item to its end, where one group-wide OR decides to leave.
+  bool bad = false;
+  auto wait_all = [&](int b, uint32_t parity) { bad |= !wait_bar(&sh->bar[b], parity, abort); };
+  auto prefetch_gb = [&](int n) {  // cp.async by the thread of each token; waited for at item n
     if (n < N && t < C) {
       const int tok = it.chunk(n) * C + t;
       const bool in = tok < it.S;
@@ -357,33 +381,38 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
   for (int n = 0; n < N; ++n) {
     const int s = n & 1;
     uint8_t* qk = sm + OFF_QK + s * 32768;
+    if (t == 0) TRACE(6, n);
     // 1. cumulative g (shuffle scan over two warps); g/beta of n+1 prefetched
-    cp_async_wait_all();
-    float gv = 0.f, bv = 0.f;
-    if (t < C) {
-      gv = sh->graw[s][t];
-      bv = sh->braw[s][t];
-    }
-    prefetch_gb(n + 1);
-    if (t < C) {
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, gv, o);
-        if ((t & 31) >= o) gv += y;
+    {
+      __shared__ float s_warp_total;
+      float gv = 0.f, bv = 0.f;
+      cp_async_wait_all();
+      if (t < C) {
+        gv = sh->graw[s][t];
+        bv = sh->braw[s][t];
       }
-      if (t == 31) s_warp_total = gv;
-    }
-    sync();
-    if (t < C) {
-      if (t >= 32) gv += s_warp_total;
-      sh->gc[s][t] = gv;
-      sh->gl[s][t] = gv * kLog2e;
-      sh->beta[s][t] = bv;
-      sh->eg[s][t] = ex2(gv * kLog2e);
+      prefetch_gb(n + 1);
+      if (t < C) {
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, gv, o);
+          if ((t & 31) >= o) gv += y;
+        }
+        if (t == 31) s_warp_total = gv;
+      }
+      sync();
+      if (t < C) {
+        if (t >= 32) gv += s_warp_total;
+        sh->gc[s][t] = gv;
+        sh->gl[s][t] = gv * kLog2e;
+        sh->beta[s][t] = bv;
+        sh->eg[s][t] = ex2(gv * kLog2e);
+      }
     }
     PROF_MARK(0, 0);
     // 2. q/k tile landed: convert, publish for G1
-    if (!wait_all(QK_FULL0 + s, (n >> 1) & 1)) break;
+    wait_all(QK_FULL0 + s, (n >> 1) & 1);
+    if (t == 0) TRACE(7, n);
     PROF_MARK(0, 1);
     sync();
     if (t == 0) {
@@ -413,7 +442,8 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
           dec[4 * q + k] = keep ? f * ex2(gi - gj[k]) : 0.f;
         }
       }
-      if (!wait_all(G1_DONE0 + (n & 1), (n >> 1) & 1)) break;
+      wait_all(G1_DONE0 + (n & 1), (n >> 1) & 1);
+      if (t == 0) TRACE(8, n);
       PROF_MARK(0, 3);
       tc::tc_fence_after();
       float a[32];
@@ -442,6 +472,7 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     tc::tc_fence_before();
     sync();
     PROF_MARK(0, 4);
+    if (t == 0) TRACE(9, n);
     // 4. T = (I - N)^-1
 #ifdef SPOCK_PHASE_PROF
     {
@@ -459,9 +490,10 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     chunk::solve_unit_lower_blk(NM, TM, YM, t, sync);
 #endif
     PROF_MARK(0, 5);
+    if (t == 0) TRACE(10, n);
     // 5. T diag(beta e^gc) -> TBE (for W^T) once W^T of the previous item has
     //    read it; T diag(beta) kept in registers
-    if (n > 0 && !wait_all(WT_DONE, (n - 1) & 1)) break;
+    if (n > 0) wait_all(WT_DONE, (n - 1) & 1);
     uint4 tbreg[2];
     {
       const int i = t >> 2;
@@ -486,10 +518,12 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     tc::fence_async_smem();
     sync();
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[TBE_READY], 0);
+    if (t == 0) TRACE(11, n);
     PROF_MARK(0, 6);
     // 6. once MMA1 of the previous item has read them: T diag(beta) and Q'
-    if (n > 0 && !wait_all(M1_DONE, (n - 1) & 1)) break;
+    if (n > 0) wait_all(M1_DONE, (n - 1) & 1);
     PROF_MARK(0, 7);
+    if (t == 0) TRACE(12, n);
     {
       const int i = t >> 2;
 #pragma unroll
@@ -497,8 +531,9 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     }
     PROF_MARK(0, 8);
     // 8. once the previous item's output MMA has read it: P
-    if (n > 0 && !wait_all(M2_DONE, (n - 1) & 1)) break;
+    if (n > 0) wait_all(M2_DONE, (n - 1) & 1);
     PROF_MARK(0, 11);
+    if (t == 0) TRACE(13, n);
     if (l < C) {
 #pragma unroll
       for (int q = 0; q < 4; ++q)
@@ -506,11 +541,13 @@ __device__ void prep_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const f
     }
     PROF_MARK(0, 12);
     // 9. V of this item (converted to fp16 by the REC warpgroup)
-    if (!wait_all(V_CONV, n & 1)) break;
+    wait_all(V_CONV, n & 1);
     PROF_MARK(0, 13);
+    if (t == 0) TRACE(14, n);
     tc::fence_async_smem();
-    sync();
+    if (group_any(BAR_PREP, kPrepThreads, bad)) break;
     if (t == 0) tc::mbar_arrive_expect_tx(&sh->bar[PREP_DONE], 0);
+    if (t == 0) TRACE(15, n);
     PROF_MARK(0, 14);
   }
   cp_async_wait_all();
@@ -528,23 +565,34 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
   const uint32_t tS = tb + lane_base, tD1 = tb + 128 + lane_base, tWT = tb + 384 + lane_base;
   int N = it.count();
   auto sync = [] { group_sync(BAR_REC, 128); };
-  auto wait_all = [&](int b, uint32_t parity) -> bool {
-    const bool ok = wait_bar(&sh->bar[b], parity, abort);
-    return !group_any(BAR_REC, 128, !ok);
-  };
+  // per-thread waits; one group-wide OR per item decides to leave (as in PREP)
+  bool bad = false;
+  auto wait_all = [&](int b, uint32_t parity) { bad |= !wait_bar(&sh->bar[b], parity, abort); };
 
   // V of item m -> fp16 in place, then published to PREP as V_CONV
-  auto convert_v = [&](int m) -> bool {
-    if (!wait_all(V_FULL, m & 1)) return false;
+  auto convert_v = [&](int m) {
+    wait_all(V_FULL, m & 1);
     if constexpr (kBf16) {
       bf16_to_f16_inplace(reinterpret_cast<uint4*>(sm + OFF_V), 16384 / 16, rt, 128);
       tc::fence_async_smem();
     }
     sync();
     if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[V_CONV], 0);
-    return true;
   };
-  if (N > 0 && !convert_v(0)) N = 0;
+  if (N > 0) convert_v(0);
+  // output rows of item m (TMEM lanes 64..127 of D1)
+  auto store_out = [&](int m) {
+    if (rt >= C) {
+      const int tok = it.chunk(m) * C + (rt - C);
+      const size_t row = (size_t)it.pair(m) * it.S + tok;
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        float v[32];
+        tc::tmem_ld32(tD1 + cb * 32, v);
+        if (tok < it.S) store_row32<kOut>(out, row * D + cb * 32, v);
+      }
+    }
+  };
 
   PROF_DECL
   for (int n = 0; n < N; ++n) {
@@ -570,9 +618,11 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
       tc::tmem_st_wait();
     }
     PROF_MARK(1, 0);
+    if (rt == 0) TRACE(16, n);
     // 2. S16 <- S ; S <- e^{gL} S
-    if (!wait_all(GC_READY0 + s, (n >> 1) & 1)) break;
+    wait_all(GC_READY0 + s, (n >> 1) & 1);
     PROF_MARK(1, 1);
+    if (rt == 0) TRACE(17, n);
     const float egL = sh->eg[s][C - 1];
     tc::tc_fence_after();
 #pragma unroll 1
@@ -591,9 +641,17 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     tc::tc_fence_before();
     sync();
     if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[S16_READY], 0);
+    if (rt == 0) TRACE(18, n);
+    // output of the previous item, off the S16 path; D1 is next written by
+    // MMA1 of this item, which waits for AW_READY below
+    if (n > 0) {
+      store_out(n - 1);
+      tc::tc_fence_before();
+    }
     // 2b. A operand of MMA1: -W (from W^T in TMEM) and Q' = diag(s e^gc) Q.
     //     MMA1 of the previous item, the last reader of AW, has completed.
-    if (!wait_all(WT_DONE, n & 1)) break;
+    wait_all(WT_DONE, n & 1);
+    if (rt == 0) TRACE(19, n);
     tc::tc_fence_after();
     {
       float w[64];
@@ -637,10 +695,12 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     tc::tc_fence_before();
     sync();
     if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[AW_READY], 0);
+    if (rt == 0) TRACE(20, n);
     PROF_MARK(1, 2);
     // 3. v_new rows (lanes 0..63) -> VN, VS
-    if (!wait_all(M1_DONE, n & 1)) break;
+    wait_all(M1_DONE, n & 1);
     PROF_MARK(1, 3);
+    if (rt == 0) TRACE(21, n);
     tc::tc_fence_after();
     if (rt < C) {
       const float fs = ex2((sh->gc[s][C - 1] - sh->gc[s][rt]) * kLog2e);
@@ -664,21 +724,15 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     tc::tc_fence_before();
     sync();
     if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[VN_READY], 0);
-    if (n + 1 < N && !convert_v(n + 1)) break;
+    if (rt == 0) TRACE(22, n);
+    if (n + 1 < N) convert_v(n + 1);
     PROF_MARK(1, 4);
+    if (rt == 0) TRACE(23, n);
     // 4. output rows (lanes 64..127); final state after a pair's last chunk
-    if (!wait_all(M2_DONE, n & 1)) break;
+    wait_all(M2_DONE, n & 1);
     PROF_MARK(1, 5);
+    if (rt == 0) TRACE(24, n);
     tc::tc_fence_after();
-    if (rt >= C) {
-      const int tok = c * C + (rt - C);
-#pragma unroll 1
-      for (int cb = 0; cb < 4; ++cb) {
-        float v[32];
-        tc::tmem_ld32(tD1 + cb * 32, v);
-        if (tok < it.S) store_row32<kOut>(out, ((size_t)p * it.S + tok) * D + cb * 32, v);
-      }
-    }
     if (c == it.nch - 1) {
 #pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
@@ -691,7 +745,10 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     }
     tc::tc_fence_before();
     PROF_MARK(1, 6);
+    if (rt == 0) TRACE(25, n);
+    if (group_any(BAR_REC, 128, bad)) break;
   }
+  if (N > 0 && !*abort) store_out(N - 1);
   PROF_FLUSH(1);
   if (*abort && rt == 0) atomicExch(err, 2);
 }
@@ -782,5 +839,8 @@ SPOCK_PIPE_INST(true, SPOCK_BF16)
 extern "C" __attribute__((visibility("default"))) int spock_debug_phase_profile(unsigned long long* out, int n) {
   if (n > 148 * 4 * 32) n = 148 * 4 * 32;
   return (int)cudaMemcpyFromSymbol(out, spock::pipe::g_phase_prof, n * sizeof(unsigned long long));
+}
+extern "C" __attribute__((visibility("default"))) int spock_debug_trace(long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, spock::pipe::g_trace, 64 * 32 * sizeof(long long));
 }
 #endif
