@@ -15,9 +15,9 @@ std::atomic<uint64_t> g_launches{0};
 
 Status launch_decode_step(const spock_dn_layer& L, int64_t batch, void* qkv, void* conv_state,
                           float* state, const void* a, const void* b, const void* z, void* out,
-                          void* core_raw, cudaStream_t stream);
+                          void* core_raw, int* err, cudaStream_t stream);
 Status launch_recurrent(int64_t batch, int H, int kd, int vd, const void* q, const void* k,
-                        const void* v, const float* g, const float* beta, float* state, void* out,
+                        const void* v, const float* g, const float* beta, float* state, void* out, int* err,
                         cudaStream_t stream);
 Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, const void* q,
                             const void* k, const void* v, const float* g, const float* beta,
@@ -191,7 +191,7 @@ __attribute__((visibility("default"))) int spock_deltanet_decode_step(
     return fail(ctx, SPOCK_ERR_INVALID, "spock_deltanet_decode_step: NULL pointer");
   DeviceGuard dg(ctx->device);
   return finish(ctx, spock::launch_decode_step(*layer, batch, qkv, conv_state, state, a, b, z, out,
-                                               core_raw, (cudaStream_t)stream));
+                                               core_raw, ctx->d_err_flag, (cudaStream_t)stream));
 }
 
 __attribute__((visibility("default"))) int spock_deltanet_recurrent(
@@ -203,7 +203,7 @@ __attribute__((visibility("default"))) int spock_deltanet_recurrent(
     return fail(ctx, SPOCK_ERR_INVALID, "spock_deltanet_recurrent: NULL pointer");
   DeviceGuard dg(ctx->device);
   return finish(ctx, spock::launch_recurrent(batch, num_heads, key_dim, value_dim, q, k, v, g,
-                                             beta, state, out, (cudaStream_t)stream));
+                                             beta, state, out, ctx->d_err_flag, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -53,7 +53,7 @@ Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64
                           cudaStream_t st);
 Status launch_decode_step_strided(const spock_dn_layer& L, int64_t batch, void* qkv, int qkv_ld,
                                   void* conv_state, float* state, const void* a, const void* b, int ab_ld,
-                                  const void* z, int z_ld, void* out, int out_ld, void* core_raw,
+                                  const void* z, int z_ld, void* out, int out_ld, void* core_raw, int* err,
                                   cudaStream_t stream);
 enum { EPI_F16 = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 
@@ -178,7 +178,7 @@ Status record_step(spock_model* m, cudaStream_t st) {
       TRY(spock::launch_decode_step_strided(
           dl, B, p, DN_IN, (uint16_t*)m->conv_state + (size_t)l.dn_idx * B * CONV * 4,
           m->dn_state + (size_t)l.dn_idx * B * DNH * DND * DND, p + CONV + 2048, p + CONV + 2048 + DNH, DN_IN,
-          p + CONV, DN_IN, m->mix, DNH * DND, nullptr, st));
+          p + CONV, DN_IN, m->mix, DNH * DND, nullptr, m->err_flag, st));
       TRY(gemm(m, spock::EPI_RESIDUAL, m->mix, l.w_out, HID, DNH * DND, m->h, HID, m->h, st));
     } else {
       TRY(gemm(m, spock::EPI_F16, m->x, l.w_in, ATT_IN, HID, m->proj, ATT_IN, nullptr, st));
