@@ -69,36 +69,55 @@ __device__ __forceinline__ float warp_tree128(const float* s, int lane) {
   return v0;
 }
 
-// q, k, v of head h of sequence s (scaled q in sq), g and beta -> shared memory.
-// Fused: causal conv + SiLU + L2 from the raw qkv token and the conv cache.
-template <bool kFused, class Sync>
-__device__ __forceinline__ void prologue(const Args& A, Smem& m, int s, int h, int t, Sync sync) {
-  const int H = A.H;
+// Global inputs of the fused prologue for one thread: its conv channels
+// c = t and c = t + 256 (threads 0..127 have two), and a, b for the last thread.
+constexpr int kPer = (3 * kDim + kThreads - 1) / kThreads;
+struct PIn {
+  uint2 st[kPer], wv[kPer];
+  uint16_t xin[kPer];
+  float a_val, b_val;
+};
+
+template <bool kFused>
+__device__ __forceinline__ PIn prologue_load(const Args& A, int s, int h, int t) {
+  PIn in{};
   if constexpr (kFused) {
-    const int conv_dim = H * 3 * kDim;
-    uint16_t* x = A.qkv + (size_t)s * A.qkv_ld;
-    uint16_t* cs = A.conv_state + (size_t)s * conv_dim * 4;
-    if (t == kThreads - 1) {  // a thread with a single conv channel
-      const float a_val = h2f(A.a_in[(size_t)s * A.ab_ld + h]);
-      const float b_val = h2f(A.b_in[(size_t)s * A.ab_ld + h]);
-      const float a_log = A.a_log_bias[h * 2 + 0], dt_bias = A.a_log_bias[h * 2 + 1];
-      const float sp = logf(add_rn(1.0f, expf(add_rn(a_val, dt_bias))));
-      m.g = mul_rn(-expf(a_log), sp);
-      m.beta = __fdiv_rn(1.0f, add_rn(1.0f, expf(-b_val)));
-    }
-    // channels c = t and c = t + 256 (threads 0..127): all loads first
-    constexpr int kPer = (3 * kDim + kThreads - 1) / kThreads;
-    uint2 stv[kPer], wvv[kPer];
-    uint16_t xinv[kPer];
+    const int H = A.H;
+    const uint16_t* x = A.qkv + (size_t)s * A.qkv_ld;
+    const uint16_t* cs = A.conv_state + (size_t)s * H * 3 * kDim * 4;
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
       const int c = t + u * kThreads;
       if (c < 3 * kDim) {
         const int ch = (c / kDim) * H * kDim + h * kDim + c % kDim;
-        stv[u] = *reinterpret_cast<const uint2*>(cs + (size_t)ch * 4);
-        wvv[u] = *reinterpret_cast<const uint2*>(A.conv_w + (size_t)ch * 4);
-        xinv[u] = x[ch];
+        in.st[u] = *reinterpret_cast<const uint2*>(cs + (size_t)ch * 4);
+        in.wv[u] = *reinterpret_cast<const uint2*>(A.conv_w + (size_t)ch * 4);
+        in.xin[u] = x[ch];
       }
+    }
+    if (t == kThreads - 1) {  // a thread with a single conv channel
+      in.a_val = h2f(A.a_in[(size_t)s * A.ab_ld + h]);
+      in.b_val = h2f(A.b_in[(size_t)s * A.ab_ld + h]);
+    }
+  }
+  return in;
+}
+
+// q, k, v of head h of sequence s (scaled q in sq), g and beta -> shared memory.
+// Fused: causal conv + SiLU + L2 from the raw qkv token and the conv cache
+// (their global inputs already in `in`).
+template <bool kFused, class Sync>
+__device__ __forceinline__ void prologue(const Args& A, Smem& m, int s, int h, int t, Sync sync, const PIn& in) {
+  const int H = A.H;
+  if constexpr (kFused) {
+    const int conv_dim = H * 3 * kDim;
+    uint16_t* x = A.qkv + (size_t)s * A.qkv_ld;
+    uint16_t* cs = A.conv_state + (size_t)s * conv_dim * 4;
+    if (t == kThreads - 1) {
+      const float a_log = A.a_log_bias[h * 2 + 0], dt_bias = A.a_log_bias[h * 2 + 1];
+      const float sp = logf(add_rn(1.0f, expf(add_rn(in.a_val, dt_bias))));
+      m.g = mul_rn(-expf(a_log), sp);
+      m.beta = __fdiv_rn(1.0f, add_rn(1.0f, expf(-in.b_val)));
     }
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
@@ -106,9 +125,9 @@ __device__ __forceinline__ void prologue(const Args& A, Smem& m, int s, int h, i
       if (c >= 3 * kDim) continue;
       const int blk = c / kDim, off = c % kDim;
       const int ch = blk * H * kDim + h * kDim + off;
-      uint2 st = stv[u];
-      const uint2 wv = wvv[u];
-      const uint16_t xin = xinv[u];
+      uint2 st = in.st[u];
+      const uint2 wv = in.wv[u];
+      const uint16_t xin = in.xin[u];
       // shift left by one slot, insert the new value at the end
       const uint16_t s0 = (uint16_t)(st.x >> 16), s1 = (uint16_t)(st.y & 0xffff),
                      s2 = (uint16_t)(st.y >> 16), s3 = xin;
@@ -258,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 2) dn_decode_kernel(const __grid_con
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r) S[r] = S4[(warp * kRowsPerWarp + r) * (kDim / 4) + lane];
   auto sync = [] { __syncthreads(); };
-  prologue<kFused>(A, m, s, h, threadIdx.x, sync);
+  prologue<kFused>(A, m, s, h, threadIdx.x, sync, prologue_load<kFused>(A, s, h, threadIdx.x));
   update_and_output<kFused>(A, m, S, S4, s, h, threadIdx.x, sync);
 }
 
@@ -298,9 +317,28 @@ __global__ void __launch_bounds__(2 * kThreads, 1)
   __syncthreads();
   const int bar_id = 1 + grp;
   auto sync = [bar_id] { asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(kThreads) : "memory"); };
+  auto coord = [&](int j, int& s, int& h) {
+    const int it = (int)blockIdx.x + j * G;
+    s = it / A.H;
+    h = it % A.H;
+  };
+  PIn nxt{};
+  if (grp < mine) {
+    int s0, h0;
+    coord(grp, s0, h0);
+    nxt = prologue_load<kFused>(A, s0, h0, t);
+  }
   for (int j = grp; j < mine; j += 2) {
-    const int it = (int)blockIdx.x + j * G, s = it / A.H, h = it % A.H, b = j % kStages;
-    prologue<kFused>(A, m, s, h, t, sync);
+    int s, h;
+    coord(j, s, h);
+    const int b = j % kStages;
+    const PIn cur = nxt;
+    if (j + 2 < mine) {  // the group's next item: its loads fly during this item
+      int s2, h2;
+      coord(j + 2, s2, h2);
+      nxt = prologue_load<kFused>(A, s2, h2, t);
+    }
+    prologue<kFused>(A, m, s, h, t, sync, cur);
     const bool ok = tc::mbar_wait_bounded(&full[b], (uint32_t)(j / kStages) & 1u, kWaitLimit);
     uint32_t any;
     asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, %2, %3, q;\n selp.u32 %0, 1, 0, p;\n}"
