@@ -8,11 +8,17 @@
 // one pass over the weights serves the whole batch; decode is HBM-bound on W.
 // Accumulators live in TMEM (lane = weight row, column = batch row).
 //
-// Grid: (row tiles, K splits). With K splits, every CTA adds its fp32 partial
-// tile into an accumulator with vector atomics (L2-side, all splits in
-// parallel); the last CTA of a tile (atomic ticket) reads the sum once, clears
-// it for the next launch and runs the epilogue. The split count is capped so
-// partial traffic stays below the weight traffic it parallelises.
+// Grid: (row tiles, K splits, batch blocks). Large batches are split over
+// batch blocks of bn >= 64 rows first (no partial sums: the CTAs of one row
+// tile share its weight slab through L2), then over K: with K splits every
+// CTA adds its fp32 partial tile into an accumulator with vector atomics
+// (L2-side, all splits in parallel); the last CTA of a tile (atomic ticket)
+// reads the sum once, clears it for the next launch and runs the epilogue.
+// The K split count is capped so partial traffic stays below the weight
+// traffic it parallelises.
+//
+// The epilogue stages the fp16 tile in shared memory (TMEM lanes are weight
+// rows) and writes it back, with the residual, in 16-byte row segments.
 //
 // Epilogues (fused):
 //   F16      y = fp16(acc)
@@ -26,28 +32,10 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "gemm.h"
 #include "tc.cuh"
 
 namespace spock {
-
-enum GemmEpi { EPI_F16 = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
-
-struct GemmArgs {
-  int n_out;        // weight rows
-  int k;            // inner dim, multiple of 64
-  int batch;        // real batch rows
-  int bpad;         // padded batch (MMA N), multiple of 16, <= 256
-  int kb_per_split; // 64-wide k blocks per split
-  int nsplit;
-  __half* y;        // [batch][ldy]
-  int ldy;
-  const __half* res;    // RESIDUAL: [batch][ldy]
-  float* ws;            // split accumulator [n_tiles*128][bpad], zero between launches
-  int* tickets;         // [n_tiles], zero before launch, left zero after
-  float* amax_val;      // ARGMAX partials [n_tiles][batch]
-  int* amax_idx;
-  int* err;
-};
 
 namespace {
 
@@ -76,7 +64,7 @@ __global__ void __launch_bounds__(128, 1)
                        GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
-  const int a_bytes = 128 * 128, b_bytes = a.bpad * 128, stage_bytes = a_bytes + b_bytes;
+  const int a_bytes = 128 * 128, b_bytes = a.bn * 128, stage_bytes = a_bytes + b_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * stage_bytes);
   uint64_t* empty = full + kStages;
   uint64_t* done = empty + kStages;
@@ -86,11 +74,11 @@ __global__ void __launch_bounds__(128, 1)
   int* s_redi = reinterpret_cast<int*>(s_red + 4 * 256);
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int tile = blockIdx.x, split = blockIdx.y;
+  const int tile = blockIdx.x, split = blockIdx.y, n0 = blockIdx.z * a.bn;
   const int kb0 = split * a.kb_per_split;
   const int nkb = min(a.kb_per_split, a.k / 64 - kb0);
   uint32_t ncols = 32;
-  while ((int)ncols < a.bpad) ncols <<= 1;
+  while ((int)ncols < a.bn) ncols <<= 1;
 
   if (t == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -120,10 +108,10 @@ __global__ void __launch_bounds__(128, 1)
       uint8_t* st = sm + s * stage_bytes;
       tc::mbar_arrive_expect_tx(&full[s], stage_bytes);
       tma_load_2d(st, &tmw, &full[s], (kb0 + i) * 64, tile * 128);
-      tma_load_2d(st + a_bytes, &tmx, &full[s], (kb0 + i) * 64, 0);
+      tma_load_2d(st + a_bytes, &tmx, &full[s], (kb0 + i) * 64, n0);
     }
   } else if (warp == 1 && lane == 0) {  // MMA issuer
-    const uint32_t idesc = tc::idesc_f16(128, a.bpad, false, false);
+    const uint32_t idesc = tc::idesc_f16(128, a.bn, false, false);
     const uint32_t sbase = tc::smem_u32(sm);
     for (int i = 0; i < nkb && ok; ++i) {
       const int s = i % kStages;
@@ -152,27 +140,26 @@ __global__ void __launch_bounds__(128, 1)
   tc::tc_fence_after();
   const int row = tile * 128 + t;
   const uint32_t taddr = tb + ((uint32_t)(warp * 32) << 16);
-  const size_t tile_stride = (size_t)gridDim.x * 128 * a.bpad;
 
   bool finisher = true;
-  (void)tile_stride;
   if (a.nsplit > 1) {
-    // partial tile -> accumulator [row][col] (vector atomics, resolved in L2)
-    float* wsp = a.ws + (size_t)row * a.bpad;
-    for (int c0 = 0; c0 < a.bpad; c0 += 32) {
+    // partial tile -> accumulator [row][n0 + col] (vector atomics, resolved in L2)
+    float* wsp = a.ws + (size_t)row * a.bpad + n0;
+    for (int c0 = 0; c0 < a.bn; c0 += 32) {
       float v[32];
       tc::tmem_ld32(taddr + c0, v);
 #pragma unroll
       for (int q = 0; q < 8; ++q)
-        if (c0 + 4 * q < a.bpad)
+        if (c0 + 4 * q < a.bn)
           atomicAdd(reinterpret_cast<float4*>(wsp + c0) + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
     }
     __threadfence();
     __syncthreads();
     if (t == 0) {
-      const int ticket = atomicAdd(&a.tickets[tile], 1);
+      int* ticket_p = a.tickets + tile * gridDim.z + blockIdx.z;
+      const int ticket = atomicAdd(ticket_p, 1);
       *s_last = (ticket == a.nsplit - 1);
-      if (*s_last) a.tickets[tile] = 0;  // ready for the next launch
+      if (*s_last) *ticket_p = 0;  // ready for the next launch
     }
     __syncthreads();
     finisher = *s_last != 0;
@@ -180,13 +167,16 @@ __global__ void __launch_bounds__(128, 1)
   }
 
   if (finisher) {
-    for (int c0 = 0; c0 < a.bpad; c0 += 32) {
+    // the pipeline's stages are idle now: fp16 staging tile [bn][width]
+    __half* stg = reinterpret_cast<__half*>(sm);
+    constexpr int width = kEpi == EPI_SWIGLU ? 64 : 128;
+    for (int c0 = 0; c0 < a.bn; c0 += 32) {
       float v[32];
       if (a.nsplit > 1) {
-        float4* p = reinterpret_cast<float4*>(a.ws + (size_t)row * a.bpad + c0);
+        float4* p = reinterpret_cast<float4*>(a.ws + (size_t)row * a.bpad + n0 + c0);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          if (c0 + 4 * q < a.bpad) {
+          if (c0 + 4 * q < a.bn) {
             const float4 x = __ldcg(p + q);
             v[4 * q] = x.x;
             v[4 * q + 1] = x.y;
@@ -201,33 +191,25 @@ __global__ void __launch_bounds__(128, 1)
         tc::tmem_ld32(taddr + c0, v);
       }
       if constexpr (kEpi == EPI_F16 || kEpi == EPI_RESIDUAL) {
-        if (row < a.n_out) {
-#pragma unroll 4
-          for (int k = 0; k < 32; ++k) {
-            const int b = c0 + k;
-            if (b < a.batch) {
-              float o = __half2float(__float2half_rn(v[k]));
-              if constexpr (kEpi == EPI_RESIDUAL) o = o + __half2float(a.res[(size_t)b * a.ldy + row]);
-              a.y[(size_t)b * a.ldy + row] = __float2half_rn(o);
-            }
-          }
-        }
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (c0 + k < a.bn) stg[(c0 + k) * width + t] = __float2half_rn(v[k]);
       } else if constexpr (kEpi == EPI_SWIGLU) {
-        const int grp = row >> 5, j = row & 31, feat = grp * 16 + (j & 15);
+        // rows are [gate g..g+15 | up g..g+15] groups of 32: lanes j and j^16 pair up
+        const int j = t & 31, feat = (t >> 5) * 16 + (j & 15);
 #pragma unroll 4
         for (int k = 0; k < 32; ++k) {
           const float u = __shfl_xor_sync(0xffffffffu, v[k], 16);
-          const int b = c0 + k;
-          if (j < 16 && b < a.batch && row < a.n_out) {
+          if (j < 16 && c0 + k < a.bn) {
             const float g16 = __half2float(__float2half_rn(v[k]));
             const float u16 = __half2float(__float2half_rn(u));
             const float silu = __fdiv_rn(g16, __fadd_rn(1.0f, expf(-g16)));
-            a.y[(size_t)b * a.ldy + feat] = __float2half_rn(__fmul_rn(silu, u16));
+            stg[(c0 + k) * width + feat] = __float2half_rn(__fmul_rn(silu, u16));
           }
         }
       } else {  // EPI_ARGMAX: per batch column, max fp16 logit over the tile's rows, lowest index on ties
         for (int k = 0; k < 32; ++k) {
-          const int b = c0 + k;
+          const int b = n0 + c0 + k;
           float val = (row < a.n_out) ? __half2float(__float2half_rn(v[k])) : -INFINITY;
           int idx = (row < a.n_out) ? row : 0x7fffffff;
 #pragma unroll
@@ -239,16 +221,18 @@ __global__ void __launch_bounds__(128, 1)
               idx = oi;
             }
           }
-          if (lane == 0) {
+          if (lane == 0 && c0 + k < a.bn) {
             s_red[warp * 256 + b] = val;
             s_redi[warp * 256 + b] = idx;
           }
         }
       }
     }
+    __syncthreads();
     if constexpr (kEpi == EPI_ARGMAX) {
-      __syncthreads();
-      for (int b = t; b < a.batch; b += 128) {
+      for (int bl = t; bl < a.bn; bl += 128) {
+        const int b = n0 + bl;
+        if (b >= a.batch) continue;
         float val = s_red[b];
         int idx = s_redi[b];
         for (int w = 1; w < 4; ++w) {
@@ -261,6 +245,28 @@ __global__ void __launch_bounds__(128, 1)
         }
         a.amax_val[(size_t)tile * a.batch + b] = val;
         a.amax_idx[(size_t)tile * a.batch + b] = idx;
+      }
+    } else {
+      // 16-byte segments: batch row bl, outputs out0 + 8c .. out0 + 8c + 7
+      const int out0 = tile * width;
+      const int n_valid = (kEpi == EPI_SWIGLU ? a.n_out / 2 : a.n_out) - out0;
+      constexpr int segs = width / 8;
+      for (int i = t; i < a.bn * segs; i += 128) {
+        const int bl = i / segs, c = i % segs, b = n0 + bl;
+        if (b >= a.batch || 8 * c >= n_valid) continue;
+        uint4 val = *reinterpret_cast<const uint4*>(stg + bl * width + 8 * c);
+        const size_t off = (size_t)b * a.ldy + out0 + 8 * c;
+        if constexpr (kEpi == EPI_RESIDUAL) {
+          const uint4 r = *reinterpret_cast<const uint4*>(a.res + off);
+          __half2* pv = reinterpret_cast<__half2*>(&val);
+          const __half2* pr = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 x = __half22float2(pv[e]), y = __half22float2(pr[e]);
+            pv[e] = __floats2half2_rn(x.x + y.x, x.y + y.y);
+          }
+        }
+        *reinterpret_cast<uint4*>(a.y + off) = val;
       }
     }
   }
@@ -334,8 +340,6 @@ Status map2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int b
 
 }  // namespace
 
-Status gemm_prepare();
-
 // x: [bpad][k] fp16 (rows >= batch may hold anything), W: [n_out][k] fp16.
 // Workspace needs nsplit * ceil(n_out/128) * 128 * bpad floats when nsplit > 1,
 // tickets ceil(n_out/128) ints (zero), ARGMAX partials ceil(n_out/128) * batch.
@@ -344,16 +348,29 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: k % 64, 16 <= bpad <= 256 (multiple of 16), batch <= bpad");
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15))
     return Status::err(SPOCK_ERR_INVALID, "gemm: operands must be 16-byte aligned");
+  if (epi != EPI_ARGMAX) {
+    const int outs = epi == EPI_SWIGLU ? a.n_out / 2 : a.n_out;
+    if (outs % 8 || a.ldy % 8 || ((uintptr_t)a.y & 15) || ((uintptr_t)a.res & 15) ||
+        (epi == EPI_SWIGLU && a.n_out % 32))
+      return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: outputs and ldy must be multiples of 8, y/res 16-byte aligned");
+  }
+  const int ntiles = (a.n_out + 127) / 128, kbs = a.k / 64;
+  // batch blocks first (no partial sums), down to 64 rows
+  int nb = 1;
+  a.bn = a.bpad;
+  while (ntiles * nb < sms && a.bn % 32 == 0 && a.bn / 2 >= 64) {
+    a.bn /= 2;
+    nb *= 2;
+  }
   CUtensorMap mw, mx;
   Status s = map2d(&mw, w, a.n_out, a.k, 128);
   if (s.code) return s;
-  s = map2d(&mx, x, a.bpad, a.k, a.bpad);
+  s = map2d(&mx, x, a.bpad, a.k, a.bn);
   if (s.code) return s;
-  const int ntiles = (a.n_out + 127) / 128, kbs = a.k / 64;
   if (a.nsplit < 1) {  // enough CTAs to stream the weights from every SM ...
-    int want = (sms + ntiles - 1) / ntiles;
-    // ... but no more partial-tile traffic (128 x bpad fp32) than weight traffic
-    const int cap = a.k / (2 * a.bpad);
+    int want = (sms + ntiles * nb - 1) / (ntiles * nb);
+    // ... but no more partial-tile traffic (128 x bn fp32) than weight traffic
+    const int cap = a.k / (2 * a.bn);
     want = want > cap ? cap : want;
     want = want < 1 ? 1 : want;
     a.nsplit = want > kbs ? kbs : want;
@@ -361,8 +378,8 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   a.kb_per_split = (kbs + a.nsplit - 1) / a.nsplit;
   a.nsplit = (kbs + a.kb_per_split - 1) / a.kb_per_split;
   if (a.nsplit > 1 && (!a.ws || !a.tickets)) return Status::err(SPOCK_ERR_INVALID, "gemm: split-K needs a workspace");
-  const int smem = kStages * (128 * 128 + a.bpad * 128) + 64 + 8 * 256 * 4 + 1024;
-  dim3 grid(ntiles, a.nsplit);
+  const int smem = kStages * (128 * 128 + a.bn * 128) + 64 + 8 * 256 * 4 + 1024;
+  dim3 grid(ntiles, a.nsplit, nb);
   {
     static std::once_flag once;
     static Status prep;

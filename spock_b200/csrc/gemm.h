@@ -1,0 +1,34 @@
+// Weight-streaming projection GEMM of the decode glue (gemm.cu): interface
+// shared by the kernels and the model session.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace spock {
+
+enum GemmEpi { EPI_F16 = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+struct GemmArgs {
+  int n_out;         // weight rows
+  int k;             // inner dim, multiple of 64
+  int batch;         // real batch rows
+  int bpad;          // padded batch rows of x, multiple of 16, <= 256
+  int bn;            // batch rows per CTA (MMA N); set by launch_gemm
+  int kb_per_split;  // 64-wide k blocks per split; set by launch_gemm
+  int nsplit;        // K splits; 0 = let launch_gemm choose
+  __half* y;         // [batch][ldy]; ldy % 8 == 0, 16-byte aligned
+  int ldy;
+  const __half* res;  // RESIDUAL: [batch][ldy]
+  float* ws;          // split accumulator [n_tiles*128][bpad], zero between launches
+  int* tickets;       // [n_tiles], zero before launch, left zero after
+  float* amax_val;    // ARGMAX partials [n_tiles][batch]
+  int* amax_idx;
+  int* err;
+};
+
+Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, cudaStream_t st);
+Status launch_argmax_finish(const float* val, const int* idx, int ntiles, int batch, int* token, cudaStream_t st);
+Status gemm_prepare();
+
+}  // namespace spock

@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm.h"
 
 namespace {
 constexpr int HID = 1024, INTER = 3584, DNH = 16, DND = 128, CONV = 6144, DN_IN = 6144 + 2048 + 32;
@@ -30,19 +31,6 @@ constexpr int QH = 8, KVH = 2, HD = 256, ATT_IN = QH * HD * 2 + 2 * KVH * HD;  /
 }  // namespace
 
 namespace spock {
-struct GemmArgs {
-  int n_out, k, batch, bpad, kb_per_split, nsplit;
-  __half* y;
-  int ldy;
-  const __half* res;
-  float* ws;
-  int* tickets;
-  float* amax_val;
-  int* amax_idx;
-  int* err;
-};
-Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, cudaStream_t st);
-Status launch_argmax_finish(const float* val, const int* idx, int ntiles, int batch, int* token, cudaStream_t st);
 Status launch_embed(const int* tokens, const void* emb, void* h, int batch, cudaStream_t st);
 Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batch, cudaStream_t st);
 Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* kn_w, const float* rope,
@@ -55,7 +43,6 @@ Status launch_decode_step_strided(const spock_dn_layer& L, int64_t batch, void* 
                                   void* conv_state, float* state, const void* a, const void* b, int ab_ld,
                                   const void* z, int z_ld, void* out, int out_ld, void* core_raw, int* err,
                                   cudaStream_t stream);
-enum { EPI_F16 = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 
 namespace {
 
