@@ -12,6 +12,10 @@
 
 namespace spock {
 std::atomic<uint64_t> g_launches{0};
+bool& pdl_enabled() {
+  static thread_local bool on = false;
+  return on;
+}
 
 Status launch_decode_step(const spock_dn_layer& L, int64_t batch, void* qkv, void* conv_state,
                           float* state, const void* a, const void* b, const void* z, void* out,

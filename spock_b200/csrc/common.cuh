@@ -44,6 +44,41 @@ inline Status cuda_status(cudaError_t e, const char* what) {
     if (_e != cudaSuccess) return spock::cuda_status(_e, what);    \
   } while (0)
 
+// ---- programmatic dependent launch -----------------------------------------
+// The decode step launches its kernels with programmatic stream serialisation
+// (pdl_scope), so a kernel's CTAs start while its predecessor drains. Every
+// kernel of the step therefore calls pdl_wait() before it reads what the
+// predecessor wrote or writes anything the predecessor may still read, and
+// pdl_launch() only after that wait (so each grid starts after everything
+// before its predecessor has completed). Outside a PDL launch both return at
+// once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: launches made by this thread while a pdl_scope is alive use PDL.
+bool& pdl_enabled();
+struct pdl_scope {
+  bool prev;
+  pdl_scope() : prev(pdl_enabled()) { pdl_enabled() = true; }
+  ~pdl_scope() { pdl_enabled() = prev; }
+};
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // ---- device helpers -------------------------------------------------------
 
 // IEEE arithmetic with contraction disabled, so per-element updates round

@@ -276,6 +276,8 @@ __global__ void __launch_bounds__(kThreads, 2) dn_decode_kernel(const __grid_con
   float4 S[kRowsPerWarp];
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r) S[r] = S4[(warp * kRowsPerWarp + r) * (kDim / 4) + lane];
+  pdl_wait();  // the state was last written by an earlier step; the token's inputs come from the predecessor
+  pdl_launch();
   auto sync = [] { __syncthreads(); };
   prologue<kFused>(A, m, s, h, threadIdx.x, sync, prologue_load<kFused>(A, s, h, threadIdx.x));
   update_and_output<kFused>(A, m, S, S4, s, h, threadIdx.x, sync);
@@ -314,6 +316,8 @@ __global__ void __launch_bounds__(2 * kThreads, 1)
     tc::fence_mbar_init();
     for (int j = 0; j < kStages && j < mine; ++j) issue(j);
   }
+  pdl_wait();  // the states were last written by an earlier step: their copies start before this
+  pdl_launch();
   __syncthreads();
   const int bar_id = 1 + grp;
   auto sync = [bar_id] { asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(kThreads) : "memory"); };
@@ -386,12 +390,12 @@ Status launch(const Args& A, int64_t batch, int* err, cudaStream_t stream) {
     auto kern = dn_decode_stream_kernel<kFused>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_status(e, "dn_decode_stream_kernel smem attribute");
-    kern<<<(unsigned)sms, 2 * kThreads, smem, stream>>>(A, (int)items, err);
+    launch_k(kern, dim3((unsigned)sms), dim3(2 * kThreads), smem, stream, A, (int)items, err);
     SPOCK_LAUNCH_CHECK(kFused ? "dn_decode_stream_kernel<fused>" : "dn_decode_stream_kernel<raw>");
     return Status::ok();
   }
   dim3 grid((unsigned)A.H, (unsigned)batch);
-  dn_decode_kernel<kFused><<<grid, kThreads, 0, stream>>>(A);
+  launch_k(dn_decode_kernel<kFused>, grid, dim3(kThreads), 0, stream, A);
   SPOCK_LAUNCH_CHECK(kFused ? "dn_decode_kernel<fused>" : "dn_decode_kernel<raw>");
   return Status::ok();
 }

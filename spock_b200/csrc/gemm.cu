@@ -101,9 +101,19 @@ __global__ void __launch_bounds__(128, 1)
   bool ok = true;
 
   if (warp == 0 && lane == 0) {  // TMA producer
-    for (int i = 0; i < nkb && ok; ++i) {
+    // The weights do not depend on the previous kernel: the first stages'
+    // weight tiles stream while it drains; activations after pdl_wait.
+    const int pre = nkb < kStages ? nkb : kStages;
+    for (int i = 0; i < pre; ++i) {
+      tc::mbar_arrive_expect_tx(&full[i], stage_bytes);
+      tma_load_2d(sm + i * stage_bytes, &tmw, &full[i], (kb0 + i) * 64, tile * 128);
+    }
+    pdl_wait();
+    pdl_launch();
+    for (int i = 0; i < pre; ++i) tma_load_2d(sm + i * stage_bytes + a_bytes, &tmx, &full[i], (kb0 + i) * 64, n0);
+    for (int i = pre; i < nkb && ok; ++i) {
       const int s = i % kStages;
-      if (i >= kStages) ok = wait_spin(&empty[s], ((i / kStages) - 1) & 1);
+      ok = wait_spin(&empty[s], ((i / kStages) - 1) & 1);
       if (!ok) break;
       uint8_t* st = sm + s * stage_bytes;
       tc::mbar_arrive_expect_tx(&full[s], stage_bytes);
@@ -128,6 +138,7 @@ __global__ void __launch_bounds__(128, 1)
     tc::mma_commit(done);
   }
   __syncwarp();
+  pdl_wait();  // the epilogue reads and writes what earlier kernels use
   // epilogue: all 128 threads; thread t <-> weight row tile*128 + t
   if (!wait_spin(done, 0)) ok = false;
   if (__syncthreads_or(!ok)) {
@@ -279,6 +290,8 @@ __global__ void __launch_bounds__(128, 1)
 __global__ void argmax_finish_kernel(const float* __restrict__ val, const int* __restrict__ idx, int ntiles,
                                      int batch, int* __restrict__ token) {
   const int b = blockIdx.x;
+  pdl_wait();
+  pdl_launch();
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
@@ -388,7 +401,7 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   }
 #define SPOCK_GEMM_CASE(E)                                                                          \
   case E: {                                                                                         \
-    gemm_swapab_kernel<E><<<grid, 128, smem, st>>>(mw, mx, a);                                      \
+    launch_k(gemm_swapab_kernel<E>, grid, dim3(128), smem, st, mw, mx, a);                          \
     break;                                                                                          \
   }
   switch (epi) {
@@ -416,7 +429,7 @@ Status gemm_prepare() {
 }
 
 Status launch_argmax_finish(const float* val, const int* idx, int ntiles, int batch, int* token, cudaStream_t st) {
-  argmax_finish_kernel<<<batch, 256, 0, st>>>(val, idx, ntiles, batch, token);
+  launch_k(argmax_finish_kernel, dim3(batch), dim3(256), 0, st, val, idx, ntiles, batch, token);
   SPOCK_LAUNCH_CHECK("argmax_finish_kernel");
   return Status::ok();
 }

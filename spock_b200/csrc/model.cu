@@ -48,6 +48,8 @@ namespace {
 
 __global__ void advance_kernel(int* pos, const int* tok_out, int* tok_in, int batch) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_launch();
   if (b < batch) {
     pos[b] += 1;
     tok_in[b] = tok_out[b];
@@ -152,6 +154,9 @@ Status gemm(spock_model* m, int epi, const void* x, const void* w, int n_out, in
 
 // One decode token for every sequence: tok_in -> tok_out, h holds the final normed hidden in x.
 Status record_step(spock_model* m, cudaStream_t st) {
+#ifndef SPOCK_NO_PDL
+  spock::pdl_scope pdl_on;  // every kernel of the step overlaps its predecessor's tail
+#endif
   const int B = m->batch;
   TRY(spock::launch_embed(m->tok_in, m->emb, m->h, B, st));
   const float eps = m->d.rms_eps;
@@ -183,7 +188,7 @@ Status record_step(spock_model* m, cudaStream_t st) {
   TRY(spock::launch_rmsnorm(m->h, m->final_norm, m->x, eps, B, st));
   TRY(gemm(m, spock::EPI_ARGMAX, m->x, m->emb, m->d.vocab, HID, nullptr, 0, nullptr, st));
   TRY(spock::launch_argmax_finish(m->amax_val, m->amax_idx, (m->d.vocab + 127) / 128, B, m->tok_out, st));
-  spock::advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(m->pos, m->tok_out, m->tok_in, B);
+  spock::launch_k(spock::advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, m->pos, m->tok_out, m->tok_in, B);
   SPOCK_LAUNCH_CHECK("advance_kernel");
   return Status::ok();
 }

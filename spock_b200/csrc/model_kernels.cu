@@ -22,6 +22,8 @@ constexpr int ROT = 64;
 __global__ void embed_kernel(const int* __restrict__ tokens, const uint4* __restrict__ emb, uint4* __restrict__ h,
                              int batch) {
   const int b = blockIdx.x;
+  pdl_wait();
+  pdl_launch();
   if (b >= batch) return;
   const int tok = tokens[b];
   for (int i = threadIdx.x; i < HID / 8; i += blockDim.x) h[(size_t)b * (HID / 8) + i] = emb[(size_t)tok * (HID / 8) + i];
@@ -31,6 +33,8 @@ __global__ void embed_kernel(const int* __restrict__ tokens, const uint4* __rest
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__ x, const __half* __restrict__ w,
                                                       __half* __restrict__ y, float eps, int batch) {
   const int b = blockIdx.x, t = threadIdx.x;
+  pdl_wait();
+  pdl_launch();
   if (b >= batch) return;
   __shared__ float s[256];
   const __half* xr = x + (size_t)b * HID;
@@ -63,6 +67,8 @@ __global__ void __launch_bounds__(256)
                      __half* __restrict__ gate_out, __half* __restrict__ kv /*[batch][layers][max_seq][2][KVH][HD]*/,
                      int64_t kv_seq_stride /*elements per sequence*/, int64_t kv_layer_off, float eps, float scale_unused) {
   const int hh = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  pdl_wait();
+  pdl_launch();
   const __half* row = qkv + (size_t)b * ld;
   __shared__ float s[256];
   __shared__ float sn[256];
@@ -112,6 +118,8 @@ __global__ void __launch_bounds__(256)
   const int kvh = blockIdx.x, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int G = QH / KVH;  // 4
+  pdl_wait();
+  pdl_launch();
   const int L = pos[b] + 1;
   float qv[G][8];
 #pragma unroll
@@ -206,13 +214,13 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 Status launch_embed(const int* tokens, const void* emb, void* h, int batch, cudaStream_t st) {
-  embed_kernel<<<batch, 128, 0, st>>>(tokens, (const uint4*)emb, (uint4*)h, batch);
+  launch_k(embed_kernel, dim3(batch), dim3(128), 0, st, tokens, (const uint4*)emb, (uint4*)h, batch);
   SPOCK_LAUNCH_CHECK("embed_kernel");
   return Status::ok();
 }
 
 Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batch, cudaStream_t st) {
-  rmsnorm_kernel<<<batch, 256, 0, st>>>((const __half*)x, (const __half*)w, (__half*)y, eps, batch);
+  launch_k(rmsnorm_kernel, dim3(batch), dim3(256), 0, st, (const __half*)x, (const __half*)w, (__half*)y, eps, batch);
   SPOCK_LAUNCH_CHECK("rmsnorm_kernel");
   return Status::ok();
 }
@@ -220,10 +228,9 @@ Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batc
 Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* kn_w, const float* rope,
                         const int* pos, void* q_out, void* gate_out, void* kv, int64_t kv_seq_stride,
                         int64_t kv_layer_off, float eps, int batch, cudaStream_t st) {
-  attn_prep_kernel<<<dim3(QH + KVH, batch), 256, 0, st>>>((const __half*)qkv, ld, (const __half*)qn_w,
-                                                           (const __half*)kn_w, rope, pos, (__half*)q_out,
-                                                           (__half*)gate_out, (__half*)kv, kv_seq_stride,
-                                                           kv_layer_off, eps, 0.f);
+  launch_k(attn_prep_kernel, dim3(QH + KVH, batch), dim3(256), 0, st, (const __half*)qkv, ld, (const __half*)qn_w,
+           (const __half*)kn_w, rope, pos, (__half*)q_out, (__half*)gate_out, (__half*)kv, kv_seq_stride,
+           kv_layer_off, eps, 0.f);
   SPOCK_LAUNCH_CHECK("attn_prep_kernel");
   return Status::ok();
 }
@@ -231,8 +238,8 @@ Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* k
 Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
                           int64_t kv_layer_off, const int* pos, float scale, void* out, int batch,
                           cudaStream_t st) {
-  attn_decode_kernel<<<dim3(KVH, batch), 256, 0, st>>>((const __half*)q, (const __half*)gate, (const __half*)kv,
-                                                        kv_seq_stride, kv_layer_off, pos, scale, (__half*)out);
+  launch_k(attn_decode_kernel, dim3(KVH, batch), dim3(256), 0, st, (const __half*)q, (const __half*)gate,
+           (const __half*)kv, kv_seq_stride, kv_layer_off, pos, scale, (__half*)out);
   SPOCK_LAUNCH_CHECK("attn_decode_kernel");
   return Status::ok();
 }
