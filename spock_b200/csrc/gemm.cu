@@ -286,6 +286,184 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) tc::tmem_dealloc(tb, ncols);
 }
 
+// ---- small batches (<= kGemvMaxB rows): CUDA-core weight streaming ---------
+// One warp per output unit (a weight row, or a gate/up row pair for SWIGLU):
+// lanes stream the row in 16-byte segments against the batch rows staged in
+// shared memory, fp32 accumulation, then a butterfly reduction. No partial
+// sums and no tensor-memory setup, which matters when the batch is tiny and
+// each projection is a few microseconds of HBM time.
+constexpr int kGemvMaxB = 8;
+constexpr int kGemvWarps = 8;
+
+__device__ __forceinline__ void fma8(float& acc, uint4 w, uint4 x) {
+  const __half2* wh = reinterpret_cast<const __half2*>(&w);
+  const __half2* xh = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 wf = __half22float2(wh[e]), xf = __half22float2(xh[e]);
+    acc = fmaf(wf.x, xf.x, acc);
+    acc = fmaf(wf.y, xf.y, acc);
+  }
+}
+
+template <int kEpi, int kB>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const uint4* __restrict__ W, const uint4* __restrict__ x,
+                                                               GemmArgs a, int units_per_cta, int wu) {
+  extern __shared__ uint4 xs[];  // [batch][k / 8]
+  __shared__ float r_val[kGemvWarps][kB];
+  __shared__ int r_idx[kGemvWarps][kB];
+  __shared__ float red[kGemvWarps * 32];
+  __shared__ float nfac;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int k8 = a.k / 8, B = a.batch;  // B <= kB
+  const int units = kEpi == EPI_SWIGLU ? a.n_out / 2 : a.n_out;
+  pdl_wait();
+  pdl_launch();
+  if (a.norm_w) {
+    // the rms_norm shader's arithmetic: 4 consecutive elements per thread,
+    // then the stride-128..1 tree (the last five levels as warp shuffles)
+    __half* xh = reinterpret_cast<__half*>(xs);
+    const __half* src = reinterpret_cast<const __half*>(x);
+    for (int b = 0; b < B; ++b) {
+      float v[4], acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[i] = __half2float(src[(size_t)b * a.k + t * 4 + i]);
+        acc = __fadd_rn(acc, __fmul_rn(v[i], v[i]));
+      }
+      red[t] = acc;
+      __syncthreads();
+      for (int stride = 128; stride >= 32; stride >>= 1) {
+        if (t < stride) red[t] = __fadd_rn(red[t], red[t + stride]);
+        __syncthreads();
+      }
+      if (t < 32) {
+        float sm = red[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_down_sync(0xffffffffu, sm, o));
+        if (t == 0) nfac = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sm, (float)a.k), a.eps)));
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float wv = __fadd_rn(1.0f, __half2float(a.norm_w[t * 4 + i]));
+        const __half y = __float2half_rn(__fmul_rn(__fmul_rn(v[i], nfac), wv));
+        xh[b * a.k + t * 4 + i] = y;
+        if (a.xnorm_out && blockIdx.x == 0) a.xnorm_out[(size_t)b * a.k + t * 4 + i] = y;
+      }
+    }
+  } else {
+    for (int i = t; i < B * k8; i += blockDim.x) xs[i] = x[i];
+  }
+  __syncthreads();
+  float bval[kB];
+  int bidx[kB];
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    bval[b] = -INFINITY;
+    bidx[b] = 0x7fffffff;
+  }
+  // wu warps per unit split its k range; groups of wu warps take units in turn
+  const int groups = kGemvWarps / wu, grp = warp / wu, sub = warp % wu;
+  const int u0 = blockIdx.x * units_per_cta, u1 = min(units, u0 + units_per_cta);
+  const int rounds = (units_per_cta + groups - 1) / groups;  // same for every warp: barriers below
+  for (int r = 0; r < rounds; ++r) {
+    const int u = u0 + r * groups + grp;
+    const bool live = u < u1;
+    // SWIGLU: unit u = feature; gate row (u/16)*32 + u%16, up row 16 further
+    const int row = kEpi == EPI_SWIGLU ? (u >> 4) * 32 + (u & 15) : u;
+    const uint4* wr = W + (size_t)row * k8;
+    float acc[kB], acc2[kB];
+#pragma unroll
+    for (int b = 0; b < kB; ++b) acc[b] = acc2[b] = 0.f;
+    if (live) {
+#pragma unroll 4
+      for (int c = lane + 32 * sub; c < k8; c += 32 * wu) {
+        const uint4 wv = __ldcs(wr + c);
+        uint4 wu4 = make_uint4(0, 0, 0, 0);
+        if constexpr (kEpi == EPI_SWIGLU) wu4 = __ldcs(wr + 16 * k8 + c);
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          if (b < B) {
+            const uint4 xv = xs[b * k8 + c];
+            fma8(acc[b], wv, xv);
+            if constexpr (kEpi == EPI_SWIGLU) fma8(acc2[b], wu4, xv);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], o);
+        if constexpr (kEpi == EPI_SWIGLU) acc2[b] += __shfl_xor_sync(0xffffffffu, acc2[b], o);
+      }
+    }
+    if (wu > 1) {  // sum the group's warps in order (the first warp of each group finishes)
+      if (lane == 0)
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          r_val[warp][b] = acc[b];
+          if constexpr (kEpi == EPI_SWIGLU) red[warp * kB + b] = acc2[b];
+        }
+      __syncthreads();
+      if (sub == 0 && lane == 0)
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          for (int w = 1; w < wu; ++w) {
+            acc[b] += r_val[warp + w][b];
+            if constexpr (kEpi == EPI_SWIGLU) acc2[b] += red[(warp + w) * kB + b];
+          }
+        }
+      __syncthreads();
+    }
+    if (live && sub == 0 && lane == 0) {
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        if (b >= B) continue;
+        const size_t off = (size_t)b * a.ldy + u;
+        if constexpr (kEpi == EPI_F16) {
+          a.y[off] = __float2half_rn(acc[b]);
+        } else if constexpr (kEpi == EPI_RESIDUAL) {
+          a.y[off] = __float2half_rn(__half2float(__float2half_rn(acc[b])) + __half2float(a.res[off]));
+        } else if constexpr (kEpi == EPI_SWIGLU) {
+          const float g16 = __half2float(__float2half_rn(acc[b]));
+          const float u16 = __half2float(__float2half_rn(acc2[b]));
+          const float silu = __fdiv_rn(g16, __fadd_rn(1.0f, expf(-g16)));
+          a.y[off] = __float2half_rn(__fmul_rn(silu, u16));
+        } else {  // ARGMAX: units visited in increasing order, so '>' keeps the lowest index
+          const float v = __half2float(__float2half_rn(acc[b]));
+          if (v > bval[b]) {
+            bval[b] = v;
+            bidx[b] = u;
+          }
+        }
+      }
+    }
+  }
+  if constexpr (kEpi == EPI_ARGMAX) {
+    if (lane == 0)
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        r_val[warp][b] = bval[b];
+        r_idx[warp][b] = bidx[b];
+      }
+    __syncthreads();
+    if (t < B) {
+      float v = r_val[0][t];
+      int i = r_idx[0][t];
+      for (int w = 1; w < kGemvWarps; ++w)
+        if (r_val[w][t] > v || (r_val[w][t] == v && r_idx[w][t] < i)) {
+          v = r_val[w][t];
+          i = r_idx[w][t];
+        }
+      a.amax_val[(size_t)blockIdx.x * B + t] = v;
+      a.amax_idx[(size_t)blockIdx.x * B + t] = i;
+    }
+  }
+}
+
 // token[b] = index of the largest fp16 logit, lowest index among equals.
 __global__ void argmax_finish_kernel(const float* __restrict__ val, const int* __restrict__ idx, int ntiles,
                                      int batch, int* __restrict__ token) {
@@ -368,6 +546,50 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
       return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: outputs and ldy must be multiples of 8, y/res 16-byte aligned");
   }
   const int ntiles = (a.n_out + 127) / 128, kbs = a.k / 64;
+  if (a.batch <= kGemvMaxB && (size_t)a.batch * a.k * 2 <= 96 * 1024) {
+    // ARGMAX keeps one partial per 128-row tile (what argmax_finish reads);
+    // the others spread their units over a few CTAs per SM
+    const int units = epi == EPI_SWIGLU ? a.n_out / 2 : a.n_out;
+    if (a.norm_w && a.k != kGemvWarps * 32 * 4)
+      return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: fused RMSNorm needs k == 1024");
+    int per = 128, wu = 1;
+    if (epi != EPI_ARGMAX) {
+      // enough warps in flight to stream the weights: split short unit lists' k
+      while (wu < kGemvWarps && units * wu < 16 * sms) wu *= 2;
+      const int groups = kGemvWarps / wu;
+      per = (units + 4 * sms - 1) / (4 * sms);
+      per = ((per + groups - 1) / groups) * groups;
+    }
+    const int grid = (units + per - 1) / per;
+    const size_t smem = (size_t)a.batch * a.k * 2;
+    const uint4* w4 = (const uint4*)w;
+    const uint4* x4 = (const uint4*)x;
+    cudaError_t e = cudaSuccess;
+    {
+      static std::once_flag once;
+      static Status prep;
+      std::call_once(once, [] { prep = gemm_prepare(); });
+      if (prep.code) return prep;
+    }
+    auto go = [&](auto kern) { e = launch_k(kern, dim3(grid), dim3(kGemvWarps * 32), smem, st, w4, x4, a, per, wu); };
+#define SPOCK_GEMV_B(E)                                     \
+  if (a.batch == 1) go(gemv_kernel<E, 1>);                  \
+  else if (a.batch == 2) go(gemv_kernel<E, 2>);             \
+  else if (a.batch <= 4) go(gemv_kernel<E, 4>);             \
+  else go(gemv_kernel<E, 8>);
+    switch (epi) {
+      case EPI_F16: SPOCK_GEMV_B(EPI_F16) break;
+      case EPI_RESIDUAL: SPOCK_GEMV_B(EPI_RESIDUAL) break;
+      case EPI_SWIGLU: SPOCK_GEMV_B(EPI_SWIGLU) break;
+      case EPI_ARGMAX: SPOCK_GEMV_B(EPI_ARGMAX) break;
+      default: return Status::err(SPOCK_ERR_INVALID, "gemm: unknown epilogue");
+    }
+#undef SPOCK_GEMV_B
+    if (e != cudaSuccess) return cuda_status(e, "gemv_kernel launch");
+    SPOCK_LAUNCH_CHECK("gemv_kernel");
+    return Status::ok();
+  }
+  if (a.norm_w) return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: fused RMSNorm only on the small-batch path");
   // batch blocks first (no partial sums), down to 64 rows
   int nb = 1;
   a.bn = a.bpad;
@@ -425,6 +647,17 @@ Status gemm_prepare() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int gsm = 96 * 1024;  // staged activations of the small-batch path
+#define SPOCK_GEMV_ATTR(E)                                                                                        \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<E, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm); \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<E, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm); \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<E, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm); \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<E, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm);
+  SPOCK_GEMV_ATTR(EPI_F16)
+  SPOCK_GEMV_ATTR(EPI_RESIDUAL)
+  SPOCK_GEMV_ATTR(EPI_SWIGLU)
+  SPOCK_GEMV_ATTR(EPI_ARGMAX)
+#undef SPOCK_GEMV_ATTR
   return cuda_status(e, "gemm_prepare");
 }
 

@@ -25,6 +25,12 @@ struct GemmArgs {
   float* amax_val;    // ARGMAX partials [n_tiles][batch]
   int* amax_idx;
   int* err;
+  // Small-batch path only: x is the residual stream h and the kernel applies
+  // RMSNorm (x * rsqrt(mean(x^2) + eps) * (1 + norm_w), k == 1024) itself;
+  // xnorm_out (nullable) receives the normed rows.
+  const __half* norm_w;
+  float eps;
+  __half* xnorm_out;
 };
 
 Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, cudaStream_t st);

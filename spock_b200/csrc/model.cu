@@ -128,8 +128,11 @@ int n_dn(const spock_model* m) { return (int)(m->d.num_layers - m->d.num_layers 
 int n_attn(const spock_model* m) { return (int)(m->d.num_layers / 4); }
 
 Status gemm(spock_model* m, int epi, const void* x, const void* w, int n_out, int k, void* y, int ldy,
-            const void* res, cudaStream_t st) {
+            const void* res, cudaStream_t st, const void* norm_w = nullptr, void* xnorm_out = nullptr) {
   spock::GemmArgs a{};
+  a.norm_w = (const __half*)norm_w;
+  a.eps = m->d.rms_eps;
+  a.xnorm_out = (__half*)xnorm_out;
   a.n_out = n_out;
   a.k = k;
   a.batch = m->batch;
@@ -160,10 +163,18 @@ Status record_step(spock_model* m, cudaStream_t st) {
   const int B = m->batch;
   TRY(spock::launch_embed(m->tok_in, m->emb, m->h, B, st));
   const float eps = m->d.rms_eps;
+  // RMSNorm then projection. Up to 8 rows the small-batch projection kernel
+  // normalises h itself (one launch instead of two).
+  const bool fuse = B <= 8;
+  auto normed = [&](int epi, const void* norm_w, const void* w, int n_out, void* y, int ldy,
+                    void* xnorm_out) -> Status {
+    if (fuse) return gemm(m, epi, m->h, w, n_out, HID, y, ldy, nullptr, st, norm_w, xnorm_out);
+    TRY(spock::launch_rmsnorm(m->h, norm_w, m->x, eps, B, st));
+    return gemm(m, epi, m->x, w, n_out, HID, y, ldy, nullptr, st);
+  };
   for (const auto& l : m->L) {
-    TRY(spock::launch_rmsnorm(m->h, l.input_norm, m->x, eps, B, st));
     if (!l.attn) {
-      TRY(gemm(m, spock::EPI_F16, m->x, l.w_in, DN_IN, HID, m->proj, DN_IN, nullptr, st));
+      TRY(normed(spock::EPI_F16, l.input_norm, l.w_in, DN_IN, m->proj, DN_IN, nullptr));
       spock_dn_layer dl{DNH, DND, DND, 4, l.conv_w, l.a_log_bias, l.dn_norm, eps, 0};
       __half* p = (__half*)m->proj;  // [batch][qkv 6144 | z 2048 | a 16 | b 16]
       // state and conv caches are [dn layer][sequence][...]
@@ -173,7 +184,7 @@ Status record_step(spock_model* m, cudaStream_t st) {
           p + CONV, DN_IN, m->mix, DNH * DND, nullptr, m->err_flag, st));
       TRY(gemm(m, spock::EPI_RESIDUAL, m->mix, l.w_out, HID, DNH * DND, m->h, HID, m->h, st));
     } else {
-      TRY(gemm(m, spock::EPI_F16, m->x, l.w_in, ATT_IN, HID, m->proj, ATT_IN, nullptr, st));
+      TRY(normed(spock::EPI_F16, l.input_norm, l.w_in, ATT_IN, m->proj, ATT_IN, nullptr));
       const int64_t layer_off = (int64_t)l.attn_idx * m->d.max_seq * 2 * KVH * HD;
       TRY(spock::launch_attn_prep(m->proj, ATT_IN, l.q_norm, l.k_norm, m->rope, m->pos, m->q, m->gate, m->kv,
                                   m->kv_seq_stride, layer_off, eps, B, st));
@@ -181,12 +192,10 @@ Status record_step(spock_model* m, cudaStream_t st) {
                                     m->mix, B, st));
       TRY(gemm(m, spock::EPI_RESIDUAL, m->mix, l.w_out, HID, QH * HD, m->h, HID, m->h, st));
     }
-    TRY(spock::launch_rmsnorm(m->h, l.post_norm, m->x, eps, B, st));
-    TRY(gemm(m, spock::EPI_SWIGLU, m->x, l.w_gu, 2 * INTER, HID, m->mlp, INTER, nullptr, st));
+    TRY(normed(spock::EPI_SWIGLU, l.post_norm, l.w_gu, 2 * INTER, m->mlp, INTER, nullptr));
     TRY(gemm(m, spock::EPI_RESIDUAL, m->mlp, l.w_down, HID, INTER, m->h, HID, m->h, st));
   }
-  TRY(spock::launch_rmsnorm(m->h, m->final_norm, m->x, eps, B, st));
-  TRY(gemm(m, spock::EPI_ARGMAX, m->x, m->emb, m->d.vocab, HID, nullptr, 0, nullptr, st));
+  TRY(normed(spock::EPI_ARGMAX, m->final_norm, m->emb, m->d.vocab, nullptr, 0, m->x));  // x: the normed hidden
   TRY(spock::launch_argmax_finish(m->amax_val, m->amax_idx, (m->d.vocab + 127) / 128, B, m->tok_out, st));
   spock::launch_k(spock::advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, m->pos, m->tok_out, m->tok_in, B);
   SPOCK_LAUNCH_CHECK("advance_kernel");
