@@ -294,6 +294,7 @@ __global__ void __launch_bounds__(128, 1)
 // each projection is a few microseconds of HBM time.
 constexpr int kGemvMaxB = 8;
 constexpr int kGemvWarps = 8;
+constexpr int kGemvChunks = 4;  // 16-byte weight segments per lane and unit: k <= 1024 * wu
 
 __device__ __forceinline__ void fma8(float& acc, uint4 w, uint4 x) {
   const __half2* wh = reinterpret_cast<const __half2*>(&w);
@@ -317,6 +318,33 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const uint4* __re
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int k8 = a.k / 8, B = a.batch;  // B <= kB
   const int units = kEpi == EPI_SWIGLU ? a.n_out / 2 : a.n_out;
+  float bval[kB];
+  int bidx[kB];
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    bval[b] = -INFINITY;
+    bidx[b] = 0x7fffffff;
+  }
+  // wu warps per unit split its k range; groups of wu warps take units in turn.
+  // Lane chunks c = lane + 32*sub + 32*wu*i (i < kGemvChunks) cover the row.
+  const int groups = kGemvWarps / wu, grp = warp / wu, sub = warp % wu;
+  const int u0 = blockIdx.x * units_per_cta, u1 = min(units, u0 + units_per_cta);
+  const int rounds = (units_per_cta + groups - 1) / groups;  // same for every warp: barriers below
+  auto unit_of = [&](int r) { return u0 + r * groups + grp; };
+  auto load_w = [&](int r, uint4 (&w)[kGemvChunks], uint4 (&w2)[kGemvChunks]) {
+    const int u = unit_of(r);
+    const int row = kEpi == EPI_SWIGLU ? (u >> 4) * 32 + (u & 15) : u;
+    const uint4* wr = W + (size_t)row * k8;
+#pragma unroll
+    for (int i = 0; i < kGemvChunks; ++i) {
+      const int c = lane + 32 * (sub + wu * i);
+      const bool in = u < u1 && c < k8;
+      w[i] = in ? __ldcs(wr + c) : make_uint4(0, 0, 0, 0);
+      if constexpr (kEpi == EPI_SWIGLU) w2[i] = in ? __ldcs(wr + 16 * k8 + c) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint4 wc[kGemvChunks], wc2[kGemvChunks];
+  load_w(0, wc, wc2);  // (issued before the activations are staged)
   pdl_wait();
   pdl_launch();
   if (a.norm_w) {
@@ -356,41 +384,32 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const uint4* __re
     for (int i = t; i < B * k8; i += blockDim.x) xs[i] = x[i];
   }
   __syncthreads();
-  float bval[kB];
-  int bidx[kB];
-#pragma unroll
-  for (int b = 0; b < kB; ++b) {
-    bval[b] = -INFINITY;
-    bidx[b] = 0x7fffffff;
-  }
-  // wu warps per unit split its k range; groups of wu warps take units in turn
-  const int groups = kGemvWarps / wu, grp = warp / wu, sub = warp % wu;
-  const int u0 = blockIdx.x * units_per_cta, u1 = min(units, u0 + units_per_cta);
-  const int rounds = (units_per_cta + groups - 1) / groups;  // same for every warp: barriers below
   for (int r = 0; r < rounds; ++r) {
-    const int u = u0 + r * groups + grp;
+    const int u = unit_of(r);
     const bool live = u < u1;
-    // SWIGLU: unit u = feature; gate row (u/16)*32 + u%16, up row 16 further
-    const int row = kEpi == EPI_SWIGLU ? (u >> 4) * 32 + (u & 15) : u;
-    const uint4* wr = W + (size_t)row * k8;
+    uint4 wn[kGemvChunks], wn2[kGemvChunks];
+    if (r + 1 < rounds) load_w(r + 1, wn, wn2);  // next round's weights fly during this one
     float acc[kB], acc2[kB];
 #pragma unroll
     for (int b = 0; b < kB; ++b) acc[b] = acc2[b] = 0.f;
-    if (live) {
-#pragma unroll 4
-      for (int c = lane + 32 * sub; c < k8; c += 32 * wu) {
-        const uint4 wv = __ldcs(wr + c);
-        uint4 wu4 = make_uint4(0, 0, 0, 0);
-        if constexpr (kEpi == EPI_SWIGLU) wu4 = __ldcs(wr + 16 * k8 + c);
+#pragma unroll
+    for (int i = 0; i < kGemvChunks; ++i) {
+      const int c = lane + 32 * (sub + wu * i);
+      if (c < k8) {
 #pragma unroll
         for (int b = 0; b < kB; ++b) {
           if (b < B) {
             const uint4 xv = xs[b * k8 + c];
-            fma8(acc[b], wv, xv);
-            if constexpr (kEpi == EPI_SWIGLU) fma8(acc2[b], wu4, xv);
+            fma8(acc[b], wc[i], xv);
+            if constexpr (kEpi == EPI_SWIGLU) fma8(acc2[b], wc2[i], xv);
           }
         }
       }
+    }
+#pragma unroll
+    for (int i = 0; i < kGemvChunks; ++i) {
+      wc[i] = wn[i];
+      if constexpr (kEpi == EPI_SWIGLU) wc2[i] = wn2[i];
     }
 #pragma unroll
     for (int b = 0; b < kB; ++b) {
@@ -550,12 +569,15 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     // ARGMAX keeps one partial per 128-row tile (what argmax_finish reads);
     // the others spread their units over a few CTAs per SM
     const int units = epi == EPI_SWIGLU ? a.n_out / 2 : a.n_out;
+    if (a.k > 1024 * kGemvWarps || (epi == EPI_ARGMAX && a.k > 1024))
+      return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: small-batch path needs k <= 8192 (ARGMAX: 1024)");
     if (a.norm_w && a.k != kGemvWarps * 32 * 4)
       return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: fused RMSNorm needs k == 1024");
     int per = 128, wu = 1;
     if (epi != EPI_ARGMAX) {
       // enough warps in flight to stream the weights: split short unit lists' k
       while (wu < kGemvWarps && units * wu < 16 * sms) wu *= 2;
+      while (wu < kGemvWarps && a.k > 1024 * wu) wu *= 2;  // kGemvChunks segments per lane
       const int groups = kGemvWarps / wu;
       per = (units + 4 * sms - 1) / (4 * sms);
       per = ((per + groups - 1) / groups) * groups;
