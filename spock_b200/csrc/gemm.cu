@@ -9,7 +9,7 @@
 // Accumulators live in TMEM (lane = weight row, column = batch row).
 //
 // Grid: (row tiles, K splits, batch blocks). Large batches are split over
-// batch blocks of bn >= 64 rows first (no partial sums: the CTAs of one row
+// batch blocks of bn >= 32 rows first (no partial sums: the CTAs of one row
 // tile share its weight slab through L2), then over K: with K splits every
 // CTA adds its fp32 partial tile into an accumulator with vector atomics
 // (L2-side, all splits in parallel); the last CTA of a tile (atomic ticket)
@@ -39,7 +39,8 @@ namespace spock {
 
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kMaxStages = 4;
+constexpr int kRingBytes = kMaxStages * (128 * 128 + 256 * 128);
 constexpr uint32_t kWaitLimit = 1u << 25;
 
 __device__ __forceinline__ bool wait_spin(uint64_t* bar, uint32_t parity) {
@@ -65,13 +66,12 @@ __global__ void __launch_bounds__(128, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   const int a_bytes = 128 * 128, b_bytes = a.bn * 128, stage_bytes = a_bytes + b_bytes;
+  const int kStages = a.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * stage_bytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* done = empty + kStages;
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* done = empty + kMaxStages;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(done + 1);
   int* s_last = reinterpret_cast<int*>(s_tmem + 1);
-  float* s_red = reinterpret_cast<float*>(s_last + 1);  // ARGMAX: [4 warps][256] vals, then idx
-  int* s_redi = reinterpret_cast<int*>(s_red + 4 * 256);
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int tile = blockIdx.x, split = blockIdx.y, n0 = blockIdx.z * a.bn;
@@ -218,40 +218,31 @@ __global__ void __launch_bounds__(128, 1)
             stg[(c0 + k) * width + feat] = __float2half_rn(__fmul_rn(silu, u16));
           }
         }
-      } else {  // EPI_ARGMAX: per batch column, max fp16 logit over the tile's rows, lowest index on ties
-        for (int k = 0; k < 32; ++k) {
-          const int b = n0 + c0 + k;
-          float val = (row < a.n_out) ? __half2float(__float2half_rn(v[k])) : -INFINITY;
-          int idx = (row < a.n_out) ? row : 0x7fffffff;
+      } else {  // EPI_ARGMAX: fp16 logits staged; rows past n_out as -inf
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, val, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (ov > val || (ov == val && oi < idx)) {
-              val = ov;
-              idx = oi;
-            }
-          }
-          if (lane == 0 && c0 + k < a.bn) {
-            s_red[warp * 256 + b] = val;
-            s_redi[warp * 256 + b] = idx;
-          }
-        }
+        for (int k = 0; k < 32; ++k)
+          if (c0 + k < a.bn) stg[(c0 + k) * width + t] = row < a.n_out ? __float2half_rn(v[k]) : __ushort_as_half(0xfc00);
       }
     }
     __syncthreads();
     if constexpr (kEpi == EPI_ARGMAX) {
+      // per batch column: max over the tile's 128 rows in row order ('>' keeps the lowest index)
       for (int bl = t; bl < a.bn; bl += 128) {
         const int b = n0 + bl;
         if (b >= a.batch) continue;
-        float val = s_red[b];
-        int idx = s_redi[b];
-        for (int w = 1; w < 4; ++w) {
-          const float ov = s_red[w * 256 + b];
-          const int oi = s_redi[w * 256 + b];
-          if (ov > val || (ov == val && oi < idx)) {
-            val = ov;
-            idx = oi;
+        const uint4* col = reinterpret_cast<const uint4*>(stg + bl * width);
+        float val = -INFINITY;
+        int idx = 0x7fffffff;
+        for (int c = 0; c < width / 8; ++c) {
+          const uint4 u = col[c];
+          const __half* hv = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float f = __half2float(hv[e]);
+            if (f > val) {
+              val = f;
+              idx = tile * 128 + 8 * c + e;
+            }
           }
         }
         a.amax_val[(size_t)tile * a.batch + b] = val;
@@ -612,10 +603,10 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     return Status::ok();
   }
   if (a.norm_w) return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: fused RMSNorm only on the small-batch path");
-  // batch blocks first (no partial sums), down to 64 rows
+  // batch blocks first (no partial sums), down to 32 rows
   int nb = 1;
   a.bn = a.bpad;
-  while (ntiles * nb < sms && a.bn % 32 == 0 && a.bn / 2 >= 64) {
+  while (ntiles * nb < sms && a.bn % 32 == 0 && a.bn / 2 >= 32) {
     a.bn /= 2;
     nb *= 2;
   }
@@ -624,6 +615,7 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   if (s.code) return s;
   s = map2d(&mx, x, a.bpad, a.k, a.bn);
   if (s.code) return s;
+  if (a.nsplit < 1 && nb > 1) a.nsplit = 1;  // large batch: compute-heavy tiles, no partial sums
   if (a.nsplit < 1) {  // enough CTAs to stream the weights from every SM ...
     int want = (sms + ntiles * nb - 1) / (ntiles * nb);
     // ... but no more partial-tile traffic (128 x bn fp32) than weight traffic
@@ -635,7 +627,9 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   a.kb_per_split = (kbs + a.nsplit - 1) / a.nsplit;
   a.nsplit = (kbs + a.kb_per_split - 1) / a.kb_per_split;
   if (a.nsplit > 1 && (!a.ws || !a.tickets)) return Status::err(SPOCK_ERR_INVALID, "gemm: split-K needs a workspace");
-  const int smem = kStages * (128 * 128 + a.bn * 128) + 64 + 8 * 256 * 4 + 1024;
+  // Four stages: deeper rings cost CTAs per SM, which these short K loops need more.
+  a.stages = kMaxStages;
+  const int smem = a.stages * (128 * 128 + a.bn * 128) + 2 * kMaxStages * 8 + 64 + 8 * 256 * 4 + 1024;
   dim3 grid(ntiles, a.nsplit, nb);
   {
     static std::once_flag once;
@@ -663,7 +657,7 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
 
 // Sets every GEMM variant's shared-memory limit once (before any graph capture).
 Status gemm_prepare() {
-  const int smem = kStages * (128 * 128 + 256 * 128) + 64 + 8 * 256 * 4 + 1024;
+  const int smem = kRingBytes + 2 * kMaxStages * 8 + 64 + 8 * 256 * 4 + 1024;
   cudaError_t e = cudaSuccess;
   e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

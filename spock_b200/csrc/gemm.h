@@ -17,6 +17,7 @@ struct GemmArgs {
   int bn;            // batch rows per CTA (MMA N); set by launch_gemm
   int kb_per_split;  // 64-wide k blocks per split; set by launch_gemm
   int nsplit;        // K splits; 0 = let launch_gemm choose
+  int stages;        // TMA ring depth; set by launch_gemm
   __half* y;         // [batch][ldy]; ldy % 8 == 0, 16-byte aligned
   int ldy;
   const __half* res;  // RESIDUAL: [batch][ldy]
