@@ -285,16 +285,28 @@ def bench_decode(args, ws, rank, local):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # The step's launches are captured once into a CUDA graph (as the model
+    # session does), so a small batch measures the kernels, not the Python
+    # and ctypes cost of issuing them.
+    graph = torch.cuda.CUDAGraph()
     n0 = spock_b200.lib().spock_kernel_launch_count()
+    with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+        stream = torch.cuda.current_stream()
+        step()
+    per_step = spock_b200.lib().spock_kernel_launch_count() - n0
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
     barrier(ws)
     with ClockSampler(local) as clk:
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for _ in range(args.steps):
-            step()
+            graph.replay()
         t1.record(stream)
         torch.cuda.synchronize()
-    launches = spock_b200.lib().spock_kernel_launch_count() - n0
+    launches = per_step * args.steps
     ms = max_over_ranks(t0.elapsed_time(t1), ws) / args.steps
     per_launch_ms = ms / layers
     value = B * layers * ws / (ms / 1e3)  # sequence-layer steps per second
