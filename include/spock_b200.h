@@ -50,6 +50,13 @@ const char* spock_last_error(const spock_ctx* ctx);
 int spock_sync(spock_ctx* ctx, void* stream);
 /* Number of kernels this library has launched since load (diagnostics). */
 uint64_t spock_kernel_launch_count(void);
+/* Failure-detection self-test: launches one CTA that waits on a device
+ * barrier nothing will complete, with the same bounded polling the chunk,
+ * decode and projection kernels use, capped at `polls` polls. The wait gives
+ * up, records the timeout in the context's error word and the kernel returns,
+ * so the next spock_sync reports SPOCK_ERR_TIMEOUT and the context stays
+ * usable. No GPU fault is involved. */
+int spock_selftest_wait_timeout(spock_ctx* ctx, uint32_t polls, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Chunked gated delta rule (prefill).                                      */

@@ -34,7 +34,7 @@ SPOCK_ERR_TIMEOUT = -5
 F32, F16, BF16 = 0, 1, 2
 
 EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
-            "spock_kernel_launch_count", "spock_chunk_prefill", "spock_chunk_last_to_fp16",
+            "spock_kernel_launch_count", "spock_selftest_wait_timeout", "spock_chunk_prefill", "spock_chunk_last_to_fp16",
             "spock_deltanet_decode_step", "spock_deltanet_recurrent", "spock_chunk_prefill_noalloc",
             "spock_model_create", "spock_model_destroy", "spock_model_last_error", "spock_model_set_weight",
             "spock_model_reset", "spock_model_step", "spock_model_generate"]
@@ -84,6 +84,7 @@ def lib():
         L.spock_last_error.restype = ctypes.c_char_p
         L.spock_sync.argtypes = [vp, vp]
         L.spock_kernel_launch_count.restype = ctypes.c_uint64
+        L.spock_selftest_wait_timeout.argtypes = [vp, ctypes.c_uint32, vp]
         L.spock_chunk_prefill.argtypes = [vp, ctypes.POINTER(ChunkDesc)] + [vp] * 9
         L.spock_chunk_prefill_noalloc.argtypes = [ctypes.POINTER(ChunkDesc)] + [vp] * 9
         L.spock_chunk_last_to_fp16.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp]
@@ -135,6 +136,11 @@ class Context:
 
     def sync(self, stream=None):
         self.check(lib().spock_sync(self.h, _stream(stream)))
+
+    def selftest_wait_timeout(self, polls=256, stream=None):
+        """Launches the failure-detection self-test (a bounded device wait that
+        must give up); the following sync() raises SpockError(SPOCK_ERR_TIMEOUT)."""
+        self.check(lib().spock_selftest_wait_timeout(self.h, int(polls), _stream(stream)))
 
     def close(self):
         if self.h:

@@ -29,6 +29,7 @@ Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, co
                             cudaStream_t stream);
 Status launch_last_to_fp16(int64_t batch, int64_t H, int64_t S, int64_t V, const float* core,
                            void* out, cudaStream_t stream);
+Status launch_wait_timeout_selftest(uint32_t polls, int* err, cudaStream_t stream);
 }  // namespace spock
 
 struct spock_ctx {
@@ -134,6 +135,14 @@ __attribute__((visibility("default"))) const char* spock_last_error(const spock_
 
 __attribute__((visibility("default"))) uint64_t spock_kernel_launch_count(void) {
   return spock::g_launches.load();
+}
+
+__attribute__((visibility("default"))) int spock_selftest_wait_timeout(spock_ctx* ctx, uint32_t polls, void* stream) {
+  if (!ctx) return fail(nullptr, SPOCK_ERR_INVALID, "spock_selftest_wait_timeout: ctx is NULL");
+  if (polls == 0 || polls > (1u << 20))
+    return fail(ctx, SPOCK_ERR_INVALID, "spock_selftest_wait_timeout: polls must be in [1, 2^20]");
+  DeviceGuard g(ctx->device);
+  return finish(ctx, spock::launch_wait_timeout_selftest(polls, ctx->d_err_flag, (cudaStream_t)stream));
 }
 
 __attribute__((visibility("default"))) int spock_sync(spock_ctx* ctx, void* stream) {

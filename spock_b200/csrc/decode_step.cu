@@ -369,6 +369,20 @@ __global__ void __launch_bounds__(2 * kThreads, 1)
   }
 }
 
+// Failure-detection self-test: the bounded mbarrier wait of the kernels above
+// on a barrier that never completes. It gives up after `polls` polls, records
+// code 5 in *err and returns; nothing faults.
+__global__ void wait_timeout_selftest_kernel(uint32_t polls, int* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = tc::mbar_wait_bounded(&bar, 0, polls);
+  if (__syncthreads_or(!ok) && threadIdx.x == 0) atomicExch(err, 5);
+}
+
 Args make_args(int H, float eps) {
   Args a{};
   a.H = H;
@@ -401,6 +415,12 @@ Status launch(const Args& A, int64_t batch, int* err, cudaStream_t stream) {
 }
 
 }  // namespace
+
+Status launch_wait_timeout_selftest(uint32_t polls, int* err, cudaStream_t stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(polls, err);
+  SPOCK_LAUNCH_CHECK("wait_timeout_selftest_kernel");
+  return Status::ok();
+}
 
 Status launch_decode_step_strided(const spock_dn_layer& L, int64_t batch, void* qkv, int qkv_ld,
                                   void* conv_state, float* state, const void* a, const void* b, int ab_ld,
