@@ -211,6 +211,13 @@ const char* spock_model_last_error(const spock_model* m);
  * find_by_role: "embedding", "final_norm", "layer.N.delta_in_proj_qkv", ...);
  * host pointer, fp16 unless the role is fp32 in the artifact. */
 int spock_model_set_weight(spock_model* m, const char* role, const void* host, size_t bytes);
+/* Loads every tensor the model needs from a repacked text artifact directory
+ * (text_repack_manifest.json + text_weights.bin, the format
+ * src/runtime/weight_loader.cpp:22-57 reads): role_path "global.token_embedding",
+ * "global.final_norm" and "layer.N.<role>". SPOCK_ERR_INVALID names missing,
+ * duplicate or mistyped roles. Replaces WeightArtifact::load + the per-role
+ * uploads of DecodeSession (vk_session.cpp:1151-1462). */
+int spock_model_load_artifact(spock_model* m, const char* repack_dir);
 /* Zeroes DeltaNet/conv/KV state and positions for `batch` sequences
  * (DecodeSession::reset, vk_session.cpp:980). */
 int spock_model_reset(spock_model* m, int32_t batch);

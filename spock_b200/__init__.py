@@ -37,7 +37,7 @@ EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
             "spock_kernel_launch_count", "spock_selftest_wait_timeout", "spock_chunk_prefill", "spock_chunk_last_to_fp16",
             "spock_deltanet_decode_step", "spock_deltanet_recurrent", "spock_chunk_prefill_noalloc",
             "spock_model_create", "spock_model_destroy", "spock_model_last_error", "spock_model_set_weight",
-            "spock_model_reset", "spock_model_step", "spock_model_generate"]
+            "spock_model_reset", "spock_model_step", "spock_model_generate", "spock_model_load_artifact"]
 
 
 class SpockError(RuntimeError):
@@ -310,6 +310,7 @@ def _model_lib():
         L.spock_model_last_error.argtypes = [vp]
         L.spock_model_last_error.restype = ctypes.c_char_p
         L.spock_model_set_weight.argtypes = [vp, ctypes.c_char_p, vp, ctypes.c_size_t]
+        L.spock_model_load_artifact.argtypes = [vp, ctypes.c_char_p]
         L.spock_model_reset.argtypes = [vp, ctypes.c_int32]
         L.spock_model_step.argtypes = [vp, vp, vp, vp, vp]
         L.spock_model_generate.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, vp, vp]
@@ -343,6 +344,10 @@ class Model:
         for role, arr in weights.items():
             arr = np.ascontiguousarray(arr)
             self._check(self.L.spock_model_set_weight(self.h, role.encode(), arr.ctypes.data, arr.nbytes))
+
+    def load_artifact(self, repack_dir):
+        """Loads a repacked text artifact (text_repack_manifest.json + text_weights.bin)."""
+        self._check(self.L.spock_model_load_artifact(self.h, os.fsencode(repack_dir)))
 
     def reset(self, batch):
         self.batch = batch

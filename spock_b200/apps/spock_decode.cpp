@@ -2,9 +2,10 @@
 // over libspock_b200's model session. Same flags where they apply (--tokens
 // FILE, --max-new-tokens N, --verbose, --help) and the same JSON keys
 // (prompt_tokens, generated_tokens, generated_count, elapsed_ms, prefill_ms,
-// decode_ms). No checkpoint exists on this machine, so weights are a seeded
-// random init of the Qwen3.5-0.8B layout (--seed, --layers, --vocab);
-// --repack-dir is reported as unsupported.
+// decode_ms). Weights come from a repacked text artifact (--repack-dir, the
+// reference's text_repack_manifest.json + text_weights.bin) or, when none is
+// given, from a seeded random init of the Qwen3.5-0.8B layout (--seed,
+// --layers, --vocab).
 #include <chrono>
 #include <fstream>
 #include <iostream>
@@ -13,7 +14,7 @@
 #include "model_common.h"
 
 int main(int argc, char** argv) {
-  std::string token_file;
+  std::string token_file, repack_dir;
   int max_new = 16, layers = 24, vocab = 248320;
   uint64_t seed = 0;
   bool verbose = false;
@@ -25,12 +26,9 @@ int main(int argc, char** argv) {
     else if (a == "--vocab" && i + 1 < argc) vocab = std::stoi(argv[++i]);
     else if (a == "--seed" && i + 1 < argc) seed = std::stoull(argv[++i]);
     else if (a == "--verbose" || a == "-v") verbose = true;
-    else if (a == "--repack-dir" && i + 1 < argc) {
-      ++i;
-      std::cout << "{\n  \"error\": \"--repack-dir: artifact loading is not implemented in spock_b200; weights are random-init\"\n}\n";
-      return 1;
-    } else if (a == "--help") {
-      std::cout << "usage: spock-decode --tokens FILE [--max-new-tokens N] [--layers N] [--vocab N] [--seed S]\n";
+    else if (a == "--repack-dir" && i + 1 < argc) repack_dir = argv[++i];
+    else if (a == "--help") {
+      std::cout << "usage: spock-decode --tokens FILE [--max-new-tokens N] [--repack-dir DIR] [--layers N] [--vocab N] [--seed S]\n";
       return 0;
     }
   }
@@ -56,7 +54,11 @@ int main(int argc, char** argv) {
     if (spock_create(0, &ctx) != SPOCK_OK) throw std::runtime_error(spock_last_error(nullptr));
     spock_model_desc d{layers, vocab, 1, (int32_t)(prompt.size() + max_new + 8), 1e-6f, 1e7f};
     if (spock_model_create(ctx, &d, &m) != SPOCK_OK) throw std::runtime_error("spock_model_create failed");
-    app::random_init(m, layers, vocab, seed);
+    if (!repack_dir.empty()) {
+      if (spock_model_load_artifact(m, repack_dir.c_str()) != SPOCK_OK) throw std::runtime_error(spock_model_last_error(m));
+    } else {
+      app::random_init(m, layers, vocab, seed);
+    }
     if (verbose) std::cerr << "spock-decode: weights uploaded\n";
     spock_model_reset(m, 1);
     cudaStream_t st;
@@ -95,7 +97,8 @@ int main(int argc, char** argv) {
     for (int i = 0; i < max_new; ++i) std::cout << (i ? ", " : "") << gen[i];
     std::cout << "],\n  \"generated_count\": " << max_new << ",\n  \"elapsed_ms\": " << elapsed
               << ",\n  \"prefill_ms\": " << prefill_ms << ",\n  \"decode_ms\": " << decode_ms
-              << ",\n  \"weights\": \"random-init (seed " << seed << ")\"\n}\n";
+              << ",\n  \"weights\": \"" << (repack_dir.empty() ? "random-init (seed " + std::to_string(seed) + ")" : repack_dir)
+              << "\"\n}\n";
     cudaFree(dp);
     cudaFree(dout);
     cudaFree(dtok);

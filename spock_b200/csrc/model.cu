@@ -22,6 +22,7 @@
 #include <string>
 #include <vector>
 
+#include "../apps/json_min.h"
 #include "common.cuh"
 #include "gemm.h"
 
@@ -407,6 +408,82 @@ __attribute__((visibility("default"))) int spock_model_set_weight(spock_model* m
     if (n == "attn_o") return put(l.w_out, (size_t)HID * QH * HD * 2);
   }
   return mfail(m, SPOCK_ERR_INVALID, "unknown role " + r);
+}
+
+// Loads the reference's repacked text artifact: <dir>/text_repack_manifest.json
+// (written by tools/repack_text_weights.py:178-230, read by
+// src/runtime/weight_loader.cpp:22-57) and its aligned blob. Each tensor record
+// gives role_path, offset, nbytes and dtype; "global.token_embedding" and
+// "global.final_norm" are the embedding and final norm, "layer.N.<role>" the
+// per-layer roles above. Every role the model needs must appear exactly once.
+__attribute__((visibility("default"))) int spock_model_load_artifact(spock_model* m, const char* dir) {
+  if (!m || !dir) return SPOCK_ERR_INVALID;
+  const std::string root(dir);
+  jm::Value man;
+  try {
+    man = jm::read_file(root + "/text_repack_manifest.json");
+  } catch (const std::exception& e) {
+    return mfail(m, SPOCK_ERR_INVALID, std::string("artifact manifest: ") + e.what());
+  }
+  std::string blob = "text_weights.bin";
+  if (const jm::Value* pk = man.get("packing"))
+    if (const jm::Value* wf = pk->get("weights_file"))
+      if (wf->kind == jm::Value::String) blob = wf->str;
+  const jm::Value* tensors = man.get("tensors");
+  if (!tensors || tensors->kind != jm::Value::Array) return mfail(m, SPOCK_ERR_INVALID, "artifact manifest: no tensors array");
+  std::ifstream f(root + "/" + blob, std::ios::binary);
+  if (!f) return mfail(m, SPOCK_ERR_INVALID, "artifact: cannot open " + blob);
+  // the roles this model needs
+  std::map<std::string, int> need;
+  need["embedding"] = 0;
+  need["final_norm"] = 0;
+  for (int i = 0; i < m->d.num_layers; ++i) {
+    const std::string p = "layer." + std::to_string(i) + ".";
+    for (const char* r : {"input_norm", "post_norm", "mlp_gate", "mlp_up", "mlp_down"}) need[p + r] = 0;
+    if (m->L[i].attn) {
+      for (const char* r : {"attn_q", "attn_k", "attn_v", "attn_q_norm", "attn_k_norm", "attn_o"}) need[p + r] = 0;
+    } else {
+      for (const char* r : {"delta_in_proj_qkv", "delta_in_proj_z", "delta_in_proj_a", "delta_in_proj_b", "delta_conv",
+                            "delta_norm", "delta_a_log", "delta_dt_bias", "delta_out_proj"})
+        need[p + r] = 0;
+    }
+  }
+  std::vector<char> buf;
+  for (const auto& t : tensors->arr) {
+    const jm::Value *rp = t.get("role_path"), *off = t.get("offset"), *nb = t.get("nbytes"), *dt = t.get("dtype");
+    if (!rp || rp->kind != jm::Value::String || !off || !nb || off->kind != jm::Value::Number ||
+        nb->kind != jm::Value::Number)
+      return mfail(m, SPOCK_ERR_INVALID, "artifact manifest: tensor record without role_path/offset/nbytes");
+    std::string role = rp->str;
+    if (role == "global.token_embedding") role = "embedding";
+    else if (role == "global.final_norm") role = "final_norm";
+    auto it = need.find(role);
+    if (it == need.end()) continue;  // roles this model does not use (e.g. other modalities)
+    if (it->second++) return mfail(m, SPOCK_ERR_INVALID, "artifact: duplicate role " + rp->str);
+    const bool f32_role = role.size() > 10 && (role.compare(role.size() - 10, 10, "delta_norm") == 0 ||
+                                               role.compare(role.size() - 11, 11, "delta_a_log") == 0);
+    if (dt && dt->kind == jm::Value::String) {
+      const bool is32 = dt->str == "fp32" || dt->str == "float32" || dt->str == "f32";
+      const bool is16 = dt->str == "fp16" || dt->str == "float16" || dt->str == "f16";
+      if (!(f32_role ? is32 : is16))
+        return mfail(m, SPOCK_ERR_INVALID, "artifact: " + rp->str + " has dtype " + dt->str);
+    }
+    const uint64_t o = (uint64_t)off->num, n = (uint64_t)nb->num;
+    buf.resize(n);
+    f.seekg((std::streamoff)o);
+    f.read(buf.data(), (std::streamsize)n);
+    if (!f) return mfail(m, SPOCK_ERR_INVALID, "artifact: short read for " + rp->str);
+    const int rc = spock_model_set_weight(m, role.c_str(), buf.data(), n);
+    if (rc != SPOCK_OK) return rc;
+  }
+  std::string missing;
+  int n_missing = 0;
+  for (const auto& kv : need)
+    if (!kv.second) {
+      if (n_missing++ < 4) missing += (missing.empty() ? "" : ", ") + kv.first;
+    }
+  if (n_missing) return mfail(m, SPOCK_ERR_INVALID, "artifact: " + std::to_string(n_missing) + " roles missing (" + missing + (n_missing > 4 ? ", ..." : "") + ")");
+  return SPOCK_OK;
 }
 
 // Zeroes recurrent state, conv and KV caches and positions for `batch` sequences.

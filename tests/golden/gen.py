@@ -128,3 +128,34 @@ def model_weights(layers=24, vocab=248320, seed=0):
             w[p + "delta_dt_bias"] = vec16(16)
             w[p + "delta_out_proj"] = mat(1024, 2048)
     return w
+
+
+def write_repack_artifact(path, weights, drop=(), alignment=256):
+    """Writes `weights` (role -> array) as a repacked text artifact in the format
+    the reference's tools/repack_text_weights.py produces and
+    src/runtime/weight_loader.cpp reads: text_weights.bin with each tensor at an
+    `alignment`-aligned offset, and text_repack_manifest.json listing role_path,
+    offset, nbytes, dtype and shape. Roles in `drop` are left out."""
+    import json
+    import os
+    os.makedirs(path, exist_ok=True)
+    tensors, off = [], 0
+    with open(os.path.join(path, "text_weights.bin"), "wb") as f:
+        for role, arr in weights.items():
+            if role in drop:
+                continue
+            arr = np.ascontiguousarray(arr)
+            pad = (-off) % alignment
+            f.write(b"\0" * pad)
+            off += pad
+            f.write(arr.tobytes())
+            rp = {"embedding": "global.token_embedding", "final_norm": "global.final_norm"}.get(role, role)
+            tensors.append({"role_path": rp, "name": rp, "file": "text_weights.bin", "offset": off,
+                            "nbytes": int(arr.nbytes), "dtype": "fp32" if arr.dtype == np.float32 else "fp16",
+                            "shape": list(arr.shape)})
+            off += arr.nbytes
+    manifest = {"schema_version": 1, "artifact": {"format": "spock-text-repacked-weights"},
+                "packing": {"alignment": alignment, "byte_order": "little", "weights_file": "text_weights.bin"},
+                "tensors": tensors}
+    with open(os.path.join(path, "text_repack_manifest.json"), "w") as f:
+        json.dump(manifest, f)
