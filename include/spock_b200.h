@@ -227,9 +227,17 @@ int spock_model_reset(spock_model* m, int32_t batch);
  * loop (vk_session.cpp:2298-4190). */
 int spock_model_step(spock_model* m, const int32_t* tokens_in, int32_t* tokens_out, void* hidden_out,
                      void* stream);
-/* Token-serial prefill of prompt [batch][len] (layer_major_prefill semantics,
- * vk_session.cpp:1003-2018) then n_new greedy tokens into out_tokens
- * [batch][n_new] (device int32). Requires a non-default stream (graph replay). */
+/* Layer-major prefill of prompt [batch][len] (device int32; the reference's
+ * layer_major_prefill, vk_session.cpp:1003-2018, batched): every layer over
+ * all prompt tokens at once, DeltaNet layers through the chunk rule. Writes
+ * each sequence's greedy next token to tokens_out [batch] (device int32) and,
+ * when non-NULL, the final-normed hidden of its last prompt token to
+ * hidden_out (device fp16 [batch][1024]). Decoding continues from there. */
+int spock_model_prefill(spock_model* m, const int32_t* prompt, int32_t len, int32_t* tokens_out,
+                        void* hidden_out, void* stream);
+/* Prefill of prompt [batch][len] (spock_model_prefill) then n_new greedy
+ * tokens (graph-replayed decode steps) into out_tokens [batch][n_new]
+ * (device int32). Requires a non-default stream. */
 int spock_model_generate(spock_model* m, const int32_t* prompt, int32_t len, int32_t n_new,
                          int32_t* out_tokens, void* stream);
 

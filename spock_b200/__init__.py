@@ -37,7 +37,8 @@ EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
             "spock_kernel_launch_count", "spock_selftest_wait_timeout", "spock_chunk_prefill", "spock_chunk_last_to_fp16",
             "spock_deltanet_decode_step", "spock_deltanet_recurrent", "spock_chunk_prefill_noalloc",
             "spock_model_create", "spock_model_destroy", "spock_model_last_error", "spock_model_set_weight",
-            "spock_model_reset", "spock_model_step", "spock_model_generate", "spock_model_load_artifact"]
+            "spock_model_reset", "spock_model_step", "spock_model_generate", "spock_model_load_artifact",
+            "spock_model_prefill"]
 
 
 class SpockError(RuntimeError):
@@ -314,6 +315,7 @@ def _model_lib():
         L.spock_model_reset.argtypes = [vp, ctypes.c_int32]
         L.spock_model_step.argtypes = [vp, vp, vp, vp, vp]
         L.spock_model_generate.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, vp, vp]
+        L.spock_model_prefill.argtypes = [vp, vp, ctypes.c_int32, vp, vp, vp]
         L._model_types = True
     return L
 
@@ -361,8 +363,20 @@ class Model:
         self._check(self.L.spock_model_step(self.h, _ptr(tokens), _ptr(out), _ptr(hid), _stream(stream)))
         return out, hid
 
+    def prefill(self, prompt, stream=None):
+        """prompt: int32 CUDA tensor [batch, len] -> (next tokens [batch], final-normed hidden of the
+        last prompt token fp16 [batch, 1024]). Layer-major: every layer over the whole prompt."""
+        import torch
+        prompt = prompt.contiguous()
+        out = torch.empty((prompt.shape[0],), dtype=torch.int32, device=prompt.device)
+        hid = torch.empty((prompt.shape[0], 1024), dtype=torch.float16, device=prompt.device)
+        self._check(self.L.spock_model_prefill(self.h, _ptr(prompt), prompt.shape[1], _ptr(out), _ptr(hid),
+                                               _stream(stream)))
+        return out, hid
+
     def generate(self, prompt, n_new, stream=None):
-        """prompt: int32 CUDA tensor [batch, len] -> greedy tokens [batch, n_new] (token-serial prefill)."""
+        """prompt: int32 CUDA tensor [batch, len] -> greedy tokens [batch, n_new] (layer-major prefill,
+        then graph-replayed decode steps)."""
         import torch
         out = torch.empty((prompt.shape[0], n_new), dtype=torch.int32, device=prompt.device)
         self._check(self.L.spock_model_generate(self.h, _ptr(prompt), prompt.shape[1], n_new, _ptr(out),

@@ -5,7 +5,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = ["capi.cu", "decode_step.cu", "chunk_prefill.cu", "chunk_pipeline.cu", "gemm.cu", "model_kernels.cu", "model.cu"]
+SOURCES = ["capi.cu", "decode_step.cu", "chunk_prefill.cu", "chunk_pipeline.cu", "gemm.cu", "model_kernels.cu", "prefill.cu", "model.cu"]
 LIB = os.path.join(HERE, "libspock_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "../apps/json_min.h"
+#include "chunk_scratch.h"
 #include "common.cuh"
 #include "gemm.h"
 
@@ -36,10 +37,10 @@ Status launch_embed(const int* tokens, const void* emb, void* h, int batch, cuda
 Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batch, cudaStream_t st);
 Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* kn_w, const float* rope,
                         const int* pos, void* q_out, void* gate_out, void* kv, int64_t kv_seq_stride,
-                        int64_t kv_layer_off, float eps, int batch, cudaStream_t st);
+                        int64_t kv_layer_off, float eps, int rows, cudaStream_t st, int rows_per_seq = 1);
 Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
-                          int64_t kv_layer_off, const int* pos, float scale, void* out, int batch,
-                          cudaStream_t st);
+                          int64_t kv_layer_off, const int* pos, float scale, void* out, int rows,
+                          cudaStream_t st, int rows_per_seq = 1);
 Status launch_decode_step_strided(const spock_dn_layer& L, int64_t batch, void* qkv, int qkv_ld,
                                   void* conv_state, float* state, const void* a, const void* b, int ab_ld,
                                   const void* z, int z_ld, void* out, int out_ld, void* core_raw, int* err,
@@ -65,6 +66,16 @@ __global__ void copy_col_kernel(int* dst, int dst_stride, int dst_off, const int
 }  // namespace
 
 Status gemm_prepare();
+Status launch_dn_prefill_conv(const void* proj, int ld, int batch, int T, int H, const void* conv_w,
+                              const void* conv_old, void* conv_new, const float* a_log_bias, void* q, void* k, void* v,
+                              float* g, float* beta, cudaStream_t st);
+Status launch_dn_prefill_gate(const float* core, const void* proj, int ld, int z_off, const float* norm_w, float eps,
+                              int batch, int T, int H, void* out, cudaStream_t st);
+Status launch_last_rows(const void* src, void* dst, int batch, int T, int width, cudaStream_t st);
+Status launch_advance_pos(int* pos, int batch, int T, cudaStream_t st);
+Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, const void* q, const void* k,
+                            const void* v, const float* g, const float* beta, const float* init, void* out,
+                            float* final_state, int* err_flag, cudaStream_t stream);
 
 struct ModelLayer {
   bool attn = false;
@@ -101,8 +112,17 @@ struct spock_model {
   void* kv = nullptr;
   int64_t kv_seq_stride = 0;
   cudaGraphExec_t graph = nullptr;
+  int h_pos = 0;  // tokens processed since reset (all sequences advance together)
   int graph_batch = -1;
   cudaStream_t graph_stream = nullptr;
+  // layer-major prefill scratch, grown on demand (rows = batch x prompt length)
+  struct Prefill {
+    size_t rows = 0;  // capacity
+    void* buf = nullptr;
+    void *h, *x, *proj, *mix, *mlp, *q, *k, *v, *aq, *agate, *last, *conv_old;
+    float *g, *beta, *core;
+  } pf;
+  spock::ChunkScratch chunk_scratch;
 };
 
 namespace {
@@ -200,6 +220,122 @@ Status record_step(spock_model* m, cudaStream_t st) {
   TRY(spock::launch_argmax_finish(m->amax_val, m->amax_idx, (m->d.vocab + 127) / 128, B, m->tok_out, st));
   spock::launch_k(spock::advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, m->pos, m->tok_out, m->tok_in, B);
   SPOCK_LAUNCH_CHECK("advance_kernel");
+  return Status::ok();
+}
+
+// Grows the prefill scratch to `rows` token rows (plus one 256-row GEMM block of slack).
+Status reserve_prefill(spock_model* m, size_t rows) {
+  if (rows <= m->pf.rows) return Status::ok();
+  if (m->pf.buf) cudaFree(m->pf.buf);  // waits for the device: no queued work still reads it
+  m->pf = spock_model::Prefill{};
+  const size_t R = rows + 256, B = (size_t)m->d.max_batch;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) / 256 * 256;
+    return o;
+  };
+  const size_t o_h = take(R * HID * 2), o_x = take(R * HID * 2), o_proj = take(R * DN_IN * 2),
+               o_mix = take(R * 2048 * 2), o_mlp = take(R * INTER * 2), o_q = take(R * 2048 * 2),
+               o_k = take(R * 2048 * 2), o_v = take(R * 2048 * 2), o_aq = take(R * QH * HD * 2),
+               o_ag = take(R * QH * HD * 2), o_last = take(B * HID * 2), o_conv = take(B * CONV * 4 * 2),
+               o_g = take(R * DNH * 4), o_b = take(R * DNH * 4), o_core = take(R * 2048 * 4);
+  void* buf = nullptr;
+  cudaError_t e = cudaMalloc(&buf, off);
+  if (e != cudaSuccess) return Status::err(SPOCK_ERR_ALLOC, "model prefill: scratch allocation failed");
+  cudaMemset(buf, 0, off);
+  char* c = static_cast<char*>(buf);
+  auto& p = m->pf;
+  p.buf = buf;
+  p.rows = rows;
+  p.h = c + o_h;
+  p.x = c + o_x;
+  p.proj = c + o_proj;
+  p.mix = c + o_mix;
+  p.mlp = c + o_mlp;
+  p.q = c + o_q;
+  p.k = c + o_k;
+  p.v = c + o_v;
+  p.aq = c + o_aq;
+  p.agate = c + o_ag;
+  p.last = c + o_last;
+  p.conv_old = c + o_conv;
+  p.g = reinterpret_cast<float*>(c + o_g);
+  p.beta = reinterpret_cast<float*>(c + o_b);
+  p.core = reinterpret_cast<float*>(c + o_core);
+  return Status::ok();
+}
+
+// A projection over R token rows: row blocks of at most 256 (the GEMM's batch
+// limit), no K split (the split accumulator is sized for decode batches).
+Status gemm_rows(spock_model* m, int epi, const void* x, const void* w, int n_out, int k, void* y, int ldy,
+                 const void* res, int R, cudaStream_t st) {
+  for (int r0 = 0; r0 < R; r0 += 256) {
+    const int rows = R - r0 < 256 ? R - r0 : 256;
+    spock::GemmArgs a{};
+    a.n_out = n_out;
+    a.k = k;
+    a.batch = rows;
+    a.bpad = (rows + 15) / 16 * 16;
+    a.nsplit = 1;
+    a.y = (__half*)y + (size_t)r0 * ldy;
+    a.ldy = ldy;
+    a.res = res ? (const __half*)res + (size_t)r0 * ldy : nullptr;
+    a.ws = m->ws;
+    a.tickets = m->tickets;
+    a.amax_val = m->amax_val;
+    a.amax_idx = m->amax_idx;
+    a.err = m->err_flag;
+    TRY(spock::launch_gemm(epi, (const __half*)x + (size_t)r0 * k, w, a, m->sms, st));
+  }
+  return Status::ok();
+}
+
+// Layer-major prefill: every layer over all T prompt tokens of every sequence
+// (rows r = b*T + t), then the final norm, LM head and argmax of each
+// sequence's last token. DeltaNet layers run the chunk rule over the prompt.
+Status record_prefill(spock_model* m, const int32_t* prompt, int T, cudaStream_t st) {
+  spock::pdl_scope pdl_on;  // (the caller disables it on the legacy default stream)
+  if (!st) spock::pdl_enabled() = false;
+  const int B = m->batch, R = B * T;
+  const float eps = m->d.rms_eps;
+  auto& p = m->pf;
+  TRY(spock::launch_embed(prompt, m->emb, p.h, R, st));
+  for (const auto& l : m->L) {
+    TRY(spock::launch_rmsnorm(p.h, l.input_norm, p.x, eps, R, st));
+    if (!l.attn) {
+      TRY(gemm_rows(m, spock::EPI_F16, p.x, l.w_in, DN_IN, HID, p.proj, DN_IN, nullptr, R, st));
+      // the decode step's layout: [dn layer][sequence][...] with the session's batch
+      uint16_t* conv = (uint16_t*)m->conv_state + (size_t)l.dn_idx * B * CONV * 4;
+      float* state = m->dn_state + (size_t)l.dn_idx * B * DNH * DND * DND;
+      if (cudaMemcpyAsync(p.conv_old, conv, (size_t)B * CONV * 4 * 2, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return Status::err(SPOCK_ERR_CUDA, "model prefill: conv snapshot failed");
+      TRY(spock::launch_dn_prefill_conv(p.proj, DN_IN, B, T, DNH, l.conv_w, p.conv_old, conv, l.a_log_bias, p.q, p.k,
+                                        p.v, p.g, p.beta, st));
+      spock_chunk_desc cd{B, DNH, T, DND, DND, 64, SPOCK_F16, SPOCK_F32, 0, 0};
+      TRY(spock::launch_chunk_prefill(m->chunk_scratch, cd, p.q, p.k, p.v, p.g, p.beta, state, p.core, state,
+                                      m->err_flag, st));
+      TRY(spock::launch_dn_prefill_gate(p.core, p.proj, DN_IN, CONV, l.dn_norm, eps, B, T, DNH, p.mix, st));
+      TRY(gemm_rows(m, spock::EPI_RESIDUAL, p.mix, l.w_out, HID, DNH * DND, p.h, HID, p.h, R, st));
+    } else {
+      TRY(gemm_rows(m, spock::EPI_F16, p.x, l.w_in, ATT_IN, HID, p.proj, ATT_IN, nullptr, R, st));
+      const int64_t layer_off = (int64_t)l.attn_idx * m->d.max_seq * 2 * KVH * HD;
+      TRY(spock::launch_attn_prep(p.proj, ATT_IN, l.q_norm, l.k_norm, m->rope, m->pos, p.aq, p.agate, m->kv,
+                                  m->kv_seq_stride, layer_off, eps, R, st, T));
+      TRY(spock::launch_attn_decode(p.aq, p.agate, m->kv, m->kv_seq_stride, layer_off, m->pos, 1.0f / 16.0f, p.mix, R,
+                                    st, T));
+      TRY(gemm_rows(m, spock::EPI_RESIDUAL, p.mix, l.w_out, HID, QH * HD, p.h, HID, p.h, R, st));
+    }
+    TRY(spock::launch_rmsnorm(p.h, l.post_norm, p.x, eps, R, st));
+    TRY(gemm_rows(m, spock::EPI_SWIGLU, p.x, l.w_gu, 2 * INTER, HID, p.mlp, INTER, nullptr, R, st));
+    TRY(gemm_rows(m, spock::EPI_RESIDUAL, p.mlp, l.w_down, HID, INTER, p.h, HID, p.h, R, st));
+  }
+  // each sequence's last token: final norm, LM head, argmax (the decode step's tail)
+  TRY(spock::launch_last_rows(p.h, p.last, B, T, HID, st));
+  TRY(spock::launch_rmsnorm(p.last, m->final_norm, m->x, eps, B, st));
+  TRY(gemm_rows(m, spock::EPI_ARGMAX, m->x, m->emb, m->d.vocab, HID, nullptr, 0, nullptr, B, st));
+  TRY(spock::launch_argmax_finish(m->amax_val, m->amax_idx, (m->d.vocab + 127) / 128, B, m->tok_out, st));
+  TRY(spock::launch_advance_pos(m->pos, B, T, st));
   return Status::ok();
 }
 
@@ -328,6 +464,8 @@ __attribute__((visibility("default"))) int spock_model_destroy(spock_model* m) {
   if (!m) return SPOCK_OK;
   if (m->graph) cudaGraphExecDestroy(m->graph);
   for (void* p : m->allocs) cudaFree(p);
+  if (m->pf.buf) cudaFree(m->pf.buf);
+  m->chunk_scratch.release();
   delete m;
   return SPOCK_OK;
 }
@@ -491,6 +629,7 @@ __attribute__((visibility("default"))) int spock_model_reset(spock_model* m, int
   if (!m || batch < 1 || batch > m->d.max_batch) return SPOCK_ERR_INVALID;
   Guard g(m->device);
   m->batch = batch;
+  m->h_pos = 0;
   const int B = m->bpad;
   cudaMemset(m->dn_state, 0, (size_t)n_dn(m) * B * DNH * DND * DND * 4);
   cudaMemset(m->conv_state, 0, (size_t)n_dn(m) * B * CONV * 4 * 2);
@@ -504,8 +643,10 @@ __attribute__((visibility("default"))) int spock_model_reset(spock_model* m, int
 __attribute__((visibility("default"))) int spock_model_step(spock_model* m, const int32_t* tokens_in,
                                                             int32_t* tokens_out, void* hidden_out, void* stream) {
   if (!m || !tokens_in || m->batch < 1) return SPOCK_ERR_INVALID;
+  if (m->h_pos + 1 > m->d.max_seq) return mfail(m, SPOCK_ERR_INVALID, "spock_model_step: past max_seq");
   Guard g(m->device);
   cudaStream_t st = (cudaStream_t)stream;
+  ++m->h_pos;
   cudaMemcpyAsync(m->tok_in, tokens_in, (size_t)m->batch * 4, cudaMemcpyDeviceToDevice, st);
   Status s = st ? ensure_graph(m, st) : Status::ok();
   if (s.code) return mfail(m, s.code, s.msg);
@@ -521,29 +662,50 @@ __attribute__((visibility("default"))) int spock_model_step(spock_model* m, cons
   return SPOCK_OK;
 }
 
-// Token-serial prefill of prompt[batch][len] (device int32), the reference's
-// own layer_major_prefill semantics (each prompt token through the decode
-// kernels), then `n_new` greedy tokens. out_tokens: device int32 [batch][n_new]
-// (the first entry is the prompt's greedy continuation).
+// Layer-major prefill of prompt [batch][len] (device int32): all layers over
+// all prompt tokens at once, the DeltaNet layers through the chunk rule.
+// tokens_out [batch] (device int32) receives each sequence's greedy next
+// token; hidden_out (nullable, device fp16 [batch][1024]) the final-normed
+// hidden of its last prompt token. The session continues from there.
+__attribute__((visibility("default"))) int spock_model_prefill(spock_model* m, const int32_t* prompt, int32_t len,
+                                                               int32_t* tokens_out, void* hidden_out, void* stream) {
+  if (!m || !prompt || len < 1 || m->batch < 1) return SPOCK_ERR_INVALID;
+  if (m->h_pos + len > m->d.max_seq) return mfail(m, SPOCK_ERR_INVALID, "spock_model_prefill: past max_seq");
+  if ((int64_t)m->batch * len > (1 << 24)) return mfail(m, SPOCK_ERR_INVALID, "spock_model_prefill: batch*len too large");
+  Guard g(m->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Status s = reserve_prefill(m, (size_t)m->batch * len);
+  if (!s.code) s = record_prefill(m, prompt, len, st);
+  if (s.code) return mfail(m, s.code, s.msg);
+  m->h_pos += len;
+  if (tokens_out) cudaMemcpyAsync(tokens_out, m->tok_out, (size_t)m->batch * 4, cudaMemcpyDeviceToDevice, st);
+  if (hidden_out) cudaMemcpyAsync(hidden_out, m->x, (size_t)m->batch * HID * 2, cudaMemcpyDeviceToDevice, st);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SPOCK_OK : mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));
+}
+
 __attribute__((visibility("default"))) int spock_model_generate(spock_model* m, const int32_t* prompt, int32_t len,
                                                                 int32_t n_new, int32_t* out_tokens, void* stream) {
-  if (!m || !prompt || len < 1 || n_new < 0 || m->batch < 1 || len + n_new > m->d.max_seq) return SPOCK_ERR_INVALID;
+  if (!m || !prompt || len < 1 || n_new < 0 || m->batch < 1) return SPOCK_ERR_INVALID;
+  if (m->h_pos + len + n_new > m->d.max_seq) return mfail(m, SPOCK_ERR_INVALID, "spock_model_generate: past max_seq");
   Guard g(m->device);
   cudaStream_t st = (cudaStream_t)stream;
   if (!st) return mfail(m, SPOCK_ERR_INVALID, "spock_model_generate needs a non-default stream (graph replay)");
+  // layer-major prefill of the prompt, then greedy decode by graph replay
+  int rc = spock_model_prefill(m, prompt, len, nullptr, nullptr, stream);
+  if (rc != SPOCK_OK) return rc;
   Status s = ensure_graph(m, st);
   if (s.code) return mfail(m, s.code, s.msg);
   const int B = m->batch;
-  std::vector<int32_t> col(B);
   const unsigned nb = (unsigned)((B + 127) / 128);
-  for (int t = 0; t < len; ++t) {
-    spock::copy_col_kernel<<<nb, 128, 0, st>>>(m->tok_in, 1, 0, prompt, len, t, B);  // prompt column t
-    if (cudaGraphLaunch(m->graph, st) != cudaSuccess) return mfail(m, SPOCK_ERR_CUDA, "graph launch failed");
-  }
+  spock::copy_col_kernel<<<nb, 128, 0, st>>>(m->tok_in, 1, 0, m->tok_out, 1, 0, B);  // first generated token
   for (int i = 0; i < n_new; ++i) {
-    // the step left its argmax in tok_in: record it, then feed it back
+    // tok_in holds generated token i: record it, then feed it back
     spock::copy_col_kernel<<<nb, 128, 0, st>>>(out_tokens, n_new, i, m->tok_in, 1, 0, B);
-    if (i + 1 < n_new && cudaGraphLaunch(m->graph, st) != cudaSuccess) return mfail(m, SPOCK_ERR_CUDA, "graph launch failed");
+    if (i + 1 < n_new) {
+      if (cudaGraphLaunch(m->graph, st) != cudaSuccess) return mfail(m, SPOCK_ERR_CUDA, "graph launch failed");
+      ++m->h_pos;
+    }
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SPOCK_OK : mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));

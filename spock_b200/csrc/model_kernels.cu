@@ -58,15 +58,18 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__
   }
 }
 
-// grid (QH + KVH, batch), 256 threads (thread d = head dimension d).
-// qkv: [batch][ld] with [q0 (256) | gate0 (256) | q1 | gate1 | ... | k (2x256) | v (2x256)].
+// grid (QH + KVH, rows), 256 threads (thread d = head dimension d). Row r is
+// token r % T of sequence r / T (T = rows_per_seq: 1 in decode, the prompt
+// length in prefill), at position pos[seq] + r % T.
+// qkv: [rows][ld] with [q0 (256) | gate0 (256) | q1 | gate1 | ... | k (2x256) | v (2x256)].
 __global__ void __launch_bounds__(256)
     attn_prep_kernel(const __half* __restrict__ qkv, int ld, const __half* __restrict__ qn_w,
                      const __half* __restrict__ kn_w, const float* __restrict__ rope /*[max_seq][64] cos,sin*/,
                      const int* __restrict__ pos, __half* __restrict__ q_out /*[batch][QH][HD]*/,
                      __half* __restrict__ gate_out, __half* __restrict__ kv /*[batch][layers][max_seq][2][KVH][HD]*/,
-                     int64_t kv_seq_stride /*elements per sequence*/, int64_t kv_layer_off, float eps, float scale_unused) {
-  const int hh = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+                     int64_t kv_seq_stride /*elements per sequence*/, int64_t kv_layer_off, float eps, int rows_per_seq) {
+  const int hh = blockIdx.x, b = blockIdx.y, d = threadIdx.x;  // b: row
+  const int seq = b / rows_per_seq;
   pdl_wait();
   pdl_launch();
   const __half* row = qkv + (size_t)b * ld;
@@ -90,7 +93,7 @@ __global__ void __launch_bounds__(256)
   __syncthreads();
   // partial RoPE: pairs (d, d+32) for d < 32 of the first 64 dims
   float o = xn;
-  const int p = pos[b];
+  const int p = pos[seq] + b % rows_per_seq;
   if (d < ROT) {
     const int i = d & 31;
     const float c = rope[(size_t)p * ROT + 2 * i], sn_ = rope[(size_t)p * ROT + 2 * i + 1];
@@ -101,26 +104,30 @@ __global__ void __launch_bounds__(256)
   if (is_q) {
     q_out[((size_t)b * QH + hh) * HD + d] = oh;
   } else {
-    __half* base = kv + (size_t)b * kv_seq_stride + kv_layer_off + (size_t)p * (2 * KVH * HD);
+    __half* base = kv + (size_t)seq * kv_seq_stride + kv_layer_off + (size_t)p * (2 * KVH * HD);
     base[kvh * HD + d] = oh;                                          // K
     base[KVH * HD + kvh * HD + d] = row[QH * 2 * HD + KVH * HD + kvh * HD + d];  // V (no norm, no rope)
   }
 }
 
-// grid (KVH, batch), 256 threads = 8 warps. Warp w takes positions w, w+8, ...;
+// grid (KVH, rows), 256 threads = 8 warps; rows as in attn_prep_kernel, each
+// query row attends causally to positions 0 .. pos[seq] + row % T.
+// Warp w takes positions w, w+8, ...;
 // lane l owns dims 8l..8l+7 of the 4 query heads of this kv head (GQA group).
 // Online softmax per warp, merged across warps in shared memory; the output is
 // fp16(acc / (sum + 1e-30)) and then fp16(out * sigmoid(gate)).
 __global__ void __launch_bounds__(256)
     attn_decode_kernel(const __half* __restrict__ q /*[batch][QH][HD]*/, const __half* __restrict__ gate,
                        const __half* __restrict__ kv, int64_t kv_seq_stride, int64_t kv_layer_off,
-                       const int* __restrict__ pos, float scale, __half* __restrict__ out /*[batch][QH*HD]*/) {
-  const int kvh = blockIdx.x, b = blockIdx.y;
+                       const int* __restrict__ pos, float scale, __half* __restrict__ out /*[rows][QH*HD]*/,
+                       int rows_per_seq) {
+  const int kvh = blockIdx.x, b = blockIdx.y;  // b: row
+  const int seq = b / rows_per_seq;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int G = QH / KVH;  // 4
   pdl_wait();
   pdl_launch();
-  const int L = pos[b] + 1;
+  const int L = pos[seq] + b % rows_per_seq + 1;
   float qv[G][8];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -141,7 +148,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc[g][k] = 0.f;
   }
-  const __half* base = kv + (size_t)b * kv_seq_stride + kv_layer_off;
+  const __half* base = kv + (size_t)seq * kv_seq_stride + kv_layer_off;
   for (int p = warp; p < L; p += 8) {
     const __half* kr = base + (size_t)p * (2 * KVH * HD) + kvh * HD + lane * 8;
     const __half* vr = base + (size_t)p * (2 * KVH * HD) + KVH * HD + kvh * HD + lane * 8;
@@ -227,19 +234,19 @@ Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batc
 
 Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* kn_w, const float* rope,
                         const int* pos, void* q_out, void* gate_out, void* kv, int64_t kv_seq_stride,
-                        int64_t kv_layer_off, float eps, int batch, cudaStream_t st) {
-  launch_k(attn_prep_kernel, dim3(QH + KVH, batch), dim3(256), 0, st, (const __half*)qkv, ld, (const __half*)qn_w,
+                        int64_t kv_layer_off, float eps, int rows, cudaStream_t st, int rows_per_seq) {
+  launch_k(attn_prep_kernel, dim3(QH + KVH, rows), dim3(256), 0, st, (const __half*)qkv, ld, (const __half*)qn_w,
            (const __half*)kn_w, rope, pos, (__half*)q_out, (__half*)gate_out, (__half*)kv, kv_seq_stride,
-           kv_layer_off, eps, 0.f);
+           kv_layer_off, eps, rows_per_seq);
   SPOCK_LAUNCH_CHECK("attn_prep_kernel");
   return Status::ok();
 }
 
 Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
-                          int64_t kv_layer_off, const int* pos, float scale, void* out, int batch,
-                          cudaStream_t st) {
-  launch_k(attn_decode_kernel, dim3(KVH, batch), dim3(256), 0, st, (const __half*)q, (const __half*)gate,
-           (const __half*)kv, kv_seq_stride, kv_layer_off, pos, scale, (__half*)out);
+                          int64_t kv_layer_off, const int* pos, float scale, void* out, int rows,
+                          cudaStream_t st, int rows_per_seq) {
+  launch_k(attn_decode_kernel, dim3(KVH, rows), dim3(256), 0, st, (const __half*)q, (const __half*)gate,
+           (const __half*)kv, kv_seq_stride, kv_layer_off, pos, scale, (__half*)out, rows_per_seq);
   SPOCK_LAUNCH_CHECK("attn_decode_kernel");
   return Status::ok();
 }
