@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__
   }
 }
 
-// grid (QH + KVH, rows), 256 threads (thread d = head dimension d). Row r is
+// grid (rows, QH + KVH), 256 threads (thread d = head dimension d). Row r is
 // token r % T of sequence r / T (T = rows_per_seq: 1 in decode, the prompt
 // length in prefill), at position pos[seq] + r % T.
 // qkv: [rows][ld] with [q0 (256) | gate0 (256) | q1 | gate1 | ... | k (2x256) | v (2x256)].
@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(256)
                      const int* __restrict__ pos, __half* __restrict__ q_out /*[batch][QH][HD]*/,
                      __half* __restrict__ gate_out, __half* __restrict__ kv /*[batch][layers][max_seq][2][KVH][HD]*/,
                      int64_t kv_seq_stride /*elements per sequence*/, int64_t kv_layer_off, float eps, int rows_per_seq) {
-  const int hh = blockIdx.x, b = blockIdx.y, d = threadIdx.x;  // b: row
+  const int hh = blockIdx.y, b = blockIdx.x, d = threadIdx.x;  // b: row
   const int seq = b / rows_per_seq;
   pdl_wait();
   pdl_launch();
@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// grid (KVH, rows), 256 threads = 8 warps; rows as in attn_prep_kernel, each
+// grid (rows, KVH), 256 threads = 8 warps; rows as in attn_prep_kernel, each
 // query row attends causally to positions 0 .. pos[seq] + row % T.
 // Warp w takes positions w, w+8, ...;
 // lane l owns dims 8l..8l+7 of the 4 query heads of this kv head (GQA group).
@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(256)
                        const __half* __restrict__ kv, int64_t kv_seq_stride, int64_t kv_layer_off,
                        const int* __restrict__ pos, float scale, __half* __restrict__ out /*[rows][QH*HD]*/,
                        int rows_per_seq) {
-  const int kvh = blockIdx.x, b = blockIdx.y;  // b: row
+  const int kvh = blockIdx.y, b = blockIdx.x;  // b: row
   const int seq = b / rows_per_seq;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int G = QH / KVH;  // 4
@@ -235,7 +235,7 @@ Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batc
 Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* kn_w, const float* rope,
                         const int* pos, void* q_out, void* gate_out, void* kv, int64_t kv_seq_stride,
                         int64_t kv_layer_off, float eps, int rows, cudaStream_t st, int rows_per_seq) {
-  launch_k(attn_prep_kernel, dim3(QH + KVH, rows), dim3(256), 0, st, (const __half*)qkv, ld, (const __half*)qn_w,
+  launch_k(attn_prep_kernel, dim3(rows, QH + KVH), dim3(256), 0, st, (const __half*)qkv, ld, (const __half*)qn_w,
            (const __half*)kn_w, rope, pos, (__half*)q_out, (__half*)gate_out, (__half*)kv, kv_seq_stride,
            kv_layer_off, eps, rows_per_seq);
   SPOCK_LAUNCH_CHECK("attn_prep_kernel");
@@ -245,7 +245,7 @@ Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* k
 Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
                           int64_t kv_layer_off, const int* pos, float scale, void* out, int rows,
                           cudaStream_t st, int rows_per_seq) {
-  launch_k(attn_decode_kernel, dim3(KVH, rows), dim3(256), 0, st, (const __half*)q, (const __half*)gate,
+  launch_k(attn_decode_kernel, dim3(rows, KVH), dim3(256), 0, st, (const __half*)q, (const __half*)gate,
            (const __half*)kv, kv_seq_stride, kv_layer_off, pos, scale, (__half*)out, rows_per_seq);
   SPOCK_LAUNCH_CHECK("attn_decode_kernel");
   return Status::ok();

@@ -121,13 +121,13 @@ __global__ void __launch_bounds__(kDim)
   }
 }
 
-// grid (H, rows), 128 threads: gated RMSNorm of the chunk rule's output.
+// grid (rows, H), 128 threads: gated RMSNorm of the chunk rule's output.
 // core: [batch][H][T][128] fp32; z from proj row [.. | z (H*128) | ..] at column z_off;
 // out: [rows][H*128] fp16 (token rows for the output projection).
 __global__ void __launch_bounds__(kDim)
     dn_prefill_gate_kernel(const float* __restrict__ core, const __half* __restrict__ proj, int ld, int z_off,
                            const float* __restrict__ norm_w, float eps, int T, int H, __half* __restrict__ out) {
-  const int h = blockIdx.x, row = blockIdx.y, c = threadIdx.x;
+  const int h = blockIdx.y, row = blockIdx.x, c = threadIdx.x;
   const int b = row / T, t = row % T;
   __shared__ float sq[kDim];
   __shared__ float nf_s;
@@ -179,7 +179,7 @@ Status launch_dn_prefill_conv(const void* proj, int ld, int batch, int T, int H,
 
 Status launch_dn_prefill_gate(const float* core, const void* proj, int ld, int z_off, const float* norm_w, float eps,
                               int batch, int T, int H, void* out, cudaStream_t st) {
-  launch_k(dn_prefill_gate_kernel, dim3(H, batch * T), dim3(kDim), 0, st, core, (const __half*)proj, ld, z_off,
+  launch_k(dn_prefill_gate_kernel, dim3(batch * T, H), dim3(kDim), 0, st, core, (const __half*)proj, ld, z_off,
            norm_w, eps, T, H, (__half*)out);
   SPOCK_LAUNCH_CHECK("dn_prefill_gate_kernel");
   return Status::ok();
