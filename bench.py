@@ -58,6 +58,11 @@ class ClockSampler:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi's start-up contends with kernel launches: let it
+            # print its first sample before the timed region opens
+            t_end = time.time() + 5.0
+            while not self.rows and time.time() < t_end:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
@@ -394,16 +399,23 @@ def bench_model(args, ws, rank, local):
         if args.config == 3:
             # layer-major prefill of the P-token prompt (spock_model_prefill, via generate's
             # first token), timed as a whole
-            for _ in range(max(1, args.warmup)):
+            for i in range(max(3, args.warmup)):
                 m.reset(B)
-                m.generate(prompt, 1, stream=stream)  # warm-up: scratch, graph capture
-            m.reset(B)
-            stream.synchronize()
+                c0 = cnt()
+                m.generate(prompt, 1, stream=stream)  # warm-up: scratch, eager run, graph capture
+                if i == 0:
+                    per_pf = cnt() - c0  # the eager run counts every kernel of one prefill
+            # each timed prefill between its own events (the session reset
+            # between prefills is outside them)
+            n_pf = max(1, args.steps)
+            evp = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_pf)]
             barrier(ws)
             with ClockSampler(local) as clk:
-                t0.record(stream)
-                m.generate(prompt, 1, stream=stream)
-                t1.record(stream)
+                for e0, e1 in evp:
+                    m.reset(B)
+                    e0.record(stream)
+                    m.generate(prompt, 1, stream=stream)
+                    e1.record(stream)
                 stream.synchronize()
             steps = P
         else:
@@ -418,8 +430,12 @@ def bench_model(args, ws, rank, local):
                 t1.record(stream)
                 stream.synchronize()
             steps = args.steps
-    launches = per_step * steps  # graph replays: kernels per step x timed steps
-    ms = max_over_ranks(t0.elapsed_time(t1), ws) / steps
+    if args.config == 3:
+        launches = per_pf * n_pf
+        ms = max_over_ranks(statistics.mean(e0.elapsed_time(e1) for e0, e1 in evp), ws) / steps
+    else:
+        launches = per_step * steps  # graph replays: kernels per step x timed steps
+        ms = max_over_ranks(t0.elapsed_time(t1), ws) / steps
     value = B * ws / (ms / 1e3)
     hbm, tf, pk = peaks()
     w_bytes = 752.4e6 * 2
@@ -461,7 +477,9 @@ def bench_model(args, ws, rank, local):
         "data": "synthetic (random-init Qwen3.5-0.8B layout, seeded random prompt)",
         "config": {"workload": f"config {args.config}", "sequences_per_gpu": B, "prompt": P, "layers": layers,
                    "vocab": vocab, "parallelism": f"dp{ws} over sequences",
-                   "l2": "weights (1.5 GB) larger than L2"},
+                   "l2": "weights (1.5 GB) larger than L2",
+                   **({"prefills_timed": n_pf, "step": "one prompt token (ms_per_step = prefill ms / prompt)"}
+                      if args.config == 3 else {})},
         "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "h2d_bytes_per_step": int(hp.numel() * 4 / (hp.shape[1] + n_e2e - 1)),
                 "d2h_bytes_per_step": int(B * 4), "note": f"{hp.shape[1]}-token prompt + {n_e2e} new tokens via spock_model_generate"},
         "gpu_launches": int(launches),

@@ -219,7 +219,8 @@ int spock_model_set_weight(spock_model* m, const char* role, const void* host, s
  * uploads of DecodeSession (vk_session.cpp:1151-1462). */
 int spock_model_load_artifact(spock_model* m, const char* repack_dir);
 /* Zeroes DeltaNet/conv/KV state and positions for `batch` sequences
- * (DecodeSession::reset, vk_session.cpp:980). */
+ * (DecodeSession::reset, vk_session.cpp:980). Synchronises the device before
+ * and after the clears, so it is ordered against work on every stream. */
 int spock_model_reset(spock_model* m, int32_t batch);
 /* One token per sequence through all layers, final norm, LM head and argmax.
  * tokens_in/out: device int32 [batch]; hidden_out (nullable): device fp16

@@ -541,12 +541,15 @@ Status map2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int b
 
 }  // namespace
 
-// x: [bpad][k] fp16 (rows >= batch may hold anything), W: [n_out][k] fp16.
+// x: [bpad][k] fp16 (rows >= batch may hold anything; a prefill's row count,
+// bpad > 256, is one launch of 256-row or smaller blocks), W: [n_out][k] fp16.
 // Workspace needs nsplit * ceil(n_out/128) * 128 * bpad floats when nsplit > 1,
 // tickets ceil(n_out/128) ints (zero), ARGMAX partials ceil(n_out/128) * batch.
 Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, cudaStream_t st) {
-  if (a.k % 64 || a.bpad % 16 || a.bpad < 16 || a.bpad > 256 || a.batch > a.bpad || a.batch < 1)
-    return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: k % 64, 16 <= bpad <= 256 (multiple of 16), batch <= bpad");
+  if (a.k % 64 || a.bpad % 16 || a.bpad < 16 || a.batch > a.bpad || a.batch < 1)
+    return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: k % 64, bpad a multiple of 16, batch <= bpad");
+  if (a.bpad > 256 && a.nsplit > 1)
+    return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: split-K needs bpad <= 256");
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15))
     return Status::err(SPOCK_ERR_INVALID, "gemm: operands must be 16-byte aligned");
   if (epi != EPI_ARGMAX) {
@@ -603,13 +606,16 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     return Status::ok();
   }
   if (a.norm_w) return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: fused RMSNorm only on the small-batch path");
-  // batch blocks first (no partial sums), down to 32 rows
-  int nb = 1;
-  a.bn = a.bpad;
+  // batch blocks first (no partial sums), down to 32 rows. Prefill row counts
+  // (bpad > 256) start from 256-row blocks: one launch covers every row, and
+  // the weight slab of a tile is re-read by its row blocks from L2.
+  a.bn = a.bpad > 256 ? 256 : a.bpad;
+  int nb = (a.bpad + a.bn - 1) / a.bn;
   while (ntiles * nb < sms && a.bn % 32 == 0 && a.bn / 2 >= 32) {
     a.bn /= 2;
-    nb *= 2;
+    nb = (a.bpad + a.bn - 1) / a.bn;
   }
+  if (nb > 65535) return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: too many row blocks");
   CUtensorMap mw, mx;
   Status s = map2d(&mw, w, a.n_out, a.k, 128);
   if (s.code) return s;

@@ -121,7 +121,13 @@ struct spock_model {
     void* buf = nullptr;
     void *h, *x, *proj, *mix, *mlp, *q, *k, *v, *aq, *agate, *last, *conv_old;
     float *g, *beta, *core;
+    int32_t* prompt;  // the replayed graph's prompt rows
   } pf;
+  // prefill graph: a prompt shape (batch, length, stream) seen twice in a row
+  // is captured and replayed from then on
+  cudaGraphExec_t pgraph = nullptr;
+  int pg_batch = -1, pg_len = -1;
+  cudaStream_t pg_stream = nullptr;
   spock::ChunkScratch chunk_scratch;
 };
 
@@ -143,6 +149,13 @@ cudaError_t dalloc(spock_model* m, T** p, size_t bytes) {
   }
   *p = static_cast<T*>(v);
   return e;
+}
+
+void drop_prefill_graph(spock_model* m) {
+  if (m->pgraph) cudaGraphExecDestroy(m->pgraph);
+  m->pgraph = nullptr;
+  m->pg_batch = m->pg_len = -1;
+  m->pg_stream = nullptr;
 }
 
 int n_dn(const spock_model* m) { return (int)(m->d.num_layers - m->d.num_layers / 4); }
@@ -228,6 +241,7 @@ Status reserve_prefill(spock_model* m, size_t rows) {
   if (rows <= m->pf.rows) return Status::ok();
   if (m->pf.buf) cudaFree(m->pf.buf);  // waits for the device: no queued work still reads it
   m->pf = spock_model::Prefill{};
+  drop_prefill_graph(m);
   const size_t R = rows + 256, B = (size_t)m->d.max_batch;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -239,7 +253,8 @@ Status reserve_prefill(spock_model* m, size_t rows) {
                o_mix = take(R * 2048 * 2), o_mlp = take(R * INTER * 2), o_q = take(R * 2048 * 2),
                o_k = take(R * 2048 * 2), o_v = take(R * 2048 * 2), o_aq = take(R * QH * HD * 2),
                o_ag = take(R * QH * HD * 2), o_last = take(B * HID * 2), o_conv = take(B * CONV * 4 * 2),
-               o_g = take(R * DNH * 4), o_b = take(R * DNH * 4), o_core = take(R * 2048 * 4);
+               o_g = take(R * DNH * 4), o_b = take(R * DNH * 4), o_core = take(R * 2048 * 4),
+               o_prompt = take(R * 4);
   void* buf = nullptr;
   cudaError_t e = cudaMalloc(&buf, off);
   if (e != cudaSuccess) return Status::err(SPOCK_ERR_ALLOC, "model prefill: scratch allocation failed");
@@ -263,6 +278,7 @@ Status reserve_prefill(spock_model* m, size_t rows) {
   p.g = reinterpret_cast<float*>(c + o_g);
   p.beta = reinterpret_cast<float*>(c + o_b);
   p.core = reinterpret_cast<float*>(c + o_core);
+  p.prompt = reinterpret_cast<int32_t*>(c + o_prompt);
   return Status::ok();
 }
 
@@ -270,25 +286,23 @@ Status reserve_prefill(spock_model* m, size_t rows) {
 // limit), no K split (the split accumulator is sized for decode batches).
 Status gemm_rows(spock_model* m, int epi, const void* x, const void* w, int n_out, int k, void* y, int ldy,
                  const void* res, int R, cudaStream_t st) {
-  for (int r0 = 0; r0 < R; r0 += 256) {
-    const int rows = R - r0 < 256 ? R - r0 : 256;
-    spock::GemmArgs a{};
-    a.n_out = n_out;
-    a.k = k;
-    a.batch = rows;
-    a.bpad = (rows + 15) / 16 * 16;
-    a.nsplit = 1;
-    a.y = (__half*)y + (size_t)r0 * ldy;
-    a.ldy = ldy;
-    a.res = res ? (const __half*)res + (size_t)r0 * ldy : nullptr;
-    a.ws = m->ws;
-    a.tickets = m->tickets;
-    a.amax_val = m->amax_val;
-    a.amax_idx = m->amax_idx;
-    a.err = m->err_flag;
-    TRY(spock::launch_gemm(epi, (const __half*)x + (size_t)r0 * k, w, a, m->sms, st));
-  }
-  return Status::ok();
+  // one launch over all R rows (the scratch holds at least R + 256 rows, so the
+  // padded rows the tensor map covers are readable)
+  spock::GemmArgs a{};
+  a.n_out = n_out;
+  a.k = k;
+  a.batch = R;
+  a.bpad = (R + 15) / 16 * 16;
+  a.nsplit = 1;
+  a.y = (__half*)y;
+  a.ldy = ldy;
+  a.res = (const __half*)res;
+  a.ws = m->ws;
+  a.tickets = m->tickets;
+  a.amax_val = m->amax_val;
+  a.amax_idx = m->amax_idx;
+  a.err = m->err_flag;
+  return spock::launch_gemm(epi, x, w, a, m->sms, st);
 }
 
 // Layer-major prefill: every layer over all T prompt tokens of every sequence
@@ -337,6 +351,44 @@ Status record_prefill(spock_model* m, const int32_t* prompt, int T, cudaStream_t
   TRY(spock::launch_argmax_finish(m->amax_val, m->amax_idx, (m->d.vocab + 127) / 128, B, m->tok_out, st));
   TRY(spock::launch_advance_pos(m->pos, B, T, st));
   return Status::ok();
+}
+
+// Runs the layer-major prefill. On a non-default stream, the second call in a
+// row with the same (batch, length, stream) captures the launch sequence as a
+// graph over the scratch's own prompt buffer; later calls of that shape copy
+// the prompt there and replay it. (The first call of a shape runs eagerly, so
+// any lazy setup in the launchers has happened before a capture.)
+Status run_prefill(spock_model* m, const int32_t* prompt, int T, cudaStream_t st) {
+  if (!st) return record_prefill(m, prompt, T, st);
+  const bool same = m->pg_batch == m->batch && m->pg_len == T && m->pg_stream == st;
+  if (!same) {
+    drop_prefill_graph(m);
+    m->pg_batch = m->batch;
+    m->pg_len = T;
+    m->pg_stream = st;
+    return record_prefill(m, prompt, T, st);
+  }
+  if (cudaMemcpyAsync(m->pf.prompt, prompt, (size_t)m->batch * T * 4, cudaMemcpyDefault, st) != cudaSuccess)
+    return Status::err(SPOCK_ERR_CUDA, "model prefill: prompt copy failed");
+  if (!m->pgraph) {
+    Status prep = spock::gemm_prepare();
+    if (prep.code) return prep;
+    cudaGraph_t g;
+    cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
+    if (e != cudaSuccess) return spock::cuda_status(e, "model prefill: begin capture");
+    Status s = record_prefill(m, m->pf.prompt, T, st);
+    e = cudaStreamEndCapture(st, &g);
+    if (s.code) return s;
+    if (e != cudaSuccess) return spock::cuda_status(e, "model prefill: end capture");
+    e = cudaGraphInstantiate(&m->pgraph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+      m->pgraph = nullptr;
+      return spock::cuda_status(e, "model prefill: graph instantiate");
+    }
+  }
+  cudaError_t e = cudaGraphLaunch(m->pgraph, st);
+  return e == cudaSuccess ? Status::ok() : spock::cuda_status(e, "model prefill: graph launch");
 }
 
 Status ensure_graph(spock_model* m, cudaStream_t st) {
@@ -463,6 +515,7 @@ __attribute__((visibility("default"))) int spock_model_create(spock_ctx* ctx, co
 __attribute__((visibility("default"))) int spock_model_destroy(spock_model* m) {
   if (!m) return SPOCK_OK;
   if (m->graph) cudaGraphExecDestroy(m->graph);
+  drop_prefill_graph(m);
   for (void* p : m->allocs) cudaFree(p);
   if (m->pf.buf) cudaFree(m->pf.buf);
   m->chunk_scratch.release();
@@ -631,10 +684,15 @@ __attribute__((visibility("default"))) int spock_model_reset(spock_model* m, int
   m->batch = batch;
   m->h_pos = 0;
   const int B = m->bpad;
+  // Work queued on any stream may still use the state: reset between
+  // device-wide synchronisations so the clears are ordered on every stream
+  // (the caller's streams need not synchronise with the legacy stream).
+  cudaDeviceSynchronize();
   cudaMemset(m->dn_state, 0, (size_t)n_dn(m) * B * DNH * DND * DND * 4);
   cudaMemset(m->conv_state, 0, (size_t)n_dn(m) * B * CONV * 4 * 2);
   cudaMemset(m->pos, 0, (size_t)B * 4);
-  cudaError_t e = cudaMemset(m->kv, 0, (size_t)B * m->kv_seq_stride * 2);
+  cudaMemset(m->kv, 0, (size_t)B * m->kv_seq_stride * 2);
+  cudaError_t e = cudaDeviceSynchronize();
   return e == cudaSuccess ? SPOCK_OK : mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));
 }
 
@@ -675,7 +733,7 @@ __attribute__((visibility("default"))) int spock_model_prefill(spock_model* m, c
   Guard g(m->device);
   cudaStream_t st = (cudaStream_t)stream;
   Status s = reserve_prefill(m, (size_t)m->batch * len);
-  if (!s.code) s = record_prefill(m, prompt, len, st);
+  if (!s.code) s = run_prefill(m, prompt, len, st);
   if (s.code) return mfail(m, s.code, s.msg);
   m->h_pos += len;
   if (tokens_out) cudaMemcpyAsync(tokens_out, m->tok_out, (size_t)m->batch * 4, cudaMemcpyDeviceToDevice, st);

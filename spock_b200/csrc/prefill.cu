@@ -14,7 +14,7 @@ namespace spock {
 namespace {
 
 constexpr int kDim = 128;
-constexpr int kTokTile = 64;  // tokens per CTA of the conv kernel
+constexpr int kTokTile = 16;  // tokens per CTA of the conv kernel (many CTAs: each thread walks its tokens in order)
 constexpr int kTokGroup = 8;  // tokens per L2 barrier round
 
 // The shaders' stride-64..1 tree over s[0..127] by one warp (decode_step.cu).
