@@ -39,8 +39,8 @@ namespace spock {
 
 namespace {
 
-constexpr int kMaxStages = 4;
-constexpr int kRingBytes = kMaxStages * (128 * 128 + 256 * 128);
+constexpr int kMaxStages = 12;
+constexpr int kRingBytes = 4 * (128 * 128 + 256 * 128);  // 192 KB: the ring never exceeds it
 constexpr uint32_t kWaitLimit = 1u << 25;
 
 __device__ __forceinline__ bool wait_spin(uint64_t* bar, uint32_t parity) {
@@ -139,6 +139,14 @@ __global__ void __launch_bounds__(128, 1)
   }
   __syncwarp();
   pdl_wait();  // the epilogue reads and writes what earlier kernels use
+  if constexpr (kEpi == EPI_RESIDUAL) {
+    // pull this CTA's residual rows (2 x 128 B each) into L2 while the K loop runs
+    for (int j = t; j < 2 * a.bn; j += 128) {
+      const int b = n0 + (j >> 1), col = tile * 128 + (j & 1) * 64;
+      if (b < a.batch && col < a.n_out)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.res + (size_t)b * a.ldy + col));
+    }
+  }
   // epilogue: all 128 threads; thread t <-> weight row tile*128 + t
   if (!wait_spin(done, 0)) ok = false;
   if (__syncthreads_or(!ok)) {
@@ -180,7 +188,7 @@ __global__ void __launch_bounds__(128, 1)
   if (finisher) {
     // the pipeline's stages are idle now: fp16 staging tile [bn][width]
     __half* stg = reinterpret_cast<__half*>(sm);
-    constexpr int width = kEpi == EPI_SWIGLU ? 64 : 128;
+    constexpr int width = 128;  // staged weight rows (SWIGLU: gate and up, 64 outputs)
     for (int c0 = 0; c0 < a.bn; c0 += 32) {
       float v[32];
       if (a.nsplit > 1) {
@@ -201,23 +209,11 @@ __global__ void __launch_bounds__(128, 1)
       } else {
         tc::tmem_ld32(taddr + c0, v);
       }
-      if constexpr (kEpi == EPI_F16 || kEpi == EPI_RESIDUAL) {
+      if constexpr (kEpi == EPI_F16 || kEpi == EPI_RESIDUAL || kEpi == EPI_SWIGLU) {
+        // SWIGLU stages fp16(gate) and fp16(up) rows; the store loop pairs them
 #pragma unroll
         for (int k = 0; k < 32; ++k)
           if (c0 + k < a.bn) stg[(c0 + k) * width + t] = __float2half_rn(v[k]);
-      } else if constexpr (kEpi == EPI_SWIGLU) {
-        // rows are [gate g..g+15 | up g..g+15] groups of 32: lanes j and j^16 pair up
-        const int j = t & 31, feat = (t >> 5) * 16 + (j & 15);
-#pragma unroll 4
-        for (int k = 0; k < 32; ++k) {
-          const float u = __shfl_xor_sync(0xffffffffu, v[k], 16);
-          if (j < 16 && c0 + k < a.bn) {
-            const float g16 = __half2float(__float2half_rn(v[k]));
-            const float u16 = __half2float(__float2half_rn(u));
-            const float silu = __fdiv_rn(g16, __fadd_rn(1.0f, expf(-g16)));
-            stg[(c0 + k) * width + feat] = __float2half_rn(__fmul_rn(silu, u16));
-          }
-        }
       } else {  // EPI_ARGMAX: fp16 logits staged; rows past n_out as -inf
 #pragma unroll
         for (int k = 0; k < 32; ++k)
@@ -250,18 +246,51 @@ __global__ void __launch_bounds__(128, 1)
       }
     } else {
       // 16-byte segments: batch row bl, outputs out0 + 8c .. out0 + 8c + 7
-      const int out0 = tile * width;
+      constexpr int outs = kEpi == EPI_SWIGLU ? 64 : 128;  // outputs of this tile
+      const int out0 = tile * outs;
       const int n_valid = (kEpi == EPI_SWIGLU ? a.n_out / 2 : a.n_out) - out0;
-      constexpr int segs = width / 8;
-      for (int i = t; i < a.bn * segs; i += 128) {
-        const int bl = i / segs, c = i % segs, b = n0 + bl;
-        if (b >= a.batch || 8 * c >= n_valid) continue;
-        uint4 val = *reinterpret_cast<const uint4*>(stg + bl * width + 8 * c);
+      constexpr int segs = outs / 8;
+      // kU segments per thread per round: the residual loads of a round are all
+      // in flight before the first add (one dependent load per segment was the
+      // epilogue's critical path)
+      constexpr int kU = 4;
+      const int total = a.bn * segs;
+      for (int i0 = t; i0 < total; i0 += 128 * kU) {
+        uint4 rv[kU];
+        if constexpr (kEpi == EPI_RESIDUAL) {
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const int i = i0 + u * 128, bl = i / segs, c = i % segs, b = n0 + bl;
+            if (i < total && b < a.batch && 8 * c < n_valid)
+              rv[u] = *reinterpret_cast<const uint4*>(a.res + (size_t)b * a.ldy + out0 + 8 * c);
+          }
+        }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int i = i0 + u * 128, bl = i / segs, c = i % segs, b = n0 + bl;
+        if (i >= total || b >= a.batch || 8 * c >= n_valid) continue;
+        uint4 val;
+        if constexpr (kEpi == EPI_SWIGLU) {
+          // outputs 8c..8c+7 of the tile: weight rows [gate 16 | up 16] groups of 32
+          const int f = 8 * c, base = (f >> 4) * 32 + (f & 15);
+          const uint4 gq = *reinterpret_cast<const uint4*>(stg + bl * width + base);
+          const uint4 uq = *reinterpret_cast<const uint4*>(stg + bl * width + base + 16);
+          const __half* gh = reinterpret_cast<const __half*>(&gq);
+          const __half* uh = reinterpret_cast<const __half*>(&uq);
+          __half* o = reinterpret_cast<__half*>(&val);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float g16 = __half2float(gh[e]), u16 = __half2float(uh[e]);
+            const float silu = __fdiv_rn(g16, __fadd_rn(1.0f, expf(-g16)));
+            o[e] = __float2half_rn(__fmul_rn(silu, u16));
+          }
+        } else {
+          val = *reinterpret_cast<const uint4*>(stg + bl * width + 8 * c);
+        }
         const size_t off = (size_t)b * a.ldy + out0 + 8 * c;
         if constexpr (kEpi == EPI_RESIDUAL) {
-          const uint4 r = *reinterpret_cast<const uint4*>(a.res + off);
           __half2* pv = reinterpret_cast<__half2*>(&val);
-          const __half2* pr = reinterpret_cast<const __half2*>(&r);
+          const __half2* pr = reinterpret_cast<const __half2*>(&rv[u]);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 x = __half22float2(pv[e]), y = __half22float2(pr[e]);
@@ -269,6 +298,7 @@ __global__ void __launch_bounds__(128, 1)
           }
         }
         *reinterpret_cast<uint4*>(a.y + off) = val;
+      }
       }
     }
   }
@@ -609,9 +639,10 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   // batch blocks first (no partial sums), down to 32 rows. Prefill row counts
   // (bpad > 256) start from 256-row blocks: one launch covers every row, and
   // the weight slab of a tile is re-read by its row blocks from L2.
-  a.bn = a.bpad > 256 ? 256 : a.bpad;
+  const bool fixed_bn = a.bn >= 16 && a.bn <= 256 && a.bn % 16 == 0;  // caller's choice (tuning)
+  if (!fixed_bn) a.bn = a.bpad > 256 ? 256 : a.bpad;
   int nb = (a.bpad + a.bn - 1) / a.bn;
-  while (ntiles * nb < sms && a.bn % 32 == 0 && a.bn / 2 >= 32) {
+  while (!fixed_bn && ntiles * nb < sms && a.bn % 32 == 0 && a.bn / 2 >= 32) {
     a.bn /= 2;
     nb = (a.bpad + a.bn - 1) / a.bn;
   }
@@ -633,8 +664,11 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   a.kb_per_split = (kbs + a.nsplit - 1) / a.nsplit;
   a.nsplit = (kbs + a.kb_per_split - 1) / a.kb_per_split;
   if (a.nsplit > 1 && (!a.ws || !a.tickets)) return Status::err(SPOCK_ERR_INVALID, "gemm: split-K needs a workspace");
-  // Four stages: deeper rings cost CTAs per SM, which these short K loops need more.
-  a.stages = kMaxStages;
+  // Four stages by default: deeper rings cost CTAs per SM, which these short K loops need more.
+  const int stage_bytes = 128 * 128 + a.bn * 128;
+  if (a.stages < 1) a.stages = 4;
+  if (a.stages > kMaxStages) a.stages = kMaxStages;
+  while (a.stages > 2 && a.stages * stage_bytes > kRingBytes) --a.stages;
   const int smem = a.stages * (128 * 128 + a.bn * 128) + 2 * kMaxStages * 8 + 64 + 8 * 256 * 4 + 1024;
   dim3 grid(ntiles, a.nsplit, nb);
   {
