@@ -10,12 +10,16 @@
 //
 // Grid: (row tiles, K splits, batch blocks). Large batches are split over
 // batch blocks of bn >= 32 rows first (no partial sums: the CTAs of one row
-// tile share its weight slab through L2), then over K: with K splits every
-// CTA adds its fp32 partial tile into an accumulator with vector atomics
-// (L2-side, all splits in parallel); the last CTA of a tile (atomic ticket)
-// reads the sum once, clears it for the next launch and runs the epilogue.
-// The K split count is capped so partial traffic stays below the weight
-// traffic it parallelises.
+// tile share its weight slab through L2), then over K while the grid is
+// shorter than the SM count (one CTA streams its slab at a bounded rate, so a
+// short grid leaves HBM idle). Up to 8 K splits of a tile run as one
+// thread-block cluster: ranks 1.. park their fp32 partial tile in shared
+// memory and rank 0 adds them in rank order through distributed shared memory
+// (deterministic, no global traffic). More splits (small batches with long K)
+// add vector atomics into an L2-resident accumulator; the last CTA of a tile
+// (atomic ticket) reads the sum once, clears it for the next launch and runs
+// the epilogue, with the split count capped so partial traffic stays below
+// the weight traffic it parallelises.
 //
 // The epilogue stages the fp16 tile in shared memory (TMEM lanes are weight
 // rows) and writes it back, with the residual, in 16-byte row segments.
@@ -40,6 +44,7 @@ namespace spock {
 namespace {
 
 constexpr int kMaxStages = 12;
+constexpr int kMaxCluster = 8;  // portable thread-block cluster size
 constexpr int kRingBytes = 4 * (128 * 128 + 256 * 128);  // 192 KB: the ring never exceeds it
 constexpr uint32_t kWaitLimit = 1u << 25;
 
@@ -57,6 +62,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
           tc::smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// Thread-block cluster helpers (distributed shared memory, no TMA).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
 }
 
 template <int kEpi>
@@ -151,6 +171,10 @@ __global__ void __launch_bounds__(128, 1)
   if (!wait_spin(done, 0)) ok = false;
   if (__syncthreads_or(!ok)) {
     if (t == 0) atomicExch(a.err, 3);
+    if (a.csplit) {  // the cluster's two barriers stay matched; the leader's result is void
+      cluster_sync();
+      cluster_sync();
+    }
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 0) tc::tmem_dealloc(tb, ncols);
@@ -161,7 +185,23 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t taddr = tb + ((uint32_t)(warp * 32) << 16);
 
   bool finisher = true;
-  if (a.nsplit > 1) {
+  // cluster split: ranks 1.. leave their fp32 partial [bn][128] in their own
+  // shared memory; rank 0 adds them to its accumulator in rank order
+  const float* part = reinterpret_cast<const float*>(sm);
+  if (a.csplit) {
+    if (blockIdx.y != 0) {
+      float* mine = reinterpret_cast<float*>(sm);
+      for (int c0 = 0; c0 < a.bn; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(taddr + c0, v);
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (c0 + k < a.bn) mine[(c0 + k) * 128 + t] = v[k];
+      }
+    }
+    cluster_sync();
+    finisher = blockIdx.y == 0;
+  } else if (a.nsplit > 1) {
     // partial tile -> accumulator [row][n0 + col] (vector atomics, resolved in L2)
     float* wsp = a.ws + (size_t)row * a.bpad + n0;
     for (int c0 = 0; c0 < a.bn; c0 += 32) {
@@ -191,7 +231,7 @@ __global__ void __launch_bounds__(128, 1)
     constexpr int width = 128;  // staged weight rows (SWIGLU: gate and up, 64 outputs)
     for (int c0 = 0; c0 < a.bn; c0 += 32) {
       float v[32];
-      if (a.nsplit > 1) {
+      if (a.nsplit > 1 && !a.csplit) {
         float4* p = reinterpret_cast<float4*>(a.ws + (size_t)row * a.bpad + n0 + c0);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -208,6 +248,16 @@ __global__ void __launch_bounds__(128, 1)
         }
       } else {
         tc::tmem_ld32(taddr + c0, v);
+        if (a.csplit) {
+          for (int r = 1; r < a.nsplit; ++r) {
+            const uint32_t base = map_rank(tc::smem_u32(part), r);
+            float pv[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) pv[k] = c0 + k < a.bn ? ld_cluster_f32(base + ((c0 + k) * 128 + t) * 4) : 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] += pv[k];
+          }
+        }
       }
       if constexpr (kEpi == EPI_F16 || kEpi == EPI_RESIDUAL || kEpi == EPI_SWIGLU) {
         // SWIGLU stages fp16(gate) and fp16(up) rows; the store loop pairs them
@@ -302,6 +352,7 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
   }
+  if (a.csplit) cluster_sync();  // partials stay in place until the leader has read them
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tb, ncols);
@@ -578,8 +629,8 @@ Status map2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int b
 Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, cudaStream_t st) {
   if (a.k % 64 || a.bpad % 16 || a.bpad < 16 || a.batch > a.bpad || a.batch < 1)
     return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: k % 64, bpad a multiple of 16, batch <= bpad");
-  if (a.bpad > 256 && a.nsplit > 1)
-    return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: split-K needs bpad <= 256");
+  if (a.bpad > 256 && a.nsplit > kMaxCluster)
+    return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: bpad > 256 allows at most 8 K splits");
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15))
     return Status::err(SPOCK_ERR_INVALID, "gemm: operands must be 16-byte aligned");
   if (epi != EPI_ARGMAX) {
@@ -652,7 +703,13 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   if (s.code) return s;
   s = map2d(&mx, x, a.bpad, a.k, a.bn);
   if (s.code) return s;
-  if (a.nsplit < 1 && nb > 1) a.nsplit = 1;  // large batch: compute-heavy tiles, no partial sums
+  if (a.nsplit < 1 && nb > 1) {
+    // blocked batch: split K only to fill the SMs (a CTA streams one weight
+    // slab at a bounded rate), in clusters that reduce on chip
+    const int want = (sms + ntiles * nb - 1) / (ntiles * nb);
+    a.nsplit = want < kMaxCluster ? want : kMaxCluster;
+    if (a.nsplit > kbs / 2) a.nsplit = kbs / 2 > 1 ? kbs / 2 : 1;
+  }
   if (a.nsplit < 1) {  // enough CTAs to stream the weights from every SM ...
     int want = (sms + ntiles * nb - 1) / (ntiles * nb);
     // ... but no more partial-tile traffic (128 x bn fp32) than weight traffic
@@ -663,7 +720,11 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   }
   a.kb_per_split = (kbs + a.nsplit - 1) / a.nsplit;
   a.nsplit = (kbs + a.kb_per_split - 1) / a.kb_per_split;
-  if (a.nsplit > 1 && (!a.ws || !a.tickets)) return Status::err(SPOCK_ERR_INVALID, "gemm: split-K needs a workspace");
+  // up to 8 splits reduce inside a cluster (deterministic, no workspace);
+  // more go through the atomic workspace
+  a.csplit = a.nsplit > 1 && a.nsplit <= kMaxCluster;
+  if (a.nsplit > 1 && !a.csplit && (!a.ws || !a.tickets))
+    return Status::err(SPOCK_ERR_INVALID, "gemm: split-K needs a workspace");
   // Four stages by default: deeper rings cost CTAs per SM, which these short K loops need more.
   const int stage_bytes = 128 * 128 + a.bn * 128;
   if (a.stages < 1) a.stages = 4;
@@ -677,10 +738,13 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     std::call_once(once, [] { prep = gemm_prepare(); });
     if (prep.code) return prep;
   }
-#define SPOCK_GEMM_CASE(E)                                                                          \
-  case E: {                                                                                         \
-    launch_k(gemm_swapab_kernel<E>, grid, dim3(128), smem, st, mw, mx, a);                          \
-    break;                                                                                          \
+#define SPOCK_GEMM_CASE(E)                                                                            \
+  case E: {                                                                                           \
+    if (a.csplit)                                                                                     \
+      launch_k_cluster(gemm_swapab_kernel<E>, grid, dim3(128), dim3(1, a.nsplit, 1), smem, st, mw, mx, a); \
+    else                                                                                              \
+      launch_k(gemm_swapab_kernel<E>, grid, dim3(128), smem, st, mw, mx, a);                          \
+    break;                                                                                            \
   }
   switch (epi) {
     SPOCK_GEMM_CASE(EPI_F16)

@@ -13,11 +13,13 @@ struct GemmArgs {
   int n_out;         // weight rows
   int k;             // inner dim, multiple of 64
   int batch;         // real batch rows
-  int bpad;          // padded batch rows of x, multiple of 16, <= 256
+  int bpad;          // padded batch rows of x, multiple of 16
   int bn;            // batch rows per CTA (MMA N): 0 = launch_gemm chooses
   int kb_per_split;  // 64-wide k blocks per split; set by launch_gemm
   int nsplit;        // K splits; 0 = let launch_gemm choose
   int stages;        // TMA ring depth: 0 = launch_gemm chooses (4), capped by its 192 KB ring
+  int csplit;        // set by launch_gemm: the K splits of a tile form one thread-block
+                     // cluster and reduce their partials through distributed shared memory
   __half* y;         // [batch][ldy]; ldy % 8 == 0, 16-byte aligned
   int ldy;
   const __half* res;  // RESIDUAL: [batch][ldy]

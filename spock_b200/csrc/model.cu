@@ -293,7 +293,7 @@ Status gemm_rows(spock_model* m, int epi, const void* x, const void* w, int n_ou
   a.k = k;
   a.batch = R;
   a.bpad = (R + 15) / 16 * 16;
-  a.nsplit = 1;
+  a.nsplit = 0;  // launch_gemm splits K (in clusters) only to fill the SMs
   a.y = (__half*)y;
   a.ldy = ldy;
   a.res = (const __half*)res;
