@@ -252,7 +252,10 @@ def bench_chunk(args, ws, rank, local):
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm" if t_hbm >= t_tc else "tensor", "achieved": round(achieved_gbs, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(achieved_gbs / hbm, 4),
-                     "traffic": None, "peak_source": pk,
+                     # DRAM read + write per launch from one ncu capture (160 pairs x 8192 tokens:
+                     # 1.337 GB), scaled by token-heads to this launch
+                     "traffic": int(1.337e9 / (160 * 8192) * B * 16 * S), "traffic_source": "ncu, scaled",
+                     "peak_source": pk,
                      "tensor": {"achieved": round(achieved_tf, 1), "peak": tf, "unit": "TFLOP/s",
                                 "frac": round(achieved_tf / tf, 4)},
                      "kernel_ms": round(kern_ms, 4), "alg_bytes": alg_bytes, "alg_flops": alg_flops},
@@ -327,7 +330,10 @@ def bench_decode(args, ws, rank, local):
                    "l2": "%d independent layer states (%.0f MB) larger than L2" % (layers, layers * B * 1.05)},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": pk,
+                     # DRAM read + write of one launch from an ncu capture at batch 64 (71.4 + 13.1 MB;
+                     # part of the written state is still in L2 when the launch ends), scaled by batch
+                     "frac": round(gbs / hbm, 4), "traffic": int(84.5e6 * B / 64), "traffic_source": "ncu, scaled",
+                     "peak_source": pk,
                      "kernel_us": round(per_launch_ms * 1e3, 2), "alg_bytes": alg},
         "clocks": clk.summary(),
     }
