@@ -4,8 +4,9 @@
 // lm_head_tiled.comp:40-86). Their outputs are fp16-rounded; so are these.
 //
 // Swap-AB tcgen05 GEMM: a 128-row slab of W is the M=128 operand (K-major, TMA,
-// 128B swizzle) and the batch of activation rows is the N operand (16..256), so
+// 128B swizzle) and a block of up to 256 activation rows is the N operand, so
 // one pass over the weights serves the whole batch; decode is HBM-bound on W.
+// Prefill row counts run as many such blocks in one launch.
 // Accumulators live in TMEM (lane = weight row, column = batch row).
 //
 // Grid: (row tiles, K splits, batch blocks). Large batches are split over
