@@ -80,13 +80,16 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   return v;
 }
 
-template <int kEpi>
+// kKB: 64-wide k blocks per ring stage. Each stage round (TMA, MMA, commit,
+// hand-off) has a fixed cost, so long unsplit K loops at prefill row counts
+// take two blocks per stage; short decode loops keep one (more CTAs per SM).
+template <int kEpi, int kKB>
 __global__ void __launch_bounds__(128, 1)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                        GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
-  const int a_bytes = 128 * 128, b_bytes = a.bn * 128, stage_bytes = a_bytes + b_bytes;
+  const int a_bytes = 128 * 128, b_bytes = a.bn * 128, sub_bytes = a_bytes + b_bytes, stage_bytes = kKB * sub_bytes;
   const int kStages = a.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * stage_bytes);
   uint64_t* empty = full + kMaxStages;
@@ -98,6 +101,8 @@ __global__ void __launch_bounds__(128, 1)
   const int tile = blockIdx.x, split = blockIdx.y, n0 = blockIdx.z * a.bn;
   const int kb0 = split * a.kb_per_split;
   const int nkb = min(a.kb_per_split, a.k / 64 - kb0);
+  const int nst = (nkb + kKB - 1) / kKB;  // ring stages of this CTA
+  auto subs = [&](int i) { return min(kKB, nkb - i * kKB); };
   uint32_t ncols = 32;
   while ((int)ncols < a.bn) ncols <<= 1;
 
@@ -124,36 +129,43 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0 && lane == 0) {  // TMA producer
     // The weights do not depend on the previous kernel: the first stages'
     // weight tiles stream while it drains; activations after pdl_wait.
-    const int pre = nkb < kStages ? nkb : kStages;
+    const int pre = nst < kStages ? nst : kStages;
     for (int i = 0; i < pre; ++i) {
-      tc::mbar_arrive_expect_tx(&full[i], stage_bytes);
-      tma_load_2d(sm + i * stage_bytes, &tmw, &full[i], (kb0 + i) * 64, tile * 128);
+      tc::mbar_arrive_expect_tx(&full[i], subs(i) * sub_bytes);
+      for (int j = 0; j < subs(i); ++j)
+        tma_load_2d(sm + i * stage_bytes + j * sub_bytes, &tmw, &full[i], (kb0 + i * kKB + j) * 64, tile * 128);
     }
     pdl_wait();
     pdl_launch();
-    for (int i = 0; i < pre; ++i) tma_load_2d(sm + i * stage_bytes + a_bytes, &tmx, &full[i], (kb0 + i) * 64, n0);
-    for (int i = pre; i < nkb && ok; ++i) {
+    for (int i = 0; i < pre; ++i)
+      for (int j = 0; j < subs(i); ++j)
+        tma_load_2d(sm + i * stage_bytes + j * sub_bytes + a_bytes, &tmx, &full[i], (kb0 + i * kKB + j) * 64, n0);
+    for (int i = pre; i < nst && ok; ++i) {
       const int s = i % kStages;
       ok = wait_spin(&empty[s], ((i / kStages) - 1) & 1);
       if (!ok) break;
       uint8_t* st = sm + s * stage_bytes;
-      tc::mbar_arrive_expect_tx(&full[s], stage_bytes);
-      tma_load_2d(st, &tmw, &full[s], (kb0 + i) * 64, tile * 128);
-      tma_load_2d(st + a_bytes, &tmx, &full[s], (kb0 + i) * 64, n0);
+      tc::mbar_arrive_expect_tx(&full[s], subs(i) * sub_bytes);
+      for (int j = 0; j < subs(i); ++j) {
+        tma_load_2d(st + j * sub_bytes, &tmw, &full[s], (kb0 + i * kKB + j) * 64, tile * 128);
+        tma_load_2d(st + j * sub_bytes + a_bytes, &tmx, &full[s], (kb0 + i * kKB + j) * 64, n0);
+      }
     }
   } else if (warp == 1 && lane == 0) {  // MMA issuer
     const uint32_t idesc = tc::idesc_f16(128, a.bn, false, false);
     const uint32_t sbase = tc::smem_u32(sm);
-    for (int i = 0; i < nkb && ok; ++i) {
+    for (int i = 0; i < nst && ok; ++i) {
       const int s = i % kStages;
       ok = wait_spin(&full[s], (i / kStages) & 1);
       if (!ok) break;
       tc::tc_fence_after();
-      const uint32_t st = sbase + s * stage_bytes;
+      for (int j = 0; j < subs(i); ++j) {
+        const uint32_t st = sbase + s * stage_bytes + j * sub_bytes;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        tc::mma_f16(tb, tc::sdesc(st + kk * 32, 16, 1024), tc::sdesc(st + a_bytes + kk * 32, 16, 1024), idesc,
-                    (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_f16(tb, tc::sdesc(st + kk * 32, 16, 1024), tc::sdesc(st + a_bytes + kk * 32, 16, 1024), idesc,
+                      (i > 0 || j > 0 || kk > 0) ? 1u : 0u);
+      }
       tc::mma_commit(&empty[s]);
     }
     tc::mma_commit(done);
@@ -727,11 +739,13 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   if (a.nsplit > 1 && !a.csplit && (!a.ws || !a.tickets))
     return Status::err(SPOCK_ERR_INVALID, "gemm: split-K needs a workspace");
   // Four stages by default: deeper rings cost CTAs per SM, which these short K loops need more.
-  const int stage_bytes = 128 * 128 + a.bn * 128;
+  // Unsplit prefill row counts take two k blocks per stage (kKB = 2).
+  const int kb_stage = a.bpad > 256 && a.nsplit == 1 ? 2 : 1;
+  const int stage_bytes = kb_stage * (128 * 128 + a.bn * 128);
   if (a.stages < 1) a.stages = 4;
   if (a.stages > kMaxStages) a.stages = kMaxStages;
   while (a.stages > 2 && a.stages * stage_bytes > kRingBytes) --a.stages;
-  const int smem = a.stages * (128 * 128 + a.bn * 128) + 2 * kMaxStages * 8 + 64 + 8 * 256 * 4 + 1024;
+  const int smem = a.stages * stage_bytes + 2 * kMaxStages * 8 + 64 + 8 * 256 * 4 + 1024;
   dim3 grid(ntiles, a.nsplit, nb);
   {
     static std::once_flag once;
@@ -739,13 +753,15 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     std::call_once(once, [] { prep = gemm_prepare(); });
     if (prep.code) return prep;
   }
-#define SPOCK_GEMM_CASE(E)                                                                            \
-  case E: {                                                                                           \
-    if (a.csplit)                                                                                     \
-      launch_k_cluster(gemm_swapab_kernel<E>, grid, dim3(128), dim3(1, a.nsplit, 1), smem, st, mw, mx, a); \
-    else                                                                                              \
-      launch_k(gemm_swapab_kernel<E>, grid, dim3(128), smem, st, mw, mx, a);                          \
-    break;                                                                                            \
+#define SPOCK_GEMM_CASE(E)                                                                               \
+  case E: {                                                                                              \
+    if (a.csplit)                                                                                        \
+      launch_k_cluster(gemm_swapab_kernel<E, 1>, grid, dim3(128), dim3(1, a.nsplit, 1), smem, st, mw, mx, a); \
+    else if (kb_stage == 2)                                                                              \
+      launch_k(gemm_swapab_kernel<E, 2>, grid, dim3(128), smem, st, mw, mx, a);                          \
+    else                                                                                                 \
+      launch_k(gemm_swapab_kernel<E, 1>, grid, dim3(128), smem, st, mw, mx, a);                          \
+    break;                                                                                               \
   }
   switch (epi) {
     SPOCK_GEMM_CASE(EPI_F16)
@@ -764,10 +780,14 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
 Status gemm_prepare() {
   const int smem = kRingBytes + 2 * kMaxStages * 8 + 64 + 8 * 256 * 4 + 1024;
   cudaError_t e = cudaSuccess;
-  e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+#define SPOCK_GEMM_ATTR(E)                                                                                      \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<E, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<E, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  SPOCK_GEMM_ATTR(EPI_F16)
+  SPOCK_GEMM_ATTR(EPI_RESIDUAL)
+  SPOCK_GEMM_ATTR(EPI_SWIGLU)
+  SPOCK_GEMM_ATTR(EPI_ARGMAX)
+#undef SPOCK_GEMM_ATTR
   const int gsm = 96 * 1024;  // staged activations of the small-batch path
 #define SPOCK_GEMV_ATTR(E)                                                                                        \
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<E, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsm); \
