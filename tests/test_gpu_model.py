@@ -56,7 +56,9 @@ def test_teacher_forced_steps(gpu_model, weights):
     assert checked > 0
 
 
-def test_generate_token_serial_prefill(gpu_model, weights):
+def test_generate_matches_token_serial_oracle(gpu_model, weights):
+    """spock_model_generate (layer-major prefill, then graph-replayed greedy
+    steps) against the oracle fed the same prompt token by token."""
     cpu = oracle.Model(weights, LAYERS, VOCAB, MAXSEQ)
     B, P, N = 2, 5, 4
     prompt = np.random.default_rng(1).integers(0, VOCAB, (B, P)).astype(np.int32)
