@@ -12,7 +12,7 @@ over the whole batch. Under torchrun each rank runs its own 64 sequences
            max over ranks
   e2e      the same metric through the public API with pinned host buffers:
            H2D of q/k/v/g/beta and D2H of core_attn_out + final_state timed
-  roofline dominant kernel (chunk_rule_kernel) against MEASURED_PEAKS.json
+  roofline dominant kernel (chunk_pipe_kernel) against MEASURED_PEAKS.json
   cpu_baseline the reference's own run_deltanet_chunk_rule (oracle/_ref) or
            the oracle port, on a bounded sample, all host threads
 

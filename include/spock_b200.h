@@ -55,7 +55,9 @@ uint64_t spock_kernel_launch_count(void);
  * decode and projection kernels use, capped at `polls` polls. The wait gives
  * up, records the timeout in the context's error word and the kernel returns,
  * so the next spock_sync reports SPOCK_ERR_TIMEOUT and the context stays
- * usable. No GPU fault is involved. */
+ * usable. No GPU fault is involved. With ctx == NULL the wait records into the
+ * error word of spock_chunk_prefill_noalloc's fixed array on the current
+ * device instead, which spock_noalloc_sync then reports. */
 int spock_selftest_wait_timeout(spock_ctx* ctx, uint32_t polls, void* stream);
 
 /* ------------------------------------------------------------------------ */
@@ -93,6 +95,10 @@ typedef struct {
  *
  * Internally the intra-chunk contractions run on tcgen05 tensor cores with
  * fp16 operands and fp32 accumulation in TMEM; the recurrent state is fp32.
+ * Range: bf16 q/k/v are converted to fp16 operands, so values must lie in
+ * fp16's range (|x| <= 65504; larger magnitudes become inf) and values below
+ * 2^-14 lose precision as fp16 subnormals. The model's inputs (L2-normalised
+ * q/k, O(1) v) are far inside it; fp32 inputs are staged as fp16 hi/lo pairs.
  * fp32 inputs, or use_qk_l2norm=1, are first staged as fp16 in the context's
  * device scratch (grown on demand with cudaMalloc).
  */
@@ -117,13 +123,32 @@ int spock_chunk_prefill(spock_ctx* ctx, const spock_chunk_desc* desc, const void
  * current device and calls no cudaMalloc, cudaFree or other allocating routine.
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Under CUDA's lazy module loading that first lookup is also when the driver
+ * loads the library's device code and commits the 16 MiB array on that
+ * device, so the first call (or first spock_noalloc_sync) on a device costs
+ * 16 MiB of device memory once; later calls allocate nothing.
  * All calls on a device share the array, so calls whose work overlaps on the
  * GPU (different streams, no ordering between them) race and must not be made.
+ *
+ * A bounded device-side wait that gives up does not fail the call (the work is
+ * asynchronous); it sets an error word at the head of the fixed array, which
+ * stays set until spock_noalloc_sync reads it. Outputs of a call followed by
+ * a SPOCK_ERR_TIMEOUT from spock_noalloc_sync are invalid.
  */
 int spock_chunk_prefill_noalloc(const spock_chunk_desc* desc, const void* q, const void* k,
                                 const void* v, const float* g, const float* beta,
                                 const float* init_state, void* core_out, float* final_state,
                                 void* stream);
+
+/*
+ * Companion of spock_chunk_prefill_noalloc (no counterpart in the reference):
+ * synchronises `stream`, then reads the fixed array's error word on the
+ * current device. Returns SPOCK_ERR_TIMEOUT (text in spock_last_error(NULL))
+ * when a kernel of an earlier allocation-free call reported a bounded wait
+ * that gave up, and clears the word only after reading it; SPOCK_OK otherwise.
+ * Allocates nothing.
+ */
+int spock_noalloc_sync(void* stream);
 
 /*
  * Last-token extraction of core_attn_out to fp16 by truncation with
@@ -155,7 +180,7 @@ typedef struct {
 /*
  * One decode token for `batch` independent sequences through one DeltaNet
  * layer's mixer core. Replaces the fused pair deltanet_conv_l2_qk.comp
- * (:41-110) + deltanet_recurrent_gbeta_norm_gate.comp (:202-335) dispatched
+ * (:41-110) + deltanet_recurrent_gbeta_norm_gate.comp (:91-224) dispatched
  * from DecodeSession::decode (src/runtime/vk_session.cpp:2878-2883, 3213-3218),
  * fused into ONE kernel (one CTA per (sequence, head)).
  *
@@ -204,8 +229,17 @@ typedef struct {
   float rope_theta;   /* 1e7 (vk_session.cpp:335) */
 } spock_model_desc;
 
+/* ctx (nullable) supplies the error word of the model's bounded device waits:
+ * with a ctx, spock_sync(ctx, ...) reports a model kernel's timeout as well;
+ * spock_model_sync reads the same word either way. */
 int spock_model_create(spock_ctx* ctx, const spock_model_desc* desc, spock_model** out);
 int spock_model_destroy(spock_model* m);
+/* Blocks until the stream's work is done; returns SPOCK_ERR_TIMEOUT (text in
+ * spock_model_last_error) when a kernel of this model's prefill, step or
+ * generate reported a bounded wait that gave up, clearing the word after
+ * reading it. The outputs of that work are invalid; spock_model_reset clears
+ * the state and the projection workspace before the session is used again. */
+int spock_model_sync(spock_model* m, void* stream);
 const char* spock_model_last_error(const spock_model* m);
 /* Uploads one tensor by the reference artifact's role name (weight_loader.hpp
  * find_by_role: "embedding", "final_norm", "layer.N.delta_in_proj_qkv", ...);

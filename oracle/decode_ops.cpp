@@ -4,7 +4,7 @@
 // The reference has no CPU decode (src/reference/qwen35_cpu_reference.cpp:14-25
 // is a placeholder), so this restates its GLSL shaders directly:
 //   oracle_conv_l2_qk   <- shaders/deltanet_conv_l2_qk.comp:48-110
-//   oracle_rec_norm_gate <- shaders/deltanet_recurrent_gbeta_norm_gate.comp:212-335
+//   oracle_rec_norm_gate <- shaders/deltanet_recurrent_gbeta_norm_gate.comp:91-224
 //   oracle_recurrent_raw <- shaders/deltanet_recurrent.comp:55-125 (g/beta read
 //                           from the state tail, raw output, no norm-gate)
 // fp16 storage points are reproduced exactly (conv output stored as fp16

@@ -38,7 +38,7 @@ EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
             "spock_deltanet_decode_step", "spock_deltanet_recurrent", "spock_chunk_prefill_noalloc",
             "spock_model_create", "spock_model_destroy", "spock_model_last_error", "spock_model_set_weight",
             "spock_model_reset", "spock_model_step", "spock_model_generate", "spock_model_load_artifact",
-            "spock_model_prefill"]
+            "spock_model_prefill", "spock_noalloc_sync", "spock_model_sync"]
 
 
 class SpockError(RuntimeError):
@@ -88,6 +88,7 @@ def lib():
         L.spock_selftest_wait_timeout.argtypes = [vp, ctypes.c_uint32, vp]
         L.spock_chunk_prefill.argtypes = [vp, ctypes.POINTER(ChunkDesc)] + [vp] * 9
         L.spock_chunk_prefill_noalloc.argtypes = [ctypes.POINTER(ChunkDesc)] + [vp] * 9
+        L.spock_noalloc_sync.argtypes = [vp]
         L.spock_chunk_last_to_fp16.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp]
         L.spock_deltanet_decode_step.argtypes = [vp, ctypes.POINTER(DnLayer), i64] + [vp] * 9
         L.spock_deltanet_recurrent.argtypes = [vp, i64, i32, i32, i32] + [vp] * 8
@@ -316,6 +317,7 @@ def _model_lib():
         L.spock_model_step.argtypes = [vp, vp, vp, vp, vp]
         L.spock_model_generate.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, vp, vp]
         L.spock_model_prefill.argtypes = [vp, vp, ctypes.c_int32, vp, vp, vp]
+        L.spock_model_sync.argtypes = [vp, vp]
         L._model_types = True
     return L
 
@@ -350,6 +352,11 @@ class Model:
     def load_artifact(self, repack_dir):
         """Loads a repacked text artifact (text_repack_manifest.json + text_weights.bin)."""
         self._check(self.L.spock_model_load_artifact(self.h, os.fsencode(repack_dir)))
+
+    def sync(self, stream=None):
+        """Waits for the stream; raises SpockError(SPOCK_ERR_TIMEOUT) when one of this
+        model's kernels reported a bounded wait that gave up (spock_model_sync)."""
+        self._check(self.L.spock_model_sync(self.h, _stream(stream)))
 
     def reset(self, batch):
         self.batch = batch

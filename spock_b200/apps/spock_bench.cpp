@@ -3,8 +3,8 @@
 // Same flags: --mode pp520|tg128|correctness [--json|--csv] [--warmup N]
 // [--runs N] [--output PATH]. Here every mode runs on the GPU with CUDA-event
 // timing over a seeded random-init Qwen3.5-0.8B-layout model:
-//   pp520        520-token prompt, token-serial prefill (layer_major_prefill
-//                semantics): ms and tok/s
+//   pp520        520-token prompt through the layer-major prefill
+//                (layer_major_prefill semantics, batched over the prompt): ms and tok/s
 //   tg128        128 greedy decode tokens after an 8-token prompt
 //   correctness  the same prompt decoded twice must give identical tokens,
 //                and a chunk-rule call must produce finite outputs

@@ -30,6 +30,7 @@ Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, co
 Status launch_last_to_fp16(int64_t batch, int64_t H, int64_t S, int64_t V, const float* core,
                            void* out, cudaStream_t stream);
 Status launch_wait_timeout_selftest(uint32_t polls, int* err, cudaStream_t stream);
+Status noalloc_err_word(int** out);
 }  // namespace spock
 
 struct spock_ctx {
@@ -45,6 +46,10 @@ std::string g_err;  // context-less errors
 }  // namespace
 
 namespace spock {
+// The context's device error word (bounded waits that gave up), shared with
+// model sessions created on the context so spock_sync reports their timeouts.
+int* ctx_err_word(spock_ctx* ctx) { return ctx ? ctx->d_err_flag : nullptr; }
+
 // Records the text returned by spock_last_error(NULL) (context-less calls).
 void record_global_error(const std::string& msg) {
   std::lock_guard<std::mutex> lk(g_err_mu);
@@ -138,9 +143,14 @@ __attribute__((visibility("default"))) uint64_t spock_kernel_launch_count(void) 
 }
 
 __attribute__((visibility("default"))) int spock_selftest_wait_timeout(spock_ctx* ctx, uint32_t polls, void* stream) {
-  if (!ctx) return fail(nullptr, SPOCK_ERR_INVALID, "spock_selftest_wait_timeout: ctx is NULL");
   if (polls == 0 || polls > (1u << 20))
     return fail(ctx, SPOCK_ERR_INVALID, "spock_selftest_wait_timeout: polls must be in [1, 2^20]");
+  if (!ctx) {  // the allocation-free entry point's error word, on the current device
+    int* word = nullptr;
+    spock::Status s = spock::noalloc_err_word(&word);
+    if (!s.code) s = spock::launch_wait_timeout_selftest(polls, word, (cudaStream_t)stream);
+    return finish(nullptr, s);
+  }
   DeviceGuard g(ctx->device);
   return finish(ctx, spock::launch_wait_timeout_selftest(polls, ctx->d_err_flag, (cudaStream_t)stream));
 }

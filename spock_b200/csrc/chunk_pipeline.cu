@@ -8,12 +8,12 @@
 // n+1's independent part runs on the PREP warpgroup while chunk n's recurrence
 // runs on the REC warpgroup:
 //
-//   warps 0-3  PREP : bf16->fp16, g scan, G1 epilogue (P, N), fp32 solve,
-//                     T diag(beta e^g) -> MMA, -W and Q' and T diag(beta) -> smem
-//   warps 4-7  REC  : S -> S16 (+ decay of S in TMEM), v_new epilogue, output
-//                     epilogue and stores, initial / final state
-//   warp 8     TMA  : q/k tiles (2-stage ring) and v (1 stage)
-//   warp 9     MMA  : one thread issues every tcgen05.mma in dependency order
+//   warps 0-7   PREP : g scan, G1 epilogue (P, N), fp32 solve,
+//                      T diag(beta e^g) -> MMA, -W and Q' and T diag(beta) -> smem
+//   warps 8-11  REC  : bf16->fp16 of V, S -> S16 (+ decay of S in TMEM), v_new
+//                      epilogue, output epilogue and stores, initial / final state
+//   warp 12     TMA  : q/k tiles (2-stage ring) and v (1 stage)
+//   warp 13     MMA  : one thread issues every tcgen05.mma in dependency order
 //
 // CTAs are persistent (grid <= #SMs) and walk a stream of (pair, chunk) items:
 // pair p = blockIdx.x + i*gridDim.x, all of its chunks in order, so the prep

@@ -503,16 +503,6 @@ __global__ void last_to_fp16_kernel(const float* __restrict__ core, uint16_t* __
 
 // ---- host side ---------------------------------------------------------------
 
-// SPOCK_CHUNK_SERIAL=1 selects the serial kernel for 16-bit inputs too
-// (diagnostics: both kernels implement the same contract).
-bool serial_forced() {
-  static const bool v = [] {
-    const char* e = getenv("SPOCK_CHUNK_SERIAL");
-    return e && e[0] == '1';
-  }();
-  return v;
-}
-
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -561,10 +551,8 @@ template <bool kBf16In, int kOut, bool kPrecise>
 Status launch_kernel(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                      const CUtensorMap& mvlo, const float* g, const float* beta, const float* init,
                      void* out, float* final_state, int64_t pairs, int S, int* err, cudaStream_t st) {
-  if constexpr (!kPrecise) {
-    if (!serial_forced())
-      return launch_chunk_pipeline<kBf16In, kOut>(mq, mk, mv, g, beta, init, out, final_state, pairs, S, err, st);
-  }
+  if constexpr (!kPrecise)
+    return launch_chunk_pipeline<kBf16In, kOut>(mq, mk, mv, g, beta, init, out, final_state, pairs, S, err, st);
   auto kern = chunk_rule_kernel<kBf16In, kOut, kPrecise>;
   const int smem = kPrecise ? SMEM_BYTES_PRECISE : SMEM_BYTES;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -735,10 +723,11 @@ Status chunk_prefill_noalloc(const spock_chunk_desc& d, const void* q, const voi
   Status s = noalloc_scratch(&base_v);
   if (s.code) return s;
   unsigned char* base = static_cast<unsigned char*>(base_v);
+  // The kernels only ever set this word (a bounded wait that gave up). It is
+  // not cleared here: spock_noalloc_sync reads it and clears it after reading,
+  // so a timeout stays visible until the caller has looked. The staged
+  // tensors are fully rewritten by every call.
   int* err_flag = reinterpret_cast<int*>(base);
-  // The error word must start at zero; the staged tensors are fully rewritten.
-  cudaError_t e = cudaMemsetAsync(err_flag, 0, sizeof(int), stream);
-  if (e != cudaSuccess) return cuda_status(e, "spock_chunk_prefill_noalloc: cudaMemsetAsync");
 
   const void *q16 = q, *k16 = k, *v16 = v, *vlo16 = nullptr;
   bool bf16 = d.dtype_in == SPOCK_BF16;
@@ -788,7 +777,40 @@ Status chunk_prefill_noalloc(const spock_chunk_desc& d, const void* q, const voi
   return Status::err(SPOCK_ERR_INVALID, "chunk prefill: unknown dtype");
 }
 }  // namespace
+
+// Device address of the fixed array's error word on the current device (the
+// word the allocation-free entry point's kernels set when a bounded wait
+// gives up). Used by spock_noalloc_sync and the context-free self-test.
+Status noalloc_err_word(int** out) {
+  void* base = nullptr;
+  Status s = noalloc_scratch(&base);
+  if (s.code) return s;
+  *out = static_cast<int*>(base);
+  return Status::ok();
+}
+
+Status noalloc_sync(cudaStream_t stream) {
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_status(e, "spock_noalloc_sync: cudaStreamSynchronize");
+  int* word = nullptr;
+  Status s = noalloc_err_word(&word);
+  if (s.code) return s;
+  int flag = 0;
+  e = cudaMemcpy(&flag, word, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "spock_noalloc_sync: reading the error word");
+  if (!flag) return Status::ok();
+  e = cudaMemset(word, 0, sizeof(int));  // cleared only now that it has been read
+  if (e != cudaSuccess) return cuda_status(e, "spock_noalloc_sync: clearing the error word");
+  return Status::err(SPOCK_ERR_TIMEOUT, "spock_noalloc_sync: a kernel's bounded wait gave up (code " +
+                                            std::to_string(flag) + ")");
+}
 }  // namespace spock
+
+extern "C" __attribute__((visibility("default"))) int spock_noalloc_sync(void* stream) {
+  spock::Status s = spock::noalloc_sync((cudaStream_t)stream);
+  if (s.code) spock::record_global_error(s.msg);
+  return s.code;
+}
 
 extern "C" __attribute__((visibility("default"))) int spock_chunk_prefill_noalloc(
     const spock_chunk_desc* d, const void* q, const void* k, const void* v, const float* g,

@@ -187,6 +187,23 @@ __global__ void __launch_bounds__(128, 1)
     if (a.csplit) {  // the cluster's two barriers stay matched; the leader's result is void
       cluster_sync();
       cluster_sync();
+    } else if (a.nsplit > 1) {
+      // Still take part in the tile's ticket, so it returns to zero; if this
+      // CTA is the last one, it clears the accumulator slice the others added
+      // to (the result is void either way, but the next launch starts clean).
+      __threadfence();
+      __syncthreads();
+      if (t == 0) {
+        int* ticket_p = a.tickets + tile * gridDim.z + blockIdx.z;
+        const int ticket = atomicAdd(ticket_p, 1);
+        *s_last = (ticket == a.nsplit - 1);
+        if (*s_last) *ticket_p = 0;
+      }
+      __syncthreads();
+      if (*s_last) {
+        float* wsp = a.ws + (size_t)(tile * 128 + t) * a.bpad + n0;
+        for (int c = 0; c < a.bn; ++c) __stcg(wsp + c, 0.f);
+      }
     }
     tc::tc_fence_before();
     __syncthreads();

@@ -69,6 +69,7 @@ __global__ void copy_col_kernel(int* dst, int dst_stride, int dst_off, const int
 }  // namespace
 
 Status gemm_prepare();
+int* ctx_err_word(spock_ctx* ctx);
 Status launch_dn_prefill_conv(const void* proj, int ld, int batch, int T, int H, const void* conv_w,
                               const void* conv_old, void* conv_new, const float* a_log_bias, void* q, void* k, void* v,
                               float* g, float* beta, cudaStream_t st);
@@ -105,10 +106,13 @@ struct spock_model {
   int bpad = 16, batch = 0;
   void *h = nullptr, *x = nullptr, *proj = nullptr, *mix = nullptr, *mlp = nullptr, *q = nullptr, *gate = nullptr;
   float *ws = nullptr;
+  size_t ws_bytes = 0, tickets_bytes = 0;
   int* tickets = nullptr;
   float* amax_val = nullptr;
   int* amax_idx = nullptr;
-  int *tok_in = nullptr, *tok_out = nullptr, *pos = nullptr, *err_flag = nullptr;
+  int *tok_in = nullptr, *tok_out = nullptr, *pos = nullptr;
+  int* err_flag = nullptr;      // the context's error word, else own_err
+  int* own_err = nullptr;
   // state
   float* dn_state = nullptr;
   void* conv_state = nullptr;
@@ -438,7 +442,6 @@ extern "C" {
 
 __attribute__((visibility("default"))) int spock_model_create(spock_ctx* ctx, const spock_model_desc* d,
                                                               spock_model** out) {
-  (void)ctx;
   if (!out || !d) return SPOCK_ERR_INVALID;
   *out = nullptr;
   if (d->num_layers <= 0 || d->num_layers % 4 || d->vocab <= 0 || d->max_batch <= 0 || d->max_batch > 256 ||
@@ -463,14 +466,17 @@ __attribute__((visibility("default"))) int spock_model_create(spock_ctx* ctx, co
   A(&m->q, (size_t)B * QH * HD * 2);
   A(&m->gate, (size_t)B * QH * HD * 2);
   // split-K accumulator: one 128 x bpad fp32 tile per weight-row tile of the largest split GEMM
-  A(&m->ws, (size_t)((2 * INTER + 127) / 128 + (DN_IN + 127) / 128) * 128 * B * 4);
-  A(&m->tickets, (size_t)((d->vocab + 127) / 128 + 64) * 4);
+  m->ws_bytes = (size_t)((2 * INTER + 127) / 128 + (DN_IN + 127) / 128) * 128 * B * 4;
+  m->tickets_bytes = (size_t)((d->vocab + 127) / 128 + 64) * 4;
+  A(&m->ws, m->ws_bytes);
+  A(&m->tickets, m->tickets_bytes);
   A(&m->amax_val, (size_t)((d->vocab + 127) / 128) * B * 4);
   A(&m->amax_idx, (size_t)((d->vocab + 127) / 128) * B * 4);
   A(&m->tok_in, (size_t)B * 4);
   A(&m->tok_out, (size_t)B * 4);
   A(&m->pos, (size_t)B * 4);
-  A(&m->err_flag, 4);
+  A(&m->own_err, 4);
+  m->err_flag = ctx ? spock::ctx_err_word(ctx) : m->own_err;
   const int ndn = n_dn(m), nat = n_attn(m);
   A(&m->dn_state, (size_t)ndn * B * DNH * DND * DND * 4);
   A(&m->conv_state, (size_t)ndn * B * CONV * 4 * 2);
@@ -528,6 +534,20 @@ __attribute__((visibility("default"))) int spock_model_destroy(spock_model* m) {
   m->chunk_scratch.release();
   delete m;
   return SPOCK_OK;
+}
+
+__attribute__((visibility("default"))) int spock_model_sync(spock_model* m, void* stream) {
+  if (!m) return SPOCK_ERR_INVALID;
+  Guard g(m->device);
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return mfail(m, SPOCK_ERR_CUDA, std::string("spock_model_sync: ") + cudaGetErrorString(e));
+  int flag = 0;
+  e = cudaMemcpy(&flag, m->err_flag, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return mfail(m, SPOCK_ERR_CUDA, std::string("spock_model_sync: ") + cudaGetErrorString(e));
+  if (!flag) return SPOCK_OK;
+  cudaMemset(m->err_flag, 0, sizeof(int));
+  return mfail(m, SPOCK_ERR_TIMEOUT,
+               "spock_model_sync: a kernel's bounded wait gave up (code " + std::to_string(flag) + ")");
 }
 
 __attribute__((visibility("default"))) const char* spock_model_last_error(const spock_model* m) {
@@ -699,6 +719,10 @@ __attribute__((visibility("default"))) int spock_model_reset(spock_model* m, int
   cudaMemset(m->conv_state, 0, (size_t)n_dn(m) * B * CONV * 4 * 2);
   cudaMemset(m->pos, 0, (size_t)B * 4);
   cudaMemset(m->kv, 0, (size_t)B * m->kv_seq_stride * 2);
+  // the projection split-K workspace and tickets: clean after any completed
+  // launch, but a launch whose bounded wait gave up may leave them dirty
+  cudaMemset(m->ws, 0, m->ws_bytes);
+  cudaMemset(m->tickets, 0, m->tickets_bytes);
   cudaError_t e = cudaDeviceSynchronize();
   return e == cudaSuccess ? SPOCK_OK : mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));
 }

@@ -338,10 +338,12 @@ __global__ void __launch_bounds__(128, 1)
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int nt = 0; nt < kAP / 8; ++nt) {
-      sc[nt][0] = expf(sc[nt][0] - mn0);
-      sc[nt][1] = expf(sc[nt][1] - mn0);
-      sc[nt][2] = expf(sc[nt][2] - mn1);
-      sc[nt][3] = expf(sc[nt][3] - mn1);
+      // P is rounded to fp16 here, where the P.V mma will see it, so the
+      // denominators sum exactly the weights the numerators use
+      sc[nt][0] = __half2float(__float2half_rn(expf(sc[nt][0] - mn0)));
+      sc[nt][1] = __half2float(__float2half_rn(expf(sc[nt][1] - mn0)));
+      sc[nt][2] = __half2float(__float2half_rn(expf(sc[nt][2] - mn1)));
+      sc[nt][3] = __half2float(__float2half_rn(expf(sc[nt][3] - mn1)));
       s0 += sc[nt][0] + sc[nt][1];
       s1 += sc[nt][2] + sc[nt][3];
     }

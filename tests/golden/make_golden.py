@@ -25,7 +25,10 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("SPOCK_REFERENCE", "/root/reference")
+# the reference checkout: $SPOCK_REFERENCE, else a checkout named "reference"
+# beside this repository
+REF = os.environ.get("SPOCK_REFERENCE") or os.path.abspath(
+    os.path.join(os.path.dirname(__file__), "..", "..", "..", "reference"))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 import oracle  # noqa: E402
 from tests.golden.gen import probe_inputs  # noqa: E402

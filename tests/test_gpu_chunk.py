@@ -133,3 +133,25 @@ def test_more_pairs_than_sms_bf16(cuda_ok):
     ro, rs = batched_oracle(qb, kb, vb, g, b, init)
     go, gs = run_gpu(qb, kb, vb, g, b, init, dtype_in=torch.bfloat16, dtype_out=torch.float32)
     assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL, (max_rel(go, ro), max_rel(gs, rs))
+
+
+def test_config2_length_bf16_pipelined_kernel(cuda_ok):
+    """The benchmarked kernel (bf16 in, bf16 out, the pipelined path) at the
+    benchmarked length: seq_len 8192 = 128 chunks carried through the
+    TMEM-resident state, 2 sequences x 16 heads drawn with bench.py's own
+    generator, plus a nonzero initial state."""
+    import bench
+    dev = torch.device("cuda", 0)
+    q, k, v, g, b = bench.make_chunk_inputs(2, 8192, 4321, dev)
+    init = torch.randn(2, 16, 128, 128, device=dev, generator=torch.Generator(device=dev).manual_seed(5)) * 0.05
+    out, st = spock_b200.chunk_prefill(q, k, v, g, b, initial_state=init, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    spock_b200.Context.get(0).sync()
+    f = lambda t: t.float().cpu().numpy()
+    ro, rs = batched_oracle(f(q), f(k), f(v), f(g), f(b), f(init))
+    e_out, e_st = max_rel(f(out), ro), max_rel(f(st), rs)
+    assert e_out <= 2 ** -8 and e_st <= TOL, (e_out, e_st)  # bf16 output rounding bounds out
+    # the fp32 output path of the same kernel, checked at the fp32 bar
+    out32, _ = spock_b200.chunk_prefill(q, k, v, g, b, initial_state=init, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert max_rel(f(out32), ro) <= TOL, max_rel(f(out32), ro)
