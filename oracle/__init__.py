@@ -54,6 +54,9 @@ def lib():
         _LIB.oracle_model_step.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int]
         _LIB.oracle_recurrent_raw.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float] + [
             _u16p, _u16p, _u16p, _f32p, _u16p]
+        _LIB.oracle_silu_gate.argtypes = [_i64, _u16p, _u16p, _u16p]
+        _LIB.oracle_residual_add.argtypes = [_i64, _u16p, _u16p, _u16p]
+        _LIB.oracle_gbeta.argtypes = [ctypes.c_int, _u16p, _u16p, _f32p, _f32p, _f32p]
     return _LIB
 
 
@@ -146,6 +149,37 @@ def recurrent_raw(q, k, v, state_with_tail, num_heads=16, k_dim=128, v_dim=128):
                                _ptr(q, _u16p), _ptr(k, _u16p), _ptr(v, _u16p), _ptr(st, _f32p),
                                _ptr(out, _u16p))
     return out, st
+
+
+def _u16(a):
+    return np.ascontiguousarray(a, dtype=np.uint16)
+
+
+def silu_gate(gate, up):
+    """silu_gate.comp: fp16 bits in, fp16 bits out."""
+    gate, up = _u16(gate), _u16(up)
+    out = np.zeros_like(gate)
+    lib().oracle_silu_gate(gate.size, _ptr(gate, _u16p), _ptr(up, _u16p), _ptr(out, _u16p))
+    return out
+
+
+def residual_add(a, b):
+    """residual_add.comp: fp16(a + b) on fp16 bits."""
+    a, b = _u16(a), _u16(b)
+    out = np.zeros_like(a)
+    lib().oracle_residual_add(a.size, _ptr(a, _u16p), _ptr(b, _u16p), _ptr(out, _u16p))
+    return out
+
+
+def gbeta(a, b, a_log_bias):
+    """Phase 1 of deltanet_recurrent_gbeta_norm_gate.comp: (g [H], beta [H]) fp32."""
+    a, b = _u16(a), _u16(b)
+    alb = _f32(a_log_bias)
+    H = a.size
+    g = np.zeros(H, np.float32)
+    beta = np.zeros(H, np.float32)
+    lib().oracle_gbeta(H, _ptr(a, _u16p), _ptr(b, _u16p), _ptr(alb, _f32p), _ptr(g, _f32p), _ptr(beta, _f32p))
+    return g, beta
 
 
 class Model:

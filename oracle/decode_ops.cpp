@@ -42,7 +42,7 @@ void conv_l2_one(int conv_dim, int ks, int key_total, int num_heads, uint16_t* q
   for (int ch = 0; ch < conv_dim; ++ch) {
     float sum = 0.f;
     for (int i = 0; i < ks; ++i) sum += h2f(conv_state[ch * ks + i]) * h2f(conv_w[ch * ks + i]);
-    float silu = sum / (1.0f + std::exp(-sum));
+    float silu = sum / (1.0f + oracle::exp_d(-sum));
     qkv[ch] = f2h(silu);
   }
   // Phase 3: L2 of the Q and K 128-blocks (:79-110)
@@ -70,16 +70,16 @@ void rec_norm_gate_one(int H, int kd, int vd, float q_scale, float eps, const ui
     float* S = state + (size_t)h * kd * vd;
     const float a_val = h2f(a[h]), b_val = h2f(b[h]);
     const float a_log = a_log_bias[h * 2 + 0], dt_bias = a_log_bias[h * 2 + 1];
-    const float sp = std::log(1.0f + std::exp(a_val + dt_bias));
-    const float g = -std::exp(a_log) * sp;
-    const float beta = 1.0f / (1.0f + std::exp(-b_val));
+    const float sp = oracle::log_d(1.0f + oracle::exp_d(a_val + dt_bias));
+    const float g = -oracle::exp_d(a_log) * sp;
+    const float beta = 1.0f / (1.0f + oracle::exp_d(-b_val));
     std::vector<float> sq(kd), sk(kd), sv(vd), kv(vd), delta(vd), o(vd);
     for (int i = 0; i < kd; ++i) {
       sq[i] = h2f(q[h * kd + i]) * q_scale;
       sk[i] = h2f(k[h * kd + i]);
     }
     for (int j = 0; j < vd; ++j) sv[j] = h2f(v[h * vd + j]);
-    const float eg = std::exp(g);
+    const float eg = oracle::exp_d(g);
     for (int e = 0; e < kd * vd; ++e) S[e] *= eg;
     for (int j = 0; j < vd; ++j) {
       float s = 0.f;
@@ -100,7 +100,7 @@ void rec_norm_gate_one(int H, int kd, int vd, float q_scale, float eps, const ui
     for (int j = 0; j < vd; ++j) {
       const float normed = o[j] * nf;
       const float zz = h2f(z[h * vd + j]);
-      const float silu = zz / (1.0f + std::exp(-zz));
+      const float silu = zz / (1.0f + oracle::exp_d(-zz));
       const float weighted = h2f(f2h(norm_w[j] * normed));
       out[h * vd + j] = f2h(weighted * silu);
     }
@@ -168,7 +168,7 @@ extern "C" int oracle_recurrent_raw(int num_heads, int k_dim, int v_dim, float q
       sk[i] = h2f(k[h * k_dim + i]);
     }
     for (int j = 0; j < v_dim; ++j) sv[j] = h2f(v[h * v_dim + j]);
-    const float eg = std::exp(g);
+    const float eg = oracle::exp_d(g);
     for (int e = 0; e < k_dim * v_dim; ++e) S[e] *= eg;
     for (int j = 0; j < v_dim; ++j) {
       float s = 0.f;
@@ -184,6 +184,30 @@ extern "C" int oracle_recurrent_raw(int num_heads, int k_dim, int v_dim, float q
     }
   }
   return 0;
+}
+
+// silu_gate.comp:main: out = fp16(silu(g) * u), silu(g) = g / (1 + exp(-g)).
+extern "C" void oracle_silu_gate(int64_t n, const uint16_t* gate, const uint16_t* up, uint16_t* out) {
+  for (int64_t i = 0; i < n; ++i) {
+    const float g = h2f(gate[i]);
+    out[i] = f2h((g / (1.0f + oracle::exp_d(-g))) * h2f(up[i]));
+  }
+}
+
+// residual_add.comp: out = fp16(a + b) (out may alias a).
+extern "C" void oracle_residual_add(int64_t n, const uint16_t* a, const uint16_t* b, uint16_t* out) {
+  for (int64_t i = 0; i < n; ++i) out[i] = f2h(h2f(a[i]) + h2f(b[i]));
+}
+
+// deltanet_recurrent_gbeta_norm_gate.comp:101-115 (phase 1), per head:
+// g = -exp(A_log) * log(1 + exp(a + dt_bias)), beta = 1 / (1 + exp(-b)).
+extern "C" void oracle_gbeta(int H, const uint16_t* a, const uint16_t* b, const float* a_log_bias, float* g,
+                             float* beta) {
+  for (int h = 0; h < H; ++h) {
+    const float sp = oracle::log_d(1.0f + oracle::exp_d(h2f(a[h]) + a_log_bias[2 * h + 1]));
+    g[h] = -oracle::exp_d(a_log_bias[2 * h]) * sp;
+    beta[h] = 1.0f / (1.0f + oracle::exp_d(-h2f(b[h])));
+  }
 }
 
 extern "C" void oracle_f32_to_f16(const float* x, uint16_t* y, int64_t n) {

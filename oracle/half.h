@@ -3,6 +3,7 @@
 // Round-to-nearest-even, matching GLSL float16_t() and CUDA __float2half_rn.
 #pragma once
 #include <cstdint>
+#include <cmath>
 #include <cstring>
 
 namespace oracle {
@@ -59,4 +60,14 @@ inline uint16_t f2bf(float f) {
 
 inline float round_h(float f) { return h2f(f2h(f)); }
 
+}  // namespace oracle
+
+namespace oracle {
+// The shaders' exp()/log() have implementation-defined precision (GLSL allows
+// several ulps), so the decode-path restatement fixes them to one definition
+// a GPU can reproduce exactly: evaluate in double precision and round once to
+// float. (The chunk rule keeps std::exp on float: it restates the reference's
+// own C++ code, src/runtime/deltanet_chunk.cpp, bit for bit.)
+inline float exp_d(float x) { return (float)std::exp((double)x); }
+inline float log_d(float x) { return (float)std::log((double)x); }
 }  // namespace oracle

@@ -224,7 +224,7 @@ extern "C" int oracle_model_step(oracle_model* m, const int* tokens, int* out_to
           float sum = 0.f;
           std::vector<float> acc(HD, 0.f);
           for (int p = 0; p < L; ++p) {
-            const float w = std::exp(sc[p] - mx);
+            const float w = oracle::exp_d(sc[p] - mx);
             sum += w;
             const uint16_t* vr = cache + (size_t)p * 2 * KVH * HD + KVH * HD + kvh * HD;
             for (int d = 0; d < HD; ++d) acc[d] += w * h2f(vr[d]);
@@ -234,22 +234,19 @@ extern "C" int oracle_model_step(oracle_model* m, const int* tokens, int* out_to
         }
         for (int i = 0; i < QH * HD; ++i) {
           const float g = h2f(gate[i]);
-          gated[i] = f2h(h2f(att[i]) * (1.0f / (1.0f + std::exp(-g))));
+          gated[i] = f2h(h2f(att[i]) * (1.0f / (1.0f + oracle::exp_d(-g))));
         }
         matvec(m->W(P + "attn_o"), gated.data(), HID, QH * HD, y.data(), threads);
         ++ai;
       }
-      for (int i = 0; i < HID; ++i) h[i] = f2h(h2f(h[i]) + h2f(y[i]));
+      oracle_residual_add(HID, h.data(), y.data(), h.data());
       rmsnorm(h.data(), m->W(P + "post_norm"), eps, x.data());
       std::vector<uint16_t> g(INTER), u(INTER), mm(INTER);
       matvec(m->W(P + "mlp_gate"), x.data(), INTER, HID, g.data(), threads);
       matvec(m->W(P + "mlp_up"), x.data(), INTER, HID, u.data(), threads);
-      for (int i = 0; i < INTER; ++i) {
-        const float gv = h2f(g[i]);
-        mm[i] = f2h((gv / (1.0f + std::exp(-gv))) * h2f(u[i]));
-      }
+      oracle_silu_gate(INTER, g.data(), u.data(), mm.data());
       matvec(m->W(P + "mlp_down"), mm.data(), HID, INTER, y.data(), threads);
-      for (int i = 0; i < HID; ++i) h[i] = f2h(h2f(h[i]) + h2f(y[i]));
+      oracle_residual_add(HID, h.data(), y.data(), h.data());
     }
     rmsnorm(h.data(), m->W("final_norm"), eps, x.data());
     if (hidden_out) std::memcpy(hidden_out + b * HID, x.data(), HID * 2);

@@ -15,7 +15,9 @@ that has the reference at REF; the GPU box never runs this).
   decode_layer0/      the reference's captured layer-0 decode fixtures for the
                       recurrent probe (CMakeLists.txt:144), copied verbatim:
                       q,k,v fp16 [2048], state_pre f32 [16*128*128 + 32]
-                      (g and beta in the tail), expected raw output fp16 [2048].
+                      (g and beta in the tail), expected raw output fp16 [2048];
+                      and the weight-free glue fixtures of the same step
+                      (mlp gate/up -> product, residual adds, b -> beta).
 """
 import importlib.util
 import os
@@ -69,7 +71,12 @@ def decode_case():
     dst = os.path.join(HERE, "decode_layer0")
     os.makedirs(dst, exist_ok=True)
     for name in ["dn_q_2048.fp16", "dn_k_2048.fp16", "dn_v_2048.fp16", "dn_g_beta_32.u32",
-                 "dn_recurrent_state_pre_262176.f32", "dn_core_2048.fp16"]:
+                 "dn_recurrent_state_pre_262176.f32", "dn_core_2048.fp16",
+                 # weight-free glue fixtures: silu_gate.comp, residual_add.comp, and
+                 # the beta = sigmoid(b) half of the g/beta computation
+                 "mlp_gate_3584.fp16", "mlp_up_3584.fp16", "mlp_product_3584.fp16",
+                 "input_hidden_1024.fp16", "mixer_output_1024.fp16", "mixer_residual_1024.fp16",
+                 "down_output_1024.fp16", "post_mlp_1024.fp16", "dn_b_16.fp16"]:
         shutil.copyfile(os.path.join(REF, "tests", "data", "layer0_step1_" + name), os.path.join(dst, name))
 
 

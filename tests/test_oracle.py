@@ -75,3 +75,34 @@ def test_oracle_threads_do_not_change_results():
     r1 = oracle.chunk_rule(q, k, v, g, b, threads=1)
     r8 = oracle.chunk_rule(q, k, v, g, b, threads=8)
     assert all(np.array_equal(x, y) for x, y in zip(r1, r8))
+
+
+def _fixture(name, dtype=np.uint16):
+    return np.fromfile(os.path.join(GOLD, "decode_layer0", name), dtype)
+
+
+def test_silu_gate_golden():
+    """silu_gate.comp pinned on the reference's captured layer-0 MLP tensors."""
+    out = oracle.silu_gate(_fixture("mlp_gate_3584.fp16"), _fixture("mlp_up_3584.fp16"))
+    assert np.array_equal(out, _fixture("mlp_product_3584.fp16"))
+
+
+def test_residual_adds_golden():
+    """residual_add.comp pinned twice: h + mixer -> mixer_residual, then + down -> post_mlp."""
+    mixed = oracle.residual_add(_fixture("input_hidden_1024.fp16"), _fixture("mixer_output_1024.fp16"))
+    assert np.array_equal(mixed, _fixture("mixer_residual_1024.fp16"))
+    post = oracle.residual_add(mixed, _fixture("down_output_1024.fp16"))
+    assert np.array_equal(post, _fixture("post_mlp_1024.fp16"))
+
+
+def test_beta_golden():
+    """beta = sigmoid(b) of the g/beta phase, pinned on the captured b and the
+    beta half of the captured g/beta tail (g also needs A_log / dt_bias weights,
+    which are not among the fixtures). GLSL leaves exp()'s precision to the
+    implementation and the oracle evaluates it in double, so the bar is one
+    fp32 ulp; 14 of the 16 values are bit-identical."""
+    gb = _fixture("dn_g_beta_32.u32", np.uint32).view(np.float32)
+    b = _fixture("dn_b_16.fp16")
+    _, beta = oracle.gbeta(np.zeros(16, np.uint16), b, np.zeros((16, 2), np.float32))
+    ulps = np.abs(beta.view(np.int32).astype(np.int64) - gb[16:].view(np.int32).astype(np.int64))
+    assert ulps.max() <= 1 and (ulps == 0).sum() >= 14, ulps
