@@ -1,22 +1,30 @@
 """Benchmark of the B200 Gated DeltaNet hot path (one JSON line on rank 0).
 
 Default workload: long batched chunk prefill, 64
-independent sequences x 16 heads x 8192 tokens per GPU, chunk 64, k=v=128,
-bf16 q/k/v, fp32 g/beta/state/accumulation, bf16 core_attn_out. Synthetic
-seeded inputs with config 0's distributions. A step is one chunk-prefill call
-over the whole batch. Under torchrun each rank runs its own 64 sequences
-(independent (sequence, head) pairs, no collective): weak scaling.
+independent sequences x 16 heads x 8192 tokens, chunk 64, k=v=128, bf16
+q/k/v, fp32 g/beta/state/accumulation, bf16 core_attn_out. Synthetic seeded
+inputs with config 0's distributions (each sequence from its own seed). A step
+is one chunk-prefill call over this rank's sequences. Under torchrun the 64
+sequences are split contiguously over the ranks (64/N each; independent
+(sequence, head) pairs, no collective on the data path): strong scaling.
+After timing, an untimed NCCL gather brings every rank's outputs to rank 0,
+which recomputes the whole batch and checks them bit for bit (gather_check).
 
   value    Mtok/s over all ranks, inputs resident in HBM (token = one position
            of one sequence across all 16 heads), device-timed with CUDA events,
            max over ranks
   e2e      the same metric through the public API with pinned host buffers:
-           H2D of q/k/v/g/beta and D2H of core_attn_out + final_state timed
+           H2D of q/k/v/g/beta and D2H of core_attn_out + final_state timed,
+           in sub-batches on three streams so copies overlap the kernel
   roofline dominant kernel (chunk_pipe_kernel) against MEASURED_PEAKS.json
   cpu_baseline the reference's own run_deltanet_chunk_rule (oracle/_ref) or
            the oracle port, on a bounded sample, all host threads
 
---config 1 runs the fused decode step instead (batch 64).
+--config 0: the chunk rule alone at H16 S104 fp32, latency per call, with the
+            reference's chunk rule on one core beside it.
+--config 1: the fused decode step (batch 64), CPU restatement beside it.
+--config 3/4: full-model prefill / greedy decode (config 4: 256 sequences split
+            over the ranks); --exact times the exact-order path.
 --impl reference times the reference CPU implementation on the same metric.
 """
 import argparse
@@ -165,12 +173,32 @@ def cpu_reference_sample(threads, S=1024, seqs=None):
     return seqs * S / dt / 1e6, kind, f"{seqs} sequences x {H} heads x {S} tokens, fp32, {threads} threads, {dt:.1f} s"
 
 
+def shard(total, ws, rank):
+    """Contiguous split of `total` independent sequences over ws ranks:
+    (first sequence, count) of this rank. Every sequence is owned once."""
+    base, extra = divmod(total, ws)
+    first = rank * base + min(rank, extra)
+    return first, base + (1 if rank < extra else 0)
+
+
+def shard_inputs(first, count, S, dev):
+    """Inputs of sequences [first, first+count): each sequence is drawn from
+    its own seed, so a shard is the same whichever rank computes it."""
+    import torch
+    parts = [make_chunk_inputs(1, S, 1234 + i, dev) for i in range(first, first + count)]
+    return tuple(torch.cat([p[j] for p in parts]) for j in range(5))
+
+
 def bench_chunk(args, ws, rank, local):
     import torch
     import spock_b200
     dev = torch.device("cuda", local)
-    B, S = args.batch, args.seq
-    q, k, v, g, b = make_chunk_inputs(B, S, 1234 + rank, dev)
+    S = args.seq
+    if args.scaling == "strong":  # BASELINE config 2: 64 sequences sharded over the ranks
+        first, B = shard(args.batch, ws, rank)
+    else:
+        first, B = rank * args.batch, args.batch
+    q, k, v, g, b = shard_inputs(first, B, S, dev)
     out = torch.empty(B, H, S, V, dtype=torch.bfloat16, device=dev)
     st = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
     ctx = spock_b200.Context.get(local)
@@ -202,10 +230,20 @@ def bench_chunk(args, ws, rank, local):
     kern_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
     kern_ms = max_over_ranks(kern_ms, ws)
     ms_step = total_ms / args.steps
-    tokens_step = B * S * ws
+    tokens_step = (args.batch if args.scaling == "strong" else B * ws) * S
     value = tokens_step / (ms_step / 1e3) / 1e6
 
-    # end to end through the public API with pinned host buffers
+    # untimed: gather every rank's outputs to rank 0 over NCCL and check them
+    # bit for bit against rank 0 recomputing the whole batch (the kernel is
+    # deterministic, so a correct shard/gather reproduces it exactly)
+    gather_ok = None
+    if ws > 1 and args.gather and args.scaling == "strong":
+        gather_ok = gather_check(args, ws, rank, dev, out, st, ctx)
+
+    # end to end through the public API with pinned host buffers: the batch
+    # goes through in sub-batches on three streams, so the H2D copy of one
+    # sub-batch, the kernel of the previous one and the D2H copy of the one
+    # before overlap (separate copy engines per direction)
     hq = [x.cpu().pin_memory() for x in (q, k, v, g, b)]
     hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     hst = torch.empty(st.shape, dtype=st.dtype).pin_memory()
@@ -213,13 +251,34 @@ def bench_chunk(args, ws, rank, local):
     h2d = sum(x.numel() * x.element_size() for x in hq)
     d2h = hout.numel() * hout.element_size() + hst.numel() * hst.element_size()
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    sub = max(1, min(B, args.e2e_sub))
+    cuts = [B * i // sub for i in range(sub + 1)]
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
 
     def e2e_step():
-        for d_, h_ in zip(dq, hq):
-            d_.copy_(h_, non_blocking=True)
-        spock_b200.chunk_prefill(*dq, out_dtype=torch.bfloat16, out=out, final_state=st, ctx=ctx, stream=stream)
-        hout.copy_(out, non_blocking=True)
-        hst.copy_(st, non_blocking=True)
+        ev_prev = torch.cuda.Event()
+        ev_prev.record(stream)
+        s_in.wait_event(ev_prev)  # the previous step's kernels are done with the inputs
+        for c0, c1 in zip(cuts[:-1], cuts[1:]):
+            if c0 == c1:
+                continue
+            with torch.cuda.stream(s_in):
+                for d_, h_ in zip(dq, hq):
+                    d_[c0:c1].copy_(h_[c0:c1], non_blocking=True)
+                e_in = torch.cuda.Event()
+                e_in.record(s_in)
+            stream.wait_event(e_in)
+            spock_b200.chunk_prefill(*(d_[c0:c1] for d_ in dq), out_dtype=torch.bfloat16, out=out[c0:c1],
+                                     final_state=st[c0:c1], ctx=ctx, stream=stream)
+            e_c = torch.cuda.Event()
+            e_c.record(stream)
+            s_out.wait_event(e_c)
+            with torch.cuda.stream(s_out):
+                hout[c0:c1].copy_(out[c0:c1], non_blocking=True)
+                hst[c0:c1].copy_(st[c0:c1], non_blocking=True)
+        e_done = torch.cuda.Event()
+        e_done.record(s_out)
+        stream.wait_event(e_done)
     e2e_step()
     torch.cuda.synchronize()
     barrier(ws)
@@ -241,14 +300,17 @@ def bench_chunk(args, ws, rank, local):
     res = {
         "metric": "chunk-prefill Mtok/s (token = one sequence position across all 16 heads)",
         "value": round(value, 3), "unit": "Mtok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "bf16 in/out, fp16 tensor-core operands, fp32 state+accumulation", "data": "synthetic (seeded, config-0 distributions)",
-        "config": {"workload": "config 2: batched chunk prefill", "sequences_per_gpu": B, "heads": H,
-                   "seq_len": S, "chunk": C, "k_dim": K, "v_dim": V, "parallelism": f"dp{ws} over sequences",
+        "config": {"workload": "config 2: batched chunk prefill", "sequences": args.batch if args.scaling == "strong" else B * ws,
+                   "sequences_per_gpu": B, "heads": H,
+                   "seq_len": S, "chunk": C, "k_dim": K, "v_dim": V,
+                   "parallelism": f"dp{ws} over sequences ({args.scaling} scaling)",
                    "l2": "inputs (%.1f GB/GPU) larger than L2" % (alg_bytes / 1e9)},
         "per_gpu_Mtok_s": round(value / ws, 3),
+        **({"gather_check": gather_ok} if gather_ok is not None else {}),
         "e2e": {"value": round(e2e_val, 4), "unit": "Mtok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms, 3)},
+                "ms_per_step": round(e2e_ms, 3), "sub_batches": sub},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm" if t_hbm >= t_tc else "tensor", "achieved": round(achieved_gbs, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(achieved_gbs / hbm, 4),
@@ -262,6 +324,42 @@ def bench_chunk(args, ws, rank, local):
         "clocks": clk.summary(),
     }
     return res
+
+
+def gather_check(args, ws, rank, dev, out, st, ctx):
+    """NCCL gather of every rank's core_attn_out and final state to rank 0, then
+    rank 0 recomputes each shard and compares bit for bit. Returns the verdict
+    on every rank (broadcast)."""
+    import torch
+    import torch.distributed as dist
+    import spock_b200
+    shapes = [shard(args.batch, ws, r) for r in range(ws)]
+    ok = True
+    if rank == 0:
+        bufs_o = [torch.empty((n,) + tuple(out.shape[1:]), dtype=out.dtype, device=dev) for _, n in shapes]
+        bufs_s = [torch.empty((n,) + tuple(st.shape[1:]), dtype=st.dtype, device=dev) for _, n in shapes]
+    else:
+        bufs_o = bufs_s = None
+    # gather of unequal shards: one point-to-point pair per rank (NCCL over NVLink)
+    for r in range(1, ws):
+        if rank == r:
+            dist.send(out, 0)
+            dist.send(st, 0)
+        elif rank == 0:
+            dist.recv(bufs_o[r], r)
+            dist.recv(bufs_s[r], r)
+    if rank == 0:
+        bufs_o[0].copy_(out)
+        bufs_s[0].copy_(st)
+        for (first, n), go, gs in zip(shapes, bufs_o, bufs_s):
+            q, k, v, g, b = shard_inputs(first, n, args.seq, dev)
+            ro, rs = spock_b200.chunk_prefill(q, k, v, g, b, out_dtype=torch.bfloat16, ctx=ctx)
+            torch.cuda.synchronize()
+            ok = ok and torch.equal(ro, go) and torch.equal(rs, gs)
+            del q, k, v, g, b, ro, rs
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.broadcast(flag, 0)
+    return bool(flag.item())
 
 
 # ---------------------------------------------------------------- config 1 ---
@@ -386,10 +484,16 @@ def bench_model(args, ws, rank, local):
     import torch
     import spock_b200
     dev = torch.device("cuda", local)
-    B, P, layers, vocab = args.batch, args.prompt, 24, 248320
+    P, layers, vocab = args.prompt, 24, 248320
+    B = shard(args.batch, ws, rank)[1] if args.scaling == "strong" else args.batch
+    total_seqs = args.batch if args.scaling == "strong" else B * ws
     w = model_weights_gpu(layers, vocab, 7, dev)
-    m = spock_b200.Model(layers, vocab, max_batch=B, max_seq=P + args.steps + args.warmup + 48, device=local)
+    m = spock_b200.Model(layers, vocab, max_batch=B, max_seq=P + args.steps + args.warmup + 48, device=local,
+                         exact=args.exact)
     m.set_weights(w)
+    cpu_base = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu_base = cpu_model_sample(w, layers, vocab)
     del w
     m.reset(B)
     stream = torch.cuda.Stream(device=dev)
@@ -442,7 +546,7 @@ def bench_model(args, ws, rank, local):
     else:
         launches = per_step * steps  # graph replays: kernels per step x timed steps
         ms = max_over_ranks(t0.elapsed_time(t1), ws) / steps
-    value = B * ws / (ms / 1e3)
+    value = total_seqs / (ms / 1e3)
     hbm, tf, pk = peaks()
     w_bytes = 752.4e6 * 2
     state_bytes = B * 18 * (16 * 128 * 128 * 4 * 2 + 6144 * 4 * 2 * 2)
@@ -473,16 +577,18 @@ def bench_model(args, ws, rank, local):
         a1.record(stream)
         stream.synchronize()
     e2e_ms = max_over_ranks(a0.elapsed_time(a1), ws)
-    e2e_val = B * ws * (hp.shape[1] + n_e2e - 1) / (e2e_ms / 1e3)
+    e2e_val = total_seqs * (hp.shape[1] + n_e2e - 1) / (e2e_ms / 1e3)
     m.close()
     name = "full-model greedy decode tok/s" if args.config == 4 else "full-model layer-major prefill tok/s"
-    return {
+    res = {
         "metric": name, "value": round(value, 1), "unit": "tok/s", "n_gpus": ws, "steps": steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "fp16 weights/activations, fp32 accumulation and DeltaNet state",
         "data": "synthetic (random-init Qwen3.5-0.8B layout, seeded random prompt)",
-        "config": {"workload": f"config {args.config}", "sequences_per_gpu": B, "prompt": P, "layers": layers,
-                   "vocab": vocab, "parallelism": f"dp{ws} over sequences",
+        "config": {"workload": f"config {args.config}", "sequences": total_seqs, "sequences_per_gpu": B, "prompt": P,
+                   "layers": layers, "path": "exact order (bit-identical tokens)" if args.exact else
+                   "tensor-core projections + chunk-rule prefill",
+                   "vocab": vocab, "parallelism": f"dp{ws} over sequences ({args.scaling} scaling)",
                    "l2": "weights (1.5 GB) larger than L2",
                    **({"prefills_timed": n_pf, "step": "one prompt token (ms_per_step = prefill ms / prompt)"}
                       if args.config == 3 else {})},
@@ -490,6 +596,136 @@ def bench_model(args, ws, rank, local):
                 "d2h_bytes_per_step": int(B * 4), "note": f"{hp.shape[1]}-token prompt + {n_e2e} new tokens via spock_model_generate"},
         "gpu_launches": int(launches),
         "roofline": roof,
+        "clocks": clk.summary(),
+    }
+    if cpu_base:
+        res["cpu_baseline"] = cpu_base
+    return res
+
+
+def cpu_model_sample(w, layers, vocab):
+    """The CPU restatement of the decode path (oracle/model.cpp, the reference
+    has no CPU decode of its own) on a bounded sample: greedy decode steps of
+    one sequence, all host threads and one. tok/s; one step = one token."""
+    import numpy as np
+    import oracle
+    threads = os.cpu_count() or 1
+    cpu = oracle.Model(w, layers, vocab, 16)
+    rates = {}
+    for th, n in ((threads, 6), (1, 2)):
+        cpu.reset(1)
+        cpu.step(np.array([1], np.int32), threads=th)
+        t0 = time.perf_counter()
+        for i in range(n):
+            cpu.step(np.array([i + 2], np.int32), threads=th)
+        rates[th] = n / (time.perf_counter() - t0)
+    return {"value": round(rates[threads], 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "single_core_value": round(rates[1], 3),
+            "sample": f"greedy decode steps of 1 sequence ({layers} layers, vocab {vocab}): 6 steps on {threads} "
+                      "threads, 2 on 1 thread (token-serial: the restatement's prefill rate is the same per token)"}
+
+
+def cpu_decode_sample(B):
+    """Oracle restatement of the fused decode step (conv_l2_qk + recurrent
+    gbeta norm gate) at batch B: sequence-layer steps/s on all threads and one."""
+    import numpy as np
+    import oracle
+    from tests.golden.gen import decode_inputs
+    threads = os.cpu_count() or 1
+    d = decode_inputs(B, seed=0)
+    rates = {}
+    for th, reps in ((threads, 5), (1, 2)):
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            qkv, _ = oracle.conv_l2_qk(d["qkv"], d["conv_state"], d["conv_w"], threads=th)
+            oracle.rec_norm_gate(qkv, d["state"], d["a"], d["b"], d["a_log_bias"], d["z"], d["norm_w"], threads=th)
+        rates[th] = B * reps / (time.perf_counter() - t0)
+    return {"value": round(rates[threads], 1), "unit": "steps/s", "cores": threads, "kind": "port",
+            "single_core_value": round(rates[1], 1),
+            "sample": f"batch {B}, one layer: 5 steps on {threads} threads, 2 on 1 thread"}
+
+
+# ---------------------------------------------------------------- config 0 ---
+
+def bench_config0(args, ws, rank, local):
+    """the chunk rule alone, H16, S104 (padded to 128), C64,
+    fp32, one call. Latency per call with L2 flushed between calls; the
+    reference's own run_deltanet_chunk_rule on one core beside it."""
+    import numpy as np
+    import torch
+    import spock_b200
+    import oracle
+    from tests.golden.gen import chunk_inputs
+    dev = torch.device("cuda", local)
+    q, k, v, g, b = chunk_inputs(16, 104, seed=0, batch=1)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    dq, dk, dv, dg, db = map(T, (q, k, v, g, b))
+    out = torch.empty((1, 16, 104, 128), device=dev)
+    st = torch.empty((1, 16, 128, 128), device=dev)
+    ctx = spock_b200.Context.get(local)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
+    run = lambda: spock_b200.chunk_prefill(dq, dk, dv, dg, db, out_dtype=torch.float32, out=out, final_state=st,
+                                           ctx=ctx, stream=stream)
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    n0 = spock_b200.lib().spock_kernel_launch_count()
+    with ClockSampler(local) as clk:
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            run()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    launches = spock_b200.lib().spock_kernel_launch_count() - n0 - 0
+    ctx.sync()
+    us = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3
+    # e2e: host fp32 buffers in, outputs back, through the public API
+    hin = [torch.from_numpy(np.ascontiguousarray(a)).pin_memory() for a in (q, k, v, g, b)]
+    hout = torch.empty(out.shape).pin_memory()
+    hst = torch.empty(st.shape).pin_memory()
+    e2e = []
+    for _ in range(args.steps):
+        flush.zero_()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for d_, h_ in zip((dq, dk, dv, dg, db), hin):
+            d_.copy_(h_, non_blocking=True)
+        run()
+        hout.copy_(out, non_blocking=True)
+        hst.copy_(st, non_blocking=True)
+        a1.record(stream)
+        torch.cuda.synchronize()
+        e2e.append(a0.elapsed_time(a1) * 1e3)
+    h2d = sum(x.numel() * 4 for x in hin)
+    d2h = (hout.numel() + hst.numel()) * 4
+    # the reference's own chunk rule (oracle/_ref) on one core, same inputs
+    ref = oracle.ref_lib()
+    kind = "reference" if ref is not None else "port"
+    t0 = time.perf_counter()
+    reps = 5
+    for _ in range(reps):
+        oracle.chunk_rule(q[0], k[0], v[0], g[0], b[0], use_reference=ref is not None, threads=1)
+    cpu_us = (time.perf_counter() - t0) / reps * 1e6
+    hbm, tf, pk = peaks()
+    alg = 3 * 16 * 104 * 128 * 4 + 2 * 16 * 104 * 4 + 16 * 104 * 128 * 4 + 16 * 128 * 128 * 4
+    return {
+        "metric": "config-0 chunk rule latency per call (H16 S104 C64 fp32)", "value": round(us, 2), "unit": "us",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32 in/out, fp16 hi/lo tensor-core "
+        "operands, fp32 state+accumulation", "data": "synthetic (seeded, config-0 distributions)",
+        "config": {"workload": "config 0: chunk rule alone", "heads": 16, "seq_len": 104, "chunk": 64, "k_dim": 128,
+                   "v_dim": 128, "l2": "256 MB buffer written between timed calls"},
+        "e2e": {"value": round(statistics.mean(e2e), 2), "unit": "us", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(alg / (us / 1e6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(alg / (us / 1e6) / 1e9 / hbm, 4), "traffic": None, "peak_source": pk,
+                     "note": "latency-bound: 16 (head) CTAs, 2 serial chunks each"},
+        "cpu_baseline": {"value": round(cpu_us, 1), "unit": "us", "cores": 1, "kind": kind,
+                         "sample": "the whole config-0 call, 5 repetitions, 1 thread"},
         "clocks": clk.summary(),
     }
 
@@ -500,16 +736,25 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="spock_b200", choices=["spock_b200", "reference"])
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4])
+    ap.add_argument("--config", type=int, default=2, choices=[0, 1, 2, 3, 4])
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--layers", type=int, default=18)
     ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-sub", type=int, default=8, help="config 2 e2e: sub-batches overlapped on 3 streams")
+    ap.add_argument("--scaling", default=None, choices=["strong", "weak"],
+                    help="strong: --batch sequences in total, split over the ranks (config 2 and 4 default); "
+                         "weak: --batch sequences per rank")
+    ap.add_argument("--no-gather", dest="gather", action="store_false",
+                    help="config 2, N > 1: skip the untimed NCCL gather + check of the outputs")
+    ap.add_argument("--exact", action="store_true", help="configs 3/4: the exact-order model path")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.batch is None:
-        args.batch = {1: 64, 2: 64, 3: 1, 4: 1}[args.config]
+        args.batch = {0: 1, 1: 64, 2: 64, 3: 1, 4: 256}[args.config]
+    if args.scaling is None:
+        args.scaling = "strong" if args.config in (2, 4) else "weak"
     args.warmup = max(args.warmup, 3) if args.impl != "reference" else args.warmup
     ws, rank, local = dist_init(args)
 
@@ -536,8 +781,12 @@ def main():
 
     if args.config == 2:
         res = bench_chunk(args, ws, rank, local)
+    elif args.config == 0:
+        res = bench_config0(args, ws, rank, local)
     elif args.config == 1:
         res = bench_decode(args, ws, rank, local)
+        if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_decode_sample(args.batch)
     else:
         res = bench_model(args, ws, rank, local)
     if rank == 0:

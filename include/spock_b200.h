@@ -227,6 +227,16 @@ typedef struct {
   int32_t max_seq;    /* KV-cache capacity, MAX_SEQ (2048) in the reference */
   float rms_eps;      /* 1e-6 */
   float rope_theta;   /* 1e7 (vk_session.cpp:335) */
+  /* 0: tensor-core projections and the chunk rule in prefill (fp16-ULP parity
+   *    with the CPU restatement; prefill semantics of the reference's
+   *    layer_major_prefill + chunk-rule state).
+   * 1: exact order: every reduction in the reference shaders' own order on
+   *    CUDA cores (sequential matvec dots, two-pass attention softmax,
+   *    per-column DeltaNet recurrence), prompt tokens walked through the
+   *    recurrence one by one; hidden states and greedy tokens bit-identical
+   *    to the CPU restatement of the shaders. */
+  int32_t exact;
+  int32_t reserved;
 } spock_model_desc;
 
 /* ctx (nullable) supplies the error word of the model's bounded device waits:

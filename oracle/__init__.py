@@ -55,6 +55,7 @@ def lib():
         _LIB.oracle_recurrent_raw.argtypes = [ctypes.c_int] * 3 + [ctypes.c_float] + [
             _u16p, _u16p, _u16p, _f32p, _u16p]
         _LIB.oracle_silu_gate.argtypes = [_i64, _u16p, _u16p, _u16p]
+        _LIB.oracle_matvec.argtypes = [_u16p, _u16p, ctypes.c_int, ctypes.c_int, _u16p, ctypes.c_int]
         _LIB.oracle_residual_add.argtypes = [_i64, _u16p, _u16p, _u16p]
         _LIB.oracle_gbeta.argtypes = [ctypes.c_int, _u16p, _u16p, _f32p, _f32p, _f32p]
     return _LIB
@@ -153,6 +154,14 @@ def recurrent_raw(q, k, v, state_with_tail, num_heads=16, k_dim=128, v_dim=128):
 
 def _u16(a):
     return np.ascontiguousarray(a, dtype=np.uint16)
+
+
+def matvec(W, x, threads=8):
+    """matvec.comp: fp16 W [out][in] (bits) times fp16 x [in] -> fp16 [out], each dot sequential."""
+    W, x = _u16(W), _u16(x)
+    out = np.zeros(W.shape[0], np.uint16)
+    lib().oracle_matvec(_ptr(W, _u16p), _ptr(x, _u16p), W.shape[0], W.shape[1], _ptr(out, _u16p), threads)
+    return out
 
 
 def silu_gate(gate, up):

@@ -16,6 +16,9 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <immintrin.h>
+
+#include <algorithm>
 #include <map>
 #include <string>
 #include <thread>
@@ -53,14 +56,70 @@ void par(int n, int threads, F f) {
   for (auto& x : th) x.join();
 }
 
+// Each row's dot is sequential over j (matvec.comp:28-41); 8 rows advance
+// together only so the independent chains overlap in the CPU's pipeline.
+// fp16 -> fp32 of every bit pattern (exact; the same values h2f returns).
+const float* h2f_table() {
+  static const std::vector<float> t = [] {
+    std::vector<float> v(65536);
+    for (int i = 0; i < 65536; ++i) v[i] = h2f((uint16_t)i);
+    return v;
+  }();
+  return t.data();
+}
+
+// 8 rows x 8 columns of fp16 weights -> fp32, transposed (t[c] holds column c
+// of the 8 rows) with AVX2/F16C; the conversions are exact.
+__attribute__((target("avx2,f16c"))) inline void load8x8_t(const uint16_t* const* w, int j, __m256 t[8]) {
+  __m256 r[8];
+  for (int i = 0; i < 8; ++i) r[i] = _mm256_cvtph_ps(_mm_loadu_si128(reinterpret_cast<const __m128i*>(w[i] + j)));
+  const __m256 a0 = _mm256_unpacklo_ps(r[0], r[1]), a1 = _mm256_unpackhi_ps(r[0], r[1]);
+  const __m256 a2 = _mm256_unpacklo_ps(r[2], r[3]), a3 = _mm256_unpackhi_ps(r[2], r[3]);
+  const __m256 a4 = _mm256_unpacklo_ps(r[4], r[5]), a5 = _mm256_unpackhi_ps(r[4], r[5]);
+  const __m256 a6 = _mm256_unpacklo_ps(r[6], r[7]), a7 = _mm256_unpackhi_ps(r[6], r[7]);
+  const __m256 b0 = _mm256_shuffle_ps(a0, a2, 0x44), b1 = _mm256_shuffle_ps(a0, a2, 0xEE);
+  const __m256 b2 = _mm256_shuffle_ps(a1, a3, 0x44), b3 = _mm256_shuffle_ps(a1, a3, 0xEE);
+  const __m256 b4 = _mm256_shuffle_ps(a4, a6, 0x44), b5 = _mm256_shuffle_ps(a4, a6, 0xEE);
+  const __m256 b6 = _mm256_shuffle_ps(a5, a7, 0x44), b7 = _mm256_shuffle_ps(a5, a7, 0xEE);
+  t[0] = _mm256_permute2f128_ps(b0, b4, 0x20);
+  t[1] = _mm256_permute2f128_ps(b1, b5, 0x20);
+  t[2] = _mm256_permute2f128_ps(b2, b6, 0x20);
+  t[3] = _mm256_permute2f128_ps(b3, b7, 0x20);
+  t[4] = _mm256_permute2f128_ps(b0, b4, 0x31);
+  t[5] = _mm256_permute2f128_ps(b1, b5, 0x31);
+  t[6] = _mm256_permute2f128_ps(b2, b6, 0x31);
+  t[7] = _mm256_permute2f128_ps(b3, b7, 0x31);
+}
+
+// 8 rows' dots, each sequential over j with a separate multiply and add per
+// term (lane i of the vectors is row i).
+__attribute__((target("avx2,f16c"))) void dot8_rows(const uint16_t* const* w, const float* xf, int in, float* out8) {
+  __m256 s = _mm256_setzero_ps();
+  __m256 t[8];
+  for (int j = 0; j < in; j += 8) {
+    load8x8_t(w, j, t);
+    for (int c = 0; c < 8; ++c) s = _mm256_add_ps(s, _mm256_mul_ps(t[c], _mm256_set1_ps(xf[j + c])));
+  }
+  _mm256_storeu_ps(out8, s);
+}
+
 void matvec(const uint16_t* W, const uint16_t* x, int out, int in, uint16_t* y, int threads) {
+  const float* H = h2f_table();
   std::vector<float> xf(in);
   for (int j = 0; j < in; ++j) xf[j] = h2f(x[j]);
-  par(out, threads, [&](int r) {
-    const uint16_t* w = W + (size_t)r * in;
-    float s = 0.f;
-    for (int j = 0; j < in; ++j) s += h2f(w[j]) * xf[j];
-    y[r] = f2h(s);
+  constexpr int RB = 8;
+  par((out + RB - 1) / RB, threads, [&](int blk) {
+    const int r0 = blk * RB, nr = std::min(RB, out - r0);
+    float s[RB] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const uint16_t* w[RB];
+    for (int i = 0; i < RB; ++i) w[i] = W + (size_t)(r0 + (i < nr ? i : 0)) * in;
+    if (in % 8 == 0) {
+      dot8_rows(w, xf.data(), in, s);
+    } else {
+      for (int j = 0; j < in; ++j)
+        for (int i = 0; i < RB; ++i) s[i] += H[w[i][j]] * xf[j];
+    }
+    for (int i = 0; i < nr; ++i) y[r0 + i] = f2h(s[i]);
   });
 }
 
@@ -269,4 +328,9 @@ extern "C" int oracle_model_step(oracle_model* m, const int* tokens, int* out_to
     sq.pos += 1;
   }
   return 0;
+}
+
+// matvec.comp on its own (per-op parity tests): y[out] = fp16(W[out][in] . x).
+extern "C" void oracle_matvec(const uint16_t* W, const uint16_t* x, int out, int in, uint16_t* y, int threads) {
+  matvec(W, x, out, in, y, threads);
 }

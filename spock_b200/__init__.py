@@ -300,7 +300,8 @@ def run_deltanet_chunk_rule(config: DeltaNetChunkConfig, inputs: DeltaNetChunkIn
 
 class ModelDesc(ctypes.Structure):
     _fields_ = [("num_layers", ctypes.c_int32), ("vocab", ctypes.c_int32), ("max_batch", ctypes.c_int32),
-                ("max_seq", ctypes.c_int32), ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float)]
+                ("max_seq", ctypes.c_int32), ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+                ("exact", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 def _model_lib():
@@ -328,11 +329,12 @@ class Model:
     independent sequences. Weights are uploaded by the reference's role names."""
 
     def __init__(self, num_layers=24, vocab=248320, max_batch=1, max_seq=2048, eps=1e-6, theta=1e7,
-                 ctx=None, device=0):
+                 ctx=None, device=0, exact=False):
         self.L = _model_lib()
         self.ctx = ctx or Context.get(device)
         self.device = device
-        d = ModelDesc(num_layers, vocab, max_batch, max_seq, eps, theta)
+        self.exact = bool(exact)
+        d = ModelDesc(num_layers, vocab, max_batch, max_seq, eps, theta, int(bool(exact)), 0)
         h = ctypes.c_void_p()
         rc = self.L.spock_model_create(self.ctx.h, ctypes.byref(d), ctypes.byref(h))
         if rc != SPOCK_OK:

@@ -5,7 +5,10 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = ["capi.cu", "decode_step.cu", "chunk_prefill.cu", "chunk_pipeline.cu", "gemm.cu", "model_kernels.cu", "prefill.cu", "model.cu"]
+SOURCES = ["capi.cu", "decode_step.cu", "chunk_prefill.cu", "chunk_pipeline.cu", "gemm.cu", "model_kernels.cu", "prefill.cu",
+           "exact.cu", "model.cu"]
+# per-file flags: the exact-order kernels must not contract a*b+c into fma
+EXTRA = {"exact.cu": ["--fmad=false"]}
 LIB = os.path.join(HERE, "libspock_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -28,7 +31,8 @@ def build(force=False, verbose=False):
     objs = []
     for src in SOURCES:
         obj = os.path.join(CSRC, src.replace(".cu", ".o"))
-        cmd = [NVCC] + FLAGS + (["-Xptxas", "-v"] if verbose else []) + ["-c", os.path.join(CSRC, src), "-o", obj]
+        cmd = [NVCC] + FLAGS + EXTRA.get(src, []) + (["-Xptxas", "-v"] if verbose else []) + [
+            "-c", os.path.join(CSRC, src), "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if verbose or r.returncode:
             sys.stderr.write(r.stdout + r.stderr)

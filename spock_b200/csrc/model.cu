@@ -70,6 +70,16 @@ __global__ void copy_col_kernel(int* dst, int dst_stride, int dst_off, const int
 
 Status gemm_prepare();
 int* ctx_err_word(spock_ctx* ctx);
+Status launch_exact_proj(int epi, const void* x, int ldx, const void* w, int K, int N, int batch, void* y, int ldy,
+                         const void* res, float* amax_val, int* amax_idx, cudaStream_t st);
+Status launch_exact_attn(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride, int64_t kv_layer_off,
+                         const int* pos, int max_seq, float scale, void* out, int rows, int rows_per_seq,
+                         cudaStream_t st);
+Status launch_exact_dn_decode(void* proj, int ld, void* conv, const void* conv_w, const float* alb, const float* norm_w,
+                              float eps, float* state, void* out, int ldo, int batch, cudaStream_t st);
+Status launch_exact_dn_prefill(const void* proj, int ld, int batch, int T, const void* conv_w, const void* conv_old,
+                               void* conv_new, const float* alb, const float* norm_w, float eps, void* q, void* k,
+                               void* v, float* g, float* beta, float* state, void* out, cudaStream_t stream);
 Status launch_dn_prefill_conv(const void* proj, int ld, int batch, int T, int H, const void* conv_w,
                               const void* conv_old, void* conv_new, const float* a_log_bias, void* q, void* k, void* v,
                               float* g, float* beta, cudaStream_t st);
@@ -196,8 +206,56 @@ Status gemm(spock_model* m, int epi, const void* x, const void* w, int n_out, in
     if (_s.code) return _s;        \
   } while (0)
 
+// ---- exact order (spock_model_desc.exact) ----------------------------------
+// The same per-layer sequence as the reference's decode step, every kernel in
+// the shaders' reduction order (exact.cu); the RMSNorm and attention-prep
+// kernels already follow it.
+Status xproj(spock_model* m, int epi, const void* x, int ldx, const void* w, int K, int N, int rows, void* y,
+             int ldy, const void* res, cudaStream_t st) {
+  return spock::launch_exact_proj(epi, x, ldx, w, K, N, rows, y, ldy, res, m->amax_val, m->amax_idx, st);
+}
+
+Status record_step_exact(spock_model* m, cudaStream_t st) {
+#ifndef SPOCK_NO_PDL
+  spock::pdl_scope pdl_on;
+#endif
+  if (!st) spock::pdl_enabled() = false;
+  const int B = m->batch;
+  const float eps = m->d.rms_eps;
+  TRY(spock::launch_embed(m->tok_in, m->emb, m->h, B, st));
+  for (const auto& l : m->L) {
+    TRY(spock::launch_rmsnorm(m->h, l.input_norm, m->x, eps, B, st));
+    if (!l.attn) {
+      TRY(xproj(m, spock::EPI_F16, m->x, HID, l.w_in, HID, DN_IN, B, m->proj, DN_IN, nullptr, st));
+      TRY(spock::launch_exact_dn_decode(m->proj, DN_IN, (uint16_t*)m->conv_state + (size_t)l.dn_idx * B * CONV * 4,
+                                        l.conv_w, l.a_log_bias, l.dn_norm, eps,
+                                        m->dn_state + (size_t)l.dn_idx * B * DNH * DND * DND, m->mix, DNH * DND, B,
+                                        st));
+      TRY(xproj(m, spock::EPI_RESIDUAL, m->mix, DNH * DND, l.w_out, DNH * DND, HID, B, m->h, HID, m->h, st));
+    } else {
+      TRY(xproj(m, spock::EPI_F16, m->x, HID, l.w_in, HID, ATT_IN, B, m->proj, ATT_IN, nullptr, st));
+      const int64_t layer_off = (int64_t)l.attn_idx * m->d.max_seq * 2 * KVH * HD;
+      TRY(spock::launch_attn_prep(m->proj, ATT_IN, l.q_norm, l.k_norm, m->rope, m->pos, m->q, m->gate, m->kv,
+                                  m->kv_seq_stride, layer_off, eps, B, st));
+      TRY(spock::launch_exact_attn(m->q, m->gate, m->kv, m->kv_seq_stride, layer_off, m->pos, m->d.max_seq,
+                                   1.0f / 16.0f, m->mix, B, 1, st));
+      TRY(xproj(m, spock::EPI_RESIDUAL, m->mix, QH * HD, l.w_out, QH * HD, HID, B, m->h, HID, m->h, st));
+    }
+    TRY(spock::launch_rmsnorm(m->h, l.post_norm, m->x, eps, B, st));
+    TRY(xproj(m, spock::EPI_SWIGLU, m->x, HID, l.w_gu, HID, 2 * INTER, B, m->mlp, INTER, nullptr, st));
+    TRY(xproj(m, spock::EPI_RESIDUAL, m->mlp, INTER, l.w_down, INTER, HID, B, m->h, HID, m->h, st));
+  }
+  TRY(spock::launch_rmsnorm(m->h, m->final_norm, m->x, eps, B, st));
+  TRY(xproj(m, spock::EPI_ARGMAX, m->x, HID, m->emb, HID, m->d.vocab, B, nullptr, 0, nullptr, st));
+  TRY(spock::launch_argmax_finish(m->amax_val, m->amax_idx, (m->d.vocab + 127) / 128, B, m->tok_out, st));
+  spock::launch_k(spock::advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, m->pos, m->tok_out, m->tok_in, B);
+  SPOCK_LAUNCH_CHECK("advance_kernel");
+  return Status::ok();
+}
+
 // One decode token for every sequence: tok_in -> tok_out, h holds the final normed hidden in x.
 Status record_step(spock_model* m, cudaStream_t st) {
+  if (m->d.exact) return record_step_exact(m, st);
 #ifndef SPOCK_NO_PDL
   spock::pdl_scope pdl_on;  // every kernel of the step overlaps its predecessor's tail
 #endif
@@ -312,10 +370,53 @@ Status gemm_rows(spock_model* m, int epi, const void* x, const void* w, int n_ou
   return spock::launch_gemm(epi, x, w, a, m->sms, st);
 }
 
+// Exact-order layer-major prefill: every layer over all T prompt tokens
+// (rows r = b*T + t); each DeltaNet layer walks the prompt through the
+// recurrence token by token (token-serial decode semantics).
+Status record_prefill_exact(spock_model* m, const int32_t* prompt, int T, cudaStream_t st) {
+  spock::pdl_scope pdl_on;
+  if (!st) spock::pdl_enabled() = false;
+  const int B = m->batch, R = B * T;
+  const float eps = m->d.rms_eps;
+  auto& p = m->pf;
+  TRY(spock::launch_embed(prompt, m->emb, p.h, R, st));
+  for (const auto& l : m->L) {
+    TRY(spock::launch_rmsnorm(p.h, l.input_norm, p.x, eps, R, st));
+    if (!l.attn) {
+      TRY(xproj(m, spock::EPI_F16, p.x, HID, l.w_in, HID, DN_IN, R, p.proj, DN_IN, nullptr, st));
+      uint16_t* conv = (uint16_t*)m->conv_state + (size_t)l.dn_idx * B * CONV * 4;
+      float* state = m->dn_state + (size_t)l.dn_idx * B * DNH * DND * DND;
+      if (cudaMemcpyAsync(p.conv_old, conv, (size_t)B * CONV * 4 * 2, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return Status::err(SPOCK_ERR_CUDA, "model prefill: conv snapshot failed");
+      TRY(spock::launch_exact_dn_prefill(p.proj, DN_IN, B, T, l.conv_w, p.conv_old, conv, l.a_log_bias, l.dn_norm, eps,
+                                         p.q, p.k, p.v, p.g, p.beta, state, p.mix, st));
+      TRY(xproj(m, spock::EPI_RESIDUAL, p.mix, DNH * DND, l.w_out, DNH * DND, HID, R, p.h, HID, p.h, st));
+    } else {
+      TRY(xproj(m, spock::EPI_F16, p.x, HID, l.w_in, HID, ATT_IN, R, p.proj, ATT_IN, nullptr, st));
+      const int64_t layer_off = (int64_t)l.attn_idx * m->d.max_seq * 2 * KVH * HD;
+      TRY(spock::launch_attn_prep(p.proj, ATT_IN, l.q_norm, l.k_norm, m->rope, m->pos, p.aq, p.agate, m->kv,
+                                  m->kv_seq_stride, layer_off, eps, R, st, T));
+      TRY(spock::launch_exact_attn(p.aq, p.agate, m->kv, m->kv_seq_stride, layer_off, m->pos, m->d.max_seq,
+                                   1.0f / 16.0f, p.mix, R, T, st));
+      TRY(xproj(m, spock::EPI_RESIDUAL, p.mix, QH * HD, l.w_out, QH * HD, HID, R, p.h, HID, p.h, st));
+    }
+    TRY(spock::launch_rmsnorm(p.h, l.post_norm, p.x, eps, R, st));
+    TRY(xproj(m, spock::EPI_SWIGLU, p.x, HID, l.w_gu, HID, 2 * INTER, R, p.mlp, INTER, nullptr, st));
+    TRY(xproj(m, spock::EPI_RESIDUAL, p.mlp, INTER, l.w_down, INTER, HID, R, p.h, HID, p.h, st));
+  }
+  TRY(spock::launch_last_rows(p.h, p.last, B, T, HID, st));
+  TRY(spock::launch_rmsnorm(p.last, m->final_norm, m->x, eps, B, st));
+  TRY(xproj(m, spock::EPI_ARGMAX, m->x, HID, m->emb, HID, m->d.vocab, B, nullptr, 0, nullptr, st));
+  TRY(spock::launch_argmax_finish(m->amax_val, m->amax_idx, (m->d.vocab + 127) / 128, B, m->tok_out, st));
+  TRY(spock::launch_advance_pos(m->pos, B, T, st));
+  return Status::ok();
+}
+
 // Layer-major prefill: every layer over all T prompt tokens of every sequence
 // (rows r = b*T + t), then the final norm, LM head and argmax of each
 // sequence's last token. DeltaNet layers run the chunk rule over the prompt.
 Status record_prefill(spock_model* m, const int32_t* prompt, int T, cudaStream_t st) {
+  if (m->d.exact) return record_prefill_exact(m, prompt, T, st);
   spock::pdl_scope pdl_on;  // (the caller disables it on the legacy default stream)
   if (!st) spock::pdl_enabled() = false;
   const int B = m->batch, R = B * T;

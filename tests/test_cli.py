@@ -74,3 +74,19 @@ def test_decode_and_bench_cli_small_model(cuda_ok, tmp_path):
     r = run("spock-bench", "--mode", "correctness", "--layers", "4", "--vocab", "32000", "--runs", "2", "--warmup", "0")
     assert r.returncode == 0, r.stdout + r.stderr
     assert json.loads(r.stdout)["ok"] is True
+
+
+def test_bench_cli_config_usage_errors():
+    """--config outside 0..4 or more GPUs than present is a usage error (exit 2)."""
+    assert run("spock-bench", "--config", "7").returncode == 2
+    assert run("spock-bench", "--config", "2", "--gpus", "4096").returncode == 2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cfg", [0, 1, 2])
+def test_bench_cli_configs(cuda_ok, cfg):
+    """spock-bench --config N on one GPU prints one JSON line with a positive rate."""
+    r = run("spock-bench", "--config", str(cfg), "--gpus", "1", "--runs", "2", "--warmup", "1")
+    assert r.returncode == 0, r.stdout + r.stderr
+    d = json.loads(r.stdout)
+    assert d["config"] == cfg and d["gpus"] == 1 and d["rate"] > 0 and d["ms_per_step"] > 0

@@ -43,3 +43,29 @@ def test_max_over_ranks_gloo(tmp_path):
     r = _torchrun([str(script)], port=29518, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.count("ok") == 2
+
+
+def test_sequence_partition_gloo(tmp_path):
+    """bench.py's strong-scaling split: on 2 gloo ranks, every one of the 64
+    config-2 sequences (and config 4's 256, and a ragged 7) is owned by exactly
+    one rank, in contiguous blocks, and the union is all of them."""
+    script = tmp_path / "part.py"
+    script.write_text(
+        "import os, sys, torch, torch.distributed as dist\n"
+        f"sys.path.insert(0, {ROOT!r})\n"
+        "import bench\n"
+        "dist.init_process_group('gloo')\n"
+        "r, ws = dist.get_rank(), dist.get_world_size()\n"
+        "for total in (64, 256, 7):\n"
+        "    first, n = bench.shard(total, ws, r)\n"
+        "    mine = torch.zeros(total, dtype=torch.int64)\n"
+        "    mine[first:first + n] = 1\n"
+        "    dist.all_reduce(mine)\n"
+        "    assert torch.equal(mine, torch.ones(total, dtype=torch.int64)), (total, mine)\n"
+        "    lo = torch.tensor([first]); dist.all_reduce(lo, op=dist.ReduceOp.MIN)\n"
+        "    assert lo.item() == 0\n"
+        "print('ok', r)\n"
+        "dist.destroy_process_group()\n")
+    r = _torchrun([str(script)], port=29519, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.count("ok") == 2

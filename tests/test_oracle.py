@@ -106,3 +106,17 @@ def test_beta_golden():
     _, beta = oracle.gbeta(np.zeros(16, np.uint16), b, np.zeros((16, 2), np.float32))
     ulps = np.abs(beta.view(np.int32).astype(np.int64) - gb[16:].view(np.int32).astype(np.int64))
     assert ulps.max() <= 1 and (ulps == 0).sum() >= 14, ulps
+
+
+def test_matvec_is_sequential_per_row():
+    """The oracle's matvec (vectorised across rows for speed) equals a plain
+    sequential fp32 loop per row, as matvec.comp:28-41 computes it."""
+    rng = np.random.default_rng(3)
+    W = (rng.standard_normal((13, 1024)) * 0.02).astype(np.float16)
+    x = rng.standard_normal(1024).astype(np.float16)
+    got = oracle.matvec(W.view(np.uint16), x.view(np.uint16))
+    for r in range(13):
+        s = np.float32(0)
+        for j in range(1024):
+            s = np.float32(s + np.float32(np.float32(W[r, j]) * np.float32(x[j])))
+        assert got[r] == np.float16(s).view(np.uint16), r
