@@ -213,6 +213,58 @@ int spock_deltanet_recurrent(spock_ctx* ctx, int64_t batch, int32_t num_heads, i
                              void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Decode-glue operations, one reference shader dispatch each.               */
+/* ------------------------------------------------------------------------ */
+/* For callers that keep the reference's own per-layer orchestration
+ * (DecodeSession::decode, src/runtime/vk_session.cpp:2658-3370, dispatches
+ * these shaders one by one). They run the kernels of the model session.
+ * `exact` = 1 selects the exact-order kernels (each reduction in the shader's
+ * own order: results bit-identical to the shader restatement), 0 the fast
+ * ones. Device pointers, fp16 unless stated, rows contiguous. */
+
+/* rms_norm.comp:31-70: y[r] = fp16(x[r] * 1/sqrt(mean(x[r]^2) + eps) * (1 + w)),
+ * dim = 1024 (the hidden size; the only width the kernel implements). y may
+ * alias x. */
+int spock_rms_norm(spock_ctx* ctx, const void* x, const void* w, void* y, int64_t rows, int32_t dim, float eps,
+                   void* stream);
+
+typedef enum {
+  SPOCK_MV_STORE = 0,     /* y[r][n] = fp16(W[n] . x[r])                                      */
+  SPOCK_MV_RESIDUAL = 1,  /* y[r][n] = fp16(res[r][n] + fp16(W[n] . x[r])) (residual_add.comp) */
+  SPOCK_MV_SILU_GATE = 2, /* W: 2*out_dim rows, gate and up rows interleaved in groups of 16;
+                             y[r][p] = fp16(silu(fp16(gate_p . x[r])) * fp16(up_p . x[r]))
+                             (silu_gate.comp)                                                  */
+  SPOCK_MV_ARGMAX = 3     /* y: int32 [rows], the index of the largest fp16(W[n] . x[r]),
+                             lowest index among equal maxima (lm_head_tiled + argmax.comp)     */
+} spock_matvec_epilogue;
+
+/* matvec.comp:28-41 over `rows` activation rows with a fused epilogue.
+ * W [out_dim (x2 for SILU_GATE)][in_dim], x [rows][in_dim], y [rows][out_dim]
+ * (ARGMAX: int32 [rows]); residual [rows][out_dim] for RESIDUAL (y may alias it).
+ * Fast path (exact = 0): in_dim % 64 == 0, out_dim % 8 == 0, rows <= 256,
+ * ARGMAX at rows <= 8 needs in_dim <= 1024. Exact path: in_dim % 16 == 0.
+ * Scratch (padded x, split-K workspace, argmax partials) grows in the context. */
+int spock_matvec(spock_ctx* ctx, int32_t epilogue, int32_t exact, const void* w, int32_t out_dim, int32_t in_dim,
+                 const void* x, int64_t rows, void* y, const void* residual, void* stream);
+
+/* argmax.comp:27-62: idx[r] (int32) = the index of the largest fp16 logit of
+ * row r of logits [rows][n], lowest index among equal maxima. */
+int spock_argmax(spock_ctx* ctx, const void* logits, int64_t rows, int64_t n, int32_t* idx, void* stream);
+
+/* One decode token of gated full attention (Qwen3.5 layout: 8 q heads, 2 kv
+ * heads, head dim 256) for `rows` independent sequences: split_q_gate,
+ * rms_norm_per_head (q_norm, k_norm: fp16 [256], (1+w) form), rope_apply
+ * (rotary 64 of 256, theta), kv_cache_store, attention_decode.comp:64-143
+ * (scale 1/16) and sigmoid_gate.
+ *   proj     [rows][5120]: per q head [q 256 | gate 256] x 8, then k (2 x 256), v (2 x 256)
+ *   pos      int32 [rows]: this token's position in each sequence (< max_seq)
+ *   kv_cache [rows][max_seq][K|V][2][256], in/out (row pos is written)
+ *   out      [rows][2048] gated attention output */
+int spock_attention_decode(spock_ctx* ctx, int32_t exact, const void* proj, const void* q_norm, const void* k_norm,
+                           float eps, float rope_theta, const int32_t* pos, void* kv_cache, int32_t max_seq,
+                           int64_t rows, void* out, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Full-model decode (Qwen3.5-0.8B layout): the decode glue around the mixer. */
 /* ------------------------------------------------------------------------ */
 

@@ -56,6 +56,11 @@ def lib():
             _u16p, _u16p, _u16p, _f32p, _u16p]
         _LIB.oracle_silu_gate.argtypes = [_i64, _u16p, _u16p, _u16p]
         _LIB.oracle_matvec.argtypes = [_u16p, _u16p, ctypes.c_int, ctypes.c_int, _u16p, ctypes.c_int]
+        _LIB.oracle_rms_norm.argtypes = [_u16p, _u16p, ctypes.c_float, _u16p]
+        _LIB.oracle_argmax.argtypes = [_u16p, ctypes.c_int]
+        _LIB.oracle_argmax.restype = ctypes.c_int
+        _LIB.oracle_attention_decode.argtypes = [_u16p, _u16p, _u16p, ctypes.c_float, ctypes.c_float, _u16p,
+                                                 ctypes.c_int, _u16p]
         _LIB.oracle_residual_add.argtypes = [_i64, _u16p, _u16p, _u16p]
         _LIB.oracle_gbeta.argtypes = [ctypes.c_int, _u16p, _u16p, _f32p, _f32p, _f32p]
     return _LIB
@@ -162,6 +167,31 @@ def matvec(W, x, threads=8):
     out = np.zeros(W.shape[0], np.uint16)
     lib().oracle_matvec(_ptr(W, _u16p), _ptr(x, _u16p), W.shape[0], W.shape[1], _ptr(out, _u16p), threads)
     return out
+
+
+def rms_norm(x, w, eps=1e-6):
+    """rms_norm.comp on one 1024-wide fp16 row (bits)."""
+    x, w = _u16(x), _u16(w)
+    y = np.zeros(1024, np.uint16)
+    lib().oracle_rms_norm(_ptr(x, _u16p), _ptr(w, _u16p), eps, _ptr(y, _u16p))
+    return y
+
+
+def argmax(logits):
+    """argmax.comp on fp16 logits (bits): lowest index among equal maxima."""
+    logits = _u16(logits)
+    return int(lib().oracle_argmax(_ptr(logits, _u16p), logits.size))
+
+
+def attention_decode(proj, q_norm, k_norm, cache, pos, eps=1e-6, theta=1e7):
+    """One gated-attention token of one sequence: proj [5120], cache [max_seq, 2, 2, 256]
+    (a copy; row pos written) -> (gated [2048], updated cache). All fp16 bits."""
+    proj, qn, kn = _u16(proj), _u16(q_norm), _u16(k_norm)
+    cache = _u16(cache).copy()
+    out = np.zeros(2048, np.uint16)
+    lib().oracle_attention_decode(_ptr(proj, _u16p), _ptr(qn, _u16p), _ptr(kn, _u16p), eps, theta,
+                                  _ptr(cache, _u16p), int(pos), _ptr(out, _u16p))
+    return out, cache
 
 
 def silu_gate(gate, up):

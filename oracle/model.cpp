@@ -32,7 +32,7 @@ using oracle::h2f;
 
 namespace {
 constexpr int HID = 1024, INTER = 3584, DNH = 16, DND = 128, CONV = 6144;
-constexpr int QH = 8, KVH = 2, HD = 256, ROT = 64;
+constexpr int QH = 8, KVH = 2, HD = 256, ROT = 64, ATT_IN = QH * HD * 2 + 2 * KVH * HD;
 
 struct Seq {
   std::vector<float> dn_state;      // [n_dn][16][128][128]
@@ -162,6 +162,76 @@ void rope(uint16_t* x, int heads, const float* cs /*[64] of this position*/) {
     }
   }
 }
+// One token of gated full attention for one sequence, from the projected row
+// proj = [q0 | gate0 | ... | q7 | gate7 | k0 k1 | v0 v1] (5120 fp16): the
+// reference's split_q_gate, rms_norm_per_head (q, k), rope_apply (cs: this
+// position's 32 (cos, sin) pairs), kv_cache_store (cache: [max_seq][K|V][2][256]
+// of this layer, row `pos`), attention_decode.comp:64-143 over positions
+// 0..pos (scale 1/16) and sigmoid_gate -> gated [8*256].
+void attention_token(const uint16_t* proj, const uint16_t* qn_w, const uint16_t* kn_w, float eps, const float* cs,
+                     uint16_t* cache, int pos, uint16_t* gated) {
+  std::vector<uint16_t> q(QH * HD), gate(QH * HD), k(KVH * HD), att(QH * HD);
+  for (int hh = 0; hh < QH; ++hh)
+    for (int d = 0; d < HD; ++d) {
+      q[hh * HD + d] = proj[hh * 2 * HD + d];
+      gate[hh * HD + d] = proj[hh * 2 * HD + HD + d];
+    }
+  std::memcpy(k.data(), proj + QH * HD * 2, KVH * HD * 2);
+  const uint16_t* v = proj + QH * HD * 2 + KVH * HD;
+  for (int hh = 0; hh < QH; ++hh) rmsnorm_head(q.data() + hh * HD, qn_w, eps, q.data() + hh * HD);
+  for (int hh = 0; hh < KVH; ++hh) rmsnorm_head(k.data() + hh * HD, kn_w, eps, k.data() + hh * HD);
+  rope(q.data(), QH, cs);
+  rope(k.data(), KVH, cs);
+  std::memcpy(cache + (size_t)pos * 2 * KVH * HD, k.data(), KVH * HD * 2);
+  std::memcpy(cache + (size_t)pos * 2 * KVH * HD + KVH * HD, v, KVH * HD * 2);
+  const int L = pos + 1;
+  const float scale = 1.0f / 16.0f;
+  for (int hh = 0; hh < QH; ++hh) {
+    const int kvh = hh / (QH / KVH);
+    std::vector<float> sc(L);
+    float mx = -1e30f;
+    for (int p = 0; p < L; ++p) {
+      float dot = 0.f;
+      const uint16_t* kr = cache + (size_t)p * 2 * KVH * HD + kvh * HD;
+      for (int d = 0; d < HD; ++d) dot += h2f(q[hh * HD + d]) * h2f(kr[d]);
+      sc[p] = dot * scale;
+      mx = std::max(mx, sc[p]);
+    }
+    float sum = 0.f;
+    std::vector<float> acc(HD, 0.f);
+    for (int p = 0; p < L; ++p) {
+      const float w = oracle::exp_d(sc[p] - mx);
+      sum += w;
+      const uint16_t* vr = cache + (size_t)p * 2 * KVH * HD + KVH * HD + kvh * HD;
+      for (int d = 0; d < HD; ++d) acc[d] += w * h2f(vr[d]);
+    }
+    const float inv = 1.0f / (sum + 1e-30f);
+    for (int d = 0; d < HD; ++d) att[hh * HD + d] = f2h(acc[d] * inv);
+  }
+  for (int i = 0; i < QH * HD; ++i) {
+    const float g = h2f(gate[i]);
+    gated[i] = f2h(h2f(att[i]) * (1.0f / (1.0f + oracle::exp_d(-g))));
+  }
+}
+
+// argmax.comp:27-62 over fp16 logits: the strictly greater value wins, so the
+// lowest index wins among equal maxima.
+int argmax16(const uint16_t* logits, int n, float* margin) {
+  int best = 0;
+  float bv = -3.402823466e+38f, second = -3.402823466e+38f;
+  for (int i = 0; i < n; ++i) {
+    const float v = h2f(logits[i]);
+    if (v > bv) {
+      second = bv;
+      bv = v;
+      best = i;
+    } else if (v > second) {
+      second = v;
+    }
+  }
+  if (margin) *margin = bv - second;
+  return best;
+}
 }  // namespace
 
 struct oracle_model {
@@ -249,52 +319,13 @@ extern "C" int oracle_model_step(oracle_model* m, const int* tokens, int* out_to
         matvec(m->W(P + "delta_out_proj"), out.data(), HID, 2048, y.data(), threads);
         ++di;
       } else {  // gated full attention
-        std::vector<uint16_t> qg(QH * HD * 2), k(KVH * HD), v(KVH * HD), q(QH * HD), gate(QH * HD), att(QH * HD),
-            gated(QH * HD);
-        matvec(m->W(P + "attn_q"), x.data(), QH * HD * 2, HID, qg.data(), threads);
-        matvec(m->W(P + "attn_k"), x.data(), KVH * HD, HID, k.data(), threads);
-        matvec(m->W(P + "attn_v"), x.data(), KVH * HD, HID, v.data(), threads);
-        for (int hh = 0; hh < QH; ++hh)
-          for (int d = 0; d < HD; ++d) {
-            q[hh * HD + d] = qg[hh * 2 * HD + d];
-            gate[hh * HD + d] = qg[hh * 2 * HD + HD + d];
-          }
-        for (int hh = 0; hh < QH; ++hh) rmsnorm_head(q.data() + hh * HD, m->W(P + "attn_q_norm"), eps, q.data() + hh * HD);
-        for (int hh = 0; hh < KVH; ++hh) rmsnorm_head(k.data() + hh * HD, m->W(P + "attn_k_norm"), eps, k.data() + hh * HD);
-        const float* cs = m->rope.data() + (size_t)sq.pos * ROT;
-        rope(q.data(), QH, cs);
-        rope(k.data(), KVH, cs);
+        std::vector<uint16_t> proj(ATT_IN), gated(QH * HD);
+        matvec(m->W(P + "attn_q"), x.data(), QH * HD * 2, HID, proj.data(), threads);
+        matvec(m->W(P + "attn_k"), x.data(), KVH * HD, HID, proj.data() + QH * HD * 2, threads);
+        matvec(m->W(P + "attn_v"), x.data(), KVH * HD, HID, proj.data() + QH * HD * 2 + KVH * HD, threads);
         uint16_t* cache = sq.kv.data() + (size_t)ai * m->max_seq * 2 * KVH * HD;
-        std::memcpy(cache + (size_t)sq.pos * 2 * KVH * HD, k.data(), KVH * HD * 2);
-        std::memcpy(cache + (size_t)sq.pos * 2 * KVH * HD + KVH * HD, v.data(), KVH * HD * 2);
-        const int L = sq.pos + 1;
-        const float scale = 1.0f / 16.0f;
-        for (int hh = 0; hh < QH; ++hh) {
-          const int kvh = hh / (QH / KVH);
-          std::vector<float> sc(L);
-          float mx = -1e30f;
-          for (int p = 0; p < L; ++p) {
-            float dot = 0.f;
-            const uint16_t* kr = cache + (size_t)p * 2 * KVH * HD + kvh * HD;
-            for (int d = 0; d < HD; ++d) dot += h2f(q[hh * HD + d]) * h2f(kr[d]);
-            sc[p] = dot * scale;
-            mx = std::max(mx, sc[p]);
-          }
-          float sum = 0.f;
-          std::vector<float> acc(HD, 0.f);
-          for (int p = 0; p < L; ++p) {
-            const float w = oracle::exp_d(sc[p] - mx);
-            sum += w;
-            const uint16_t* vr = cache + (size_t)p * 2 * KVH * HD + KVH * HD + kvh * HD;
-            for (int d = 0; d < HD; ++d) acc[d] += w * h2f(vr[d]);
-          }
-          const float inv = 1.0f / (sum + 1e-30f);
-          for (int d = 0; d < HD; ++d) att[hh * HD + d] = f2h(acc[d] * inv);
-        }
-        for (int i = 0; i < QH * HD; ++i) {
-          const float g = h2f(gate[i]);
-          gated[i] = f2h(h2f(att[i]) * (1.0f / (1.0f + oracle::exp_d(-g))));
-        }
+        attention_token(proj.data(), m->W(P + "attn_q_norm"), m->W(P + "attn_k_norm"), eps,
+                        m->rope.data() + (size_t)sq.pos * ROT, cache, sq.pos, gated.data());
         matvec(m->W(P + "attn_o"), gated.data(), HID, QH * HD, y.data(), threads);
         ++ai;
       }
@@ -311,20 +342,7 @@ extern "C" int oracle_model_step(oracle_model* m, const int* tokens, int* out_to
     if (hidden_out) std::memcpy(hidden_out + b * HID, x.data(), HID * 2);
     std::vector<uint16_t> logits(m->vocab);
     matvec(emb, x.data(), m->vocab, HID, logits.data(), threads);
-    int best = 0;
-    float bv = -3.402823466e+38f, second = -3.402823466e+38f;
-    for (int i = 0; i < m->vocab; ++i) {
-      const float v = h2f(logits[i]);
-      if (v > bv) {
-        second = bv;
-        bv = v;
-        best = i;
-      } else if (v > second) {
-        second = v;
-      }
-    }
-    out_tokens[b] = best;
-    if (margin) margin[b] = bv - second;
+    out_tokens[b] = argmax16(logits.data(), m->vocab, margin ? margin + b : nullptr);
     sq.pos += 1;
   }
   return 0;
@@ -333,4 +351,24 @@ extern "C" int oracle_model_step(oracle_model* m, const int* tokens, int* out_to
 // matvec.comp on its own (per-op parity tests): y[out] = fp16(W[out][in] . x).
 extern "C" void oracle_matvec(const uint16_t* W, const uint16_t* x, int out, int in, uint16_t* y, int threads) {
   matvec(W, x, out, in, y, threads);
+}
+
+// rms_norm.comp on one 1024-wide row: y = fp16(x * (1/sqrt(mean(x^2) + eps)) * (1 + w)).
+extern "C" void oracle_rms_norm(const uint16_t* x, const uint16_t* w, float eps, uint16_t* y) { rmsnorm(x, w, eps, y); }
+
+// argmax.comp on fp16 logits [n].
+extern "C" int oracle_argmax(const uint16_t* logits, int n) { return argmax16(logits, n, nullptr); }
+
+// One attention token of one sequence (attention_token above); the RoPE row is
+// built here from theta with the reference's host formula.
+extern "C" void oracle_attention_decode(const uint16_t* proj, const uint16_t* qn_w, const uint16_t* kn_w, float eps,
+                                        float theta, uint16_t* cache, int pos, uint16_t* gated) {
+  float cs[ROT];
+  for (int i = 0; i < 32; ++i) {
+    const float inv_freq = 1.0f / std::pow(theta, 2.0f * (float)i / (float)ROT);
+    const float ang = (float)pos * inv_freq;
+    cs[2 * i] = std::cos(ang);
+    cs[2 * i + 1] = std::sin(ang);
+  }
+  attention_token(proj, qn_w, kn_w, eps, cs, cache, pos, gated);
 }

@@ -28,6 +28,10 @@ void oracle_model_reset(oracle_model* m, int batch);
 int oracle_model_step(oracle_model* m, const int* tokens, int* out_tokens, uint16_t* hidden_out,
                       float* margin, int threads);
 void oracle_matvec(const uint16_t* W, const uint16_t* x, int out, int in, uint16_t* y, int threads);
+void oracle_rms_norm(const uint16_t* x, const uint16_t* w, float eps, uint16_t* y);
+int oracle_argmax(const uint16_t* logits, int n);
+void oracle_attention_decode(const uint16_t* proj, const uint16_t* qn_w, const uint16_t* kn_w, float eps, float theta,
+                             uint16_t* cache, int pos, uint16_t* gated);
 void oracle_silu_gate(int64_t n, const uint16_t* gate, const uint16_t* up, uint16_t* out);
 void oracle_residual_add(int64_t n, const uint16_t* a, const uint16_t* b, uint16_t* out);
 void oracle_gbeta(int H, const uint16_t* a, const uint16_t* b, const float* a_log_bias, float* g, float* beta);

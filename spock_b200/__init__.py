@@ -38,7 +38,8 @@ EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
             "spock_deltanet_decode_step", "spock_deltanet_recurrent", "spock_chunk_prefill_noalloc",
             "spock_model_create", "spock_model_destroy", "spock_model_last_error", "spock_model_set_weight",
             "spock_model_reset", "spock_model_step", "spock_model_generate", "spock_model_load_artifact",
-            "spock_model_prefill", "spock_noalloc_sync", "spock_model_sync"]
+            "spock_model_prefill", "spock_noalloc_sync", "spock_model_sync",
+            "spock_rms_norm", "spock_matvec", "spock_argmax", "spock_attention_decode"]
 
 
 class SpockError(RuntimeError):
@@ -89,6 +90,11 @@ def lib():
         L.spock_chunk_prefill.argtypes = [vp, ctypes.POINTER(ChunkDesc)] + [vp] * 9
         L.spock_chunk_prefill_noalloc.argtypes = [ctypes.POINTER(ChunkDesc)] + [vp] * 9
         L.spock_noalloc_sync.argtypes = [vp]
+        L.spock_rms_norm.argtypes = [vp, vp, vp, vp, i64, i32, ctypes.c_float, vp]
+        L.spock_matvec.argtypes = [vp, i32, i32, vp, i32, i32, vp, i64, vp, vp, vp]
+        L.spock_argmax.argtypes = [vp, vp, i64, i64, vp, vp]
+        L.spock_attention_decode.argtypes = [vp, i32, vp, vp, vp, ctypes.c_float, ctypes.c_float, vp, vp, i32, i64,
+                                             vp, vp]
         L.spock_chunk_last_to_fp16.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp]
         L.spock_deltanet_decode_step.argtypes = [vp, ctypes.POINTER(DnLayer), i64] + [vp] * 9
         L.spock_deltanet_recurrent.argtypes = [vp, i64, i32, i32, i32] + [vp] * 8
@@ -189,6 +195,55 @@ def chunk_last_to_fp16(core_out, ctx=None, stream=None):
     ctx = ctx or Context.get(core_out.device.index or 0)
     out = torch.empty((B, H * V), dtype=torch.float16, device=core_out.device)
     ctx.check(lib().spock_chunk_last_to_fp16(ctx.h, B, H, S, V, _ptr(core_out), _ptr(out), _stream(stream)))
+    return out
+
+
+MV_STORE, MV_RESIDUAL, MV_SILU_GATE, MV_ARGMAX = 0, 1, 2, 3
+
+
+def rms_norm(x, w, eps=1e-6, out=None, ctx=None, stream=None):
+    """rms_norm.comp on fp16 rows x [rows, 1024] with (1+w) weights w [1024] fp16."""
+    import torch
+    ctx = ctx or Context.get(x.device.index or 0)
+    out = torch.empty_like(x) if out is None else out
+    ctx.check(lib().spock_rms_norm(ctx.h, _ptr(x), _ptr(w), _ptr(out), x.shape[0], x.shape[1], eps, _stream(stream)))
+    return out
+
+
+def matvec(w, x, epilogue=MV_STORE, residual=None, exact=False, out=None, ctx=None, stream=None):
+    """matvec.comp over rows x [rows, in] with fp16 W [out(, x2 for SILU_GATE), in] and a fused epilogue;
+    ARGMAX returns int32 token ids [rows]."""
+    import torch
+    ctx = ctx or Context.get(x.device.index or 0)
+    rows, n_in = x.shape
+    n_out = w.shape[0] // 2 if epilogue == MV_SILU_GATE else w.shape[0]
+    if out is None:
+        out = (torch.empty(rows, dtype=torch.int32, device=x.device) if epilogue == MV_ARGMAX
+               else torch.empty((rows, n_out), dtype=torch.float16, device=x.device))
+    ctx.check(lib().spock_matvec(ctx.h, int(epilogue), int(bool(exact)), _ptr(w), n_out, n_in, _ptr(x), rows,
+                                 _ptr(out), _ptr(residual), _stream(stream)))
+    return out
+
+
+def argmax(logits, ctx=None, stream=None):
+    """argmax.comp per row of fp16 logits [rows, n] -> int32 [rows] (lowest index among ties)."""
+    import torch
+    ctx = ctx or Context.get(logits.device.index or 0)
+    out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    ctx.check(lib().spock_argmax(ctx.h, _ptr(logits), logits.shape[0], logits.shape[1], _ptr(out), _stream(stream)))
+    return out
+
+
+def attention_decode(proj, q_norm, k_norm, pos, kv_cache, eps=1e-6, theta=1e7, exact=False, ctx=None, stream=None):
+    """One gated-attention decode token per sequence: proj [rows, 5120] fp16, pos int32 [rows],
+    kv_cache [rows, max_seq, 2, 2, 256] fp16 (row pos written) -> out [rows, 2048] fp16."""
+    import torch
+    ctx = ctx or Context.get(proj.device.index or 0)
+    rows = proj.shape[0]
+    out = torch.empty((rows, 2048), dtype=torch.float16, device=proj.device)
+    ctx.check(lib().spock_attention_decode(ctx.h, int(bool(exact)), _ptr(proj), _ptr(q_norm), _ptr(k_norm), eps, theta,
+                                           _ptr(pos), _ptr(kv_cache), kv_cache.shape[1], rows, _ptr(out),
+                                           _stream(stream)))
     return out
 
 

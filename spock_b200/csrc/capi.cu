@@ -9,6 +9,7 @@
 
 #include "chunk_scratch.h"
 #include "common.cuh"
+#include "ops.h"
 
 namespace spock {
 std::atomic<uint64_t> g_launches{0};
@@ -37,7 +38,9 @@ struct spock_ctx {
   int device = 0;
   std::string err;
   int* d_err_flag = nullptr;  // device word written by kernels whose bounded waits gave up
+  int sms = 148;
   spock::ChunkScratch chunk;
+  spock::OpsScratch ops;
 };
 
 namespace {
@@ -117,6 +120,8 @@ __attribute__((visibility("default"))) int spock_create(int device, spock_ctx** 
     delete c;
     return fail(nullptr, SPOCK_ERR_ALLOC, "spock_create: device allocation failed");
   }
+  c->ops.err = c->d_err_flag;
+  cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
   *out = c;
   return SPOCK_OK;
 }
@@ -127,6 +132,7 @@ __attribute__((visibility("default"))) int spock_destroy(spock_ctx* ctx) {
     DeviceGuard g(ctx->device);
     cudaFree(ctx->d_err_flag);
     ctx->chunk.release();
+    ctx->ops.release();
   }
   delete ctx;
   return SPOCK_OK;
@@ -227,6 +233,52 @@ __attribute__((visibility("default"))) int spock_deltanet_recurrent(
   DeviceGuard dg(ctx->device);
   return finish(ctx, spock::launch_recurrent(batch, num_heads, key_dim, value_dim, q, k, v, g,
                                              beta, state, out, ctx->d_err_flag, (cudaStream_t)stream));
+}
+
+__attribute__((visibility("default"))) int spock_rms_norm(spock_ctx* ctx, const void* x, const void* w, void* y,
+                                                          int64_t rows, int32_t dim, float eps, void* stream) {
+  if (!ctx) return fail(nullptr, SPOCK_ERR_INVALID, "spock_rms_norm: ctx is NULL");
+  if (!x || !w || !y || rows <= 0 || dim <= 0) return fail(ctx, SPOCK_ERR_INVALID, "spock_rms_norm: bad arguments");
+  DeviceGuard dg(ctx->device);
+  return finish(ctx, spock::op_rms_norm(x, w, y, rows, dim, eps, (cudaStream_t)stream));
+}
+
+__attribute__((visibility("default"))) int spock_matvec(spock_ctx* ctx, int32_t epilogue, int32_t exact, const void* w,
+                                                        int32_t out_dim, int32_t in_dim, const void* x, int64_t rows,
+                                                        void* y, const void* residual, void* stream) {
+  if (!ctx) return fail(nullptr, SPOCK_ERR_INVALID, "spock_matvec: ctx is NULL");
+  if (!w || !x || !y || rows <= 0 || out_dim <= 0 || in_dim <= 0 || epilogue < SPOCK_MV_STORE ||
+      epilogue > SPOCK_MV_ARGMAX || (epilogue == SPOCK_MV_RESIDUAL && !residual))
+    return fail(ctx, SPOCK_ERR_INVALID, "spock_matvec: bad arguments");
+  if (exact ? in_dim % 16 : (in_dim % 64 || (epilogue != SPOCK_MV_ARGMAX && out_dim % 8)))
+    return fail(ctx, SPOCK_ERR_UNSUPPORTED, exact ? "spock_matvec: exact path needs in_dim % 16 == 0"
+                                                  : "spock_matvec: fast path needs in_dim % 64 == 0, out_dim % 8 == 0");
+  if (epilogue == SPOCK_MV_SILU_GATE && out_dim % 16)
+    return fail(ctx, SPOCK_ERR_UNSUPPORTED, "spock_matvec: SILU_GATE needs out_dim % 16 == 0");
+  DeviceGuard dg(ctx->device);
+  return finish(ctx, spock::op_matvec(ctx->ops, epilogue, exact, w, out_dim, in_dim, x, rows, y, residual, ctx->sms,
+                                      (cudaStream_t)stream));
+}
+
+__attribute__((visibility("default"))) int spock_argmax(spock_ctx* ctx, const void* logits, int64_t rows, int64_t n,
+                                                        int32_t* idx, void* stream) {
+  if (!ctx) return fail(nullptr, SPOCK_ERR_INVALID, "spock_argmax: ctx is NULL");
+  if (!logits || !idx || rows <= 0 || n <= 0) return fail(ctx, SPOCK_ERR_INVALID, "spock_argmax: bad arguments");
+  DeviceGuard dg(ctx->device);
+  return finish(ctx, spock::op_argmax(logits, rows, n, idx, (cudaStream_t)stream));
+}
+
+__attribute__((visibility("default"))) int spock_attention_decode(spock_ctx* ctx, int32_t exact, const void* proj,
+                                                                  const void* q_norm, const void* k_norm, float eps,
+                                                                  float rope_theta, const int32_t* pos, void* kv_cache,
+                                                                  int32_t max_seq, int64_t rows, void* out,
+                                                                  void* stream) {
+  if (!ctx) return fail(nullptr, SPOCK_ERR_INVALID, "spock_attention_decode: ctx is NULL");
+  if (!proj || !q_norm || !k_norm || !pos || !kv_cache || !out || rows <= 0 || max_seq <= 0)
+    return fail(ctx, SPOCK_ERR_INVALID, "spock_attention_decode: bad arguments");
+  DeviceGuard dg(ctx->device);
+  return finish(ctx, spock::op_attention_decode(ctx->ops, exact, proj, q_norm, k_norm, eps, rope_theta, pos, kv_cache,
+                                                max_seq, rows, out, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -212,46 +212,171 @@ __global__ void __launch_bounds__(128) xgemv_kernel(const __half* __restrict__ x
   }
 }
 
-// ---- batched projection: register-tiled, sequential k per output ------------
-// CTA tile 128 weight rows x (16*TB) batch rows, 256 threads in a 16 x 16 grid,
-// each with 8 rows x TB batch columns. Thread (ty, tx) owns rows
-// base..base+3 and base+16..base+19 with base = (ty/4)*32 + (ty%4)*4 (so the
-// gate and up rows of one SWIGLU output pair sit in the same thread) and batch
-// columns tx*TB..tx*TB+TB-1. k advances 16 at a time through double-buffered
-// shared tiles (fp32, transposed: [k][row]); every output accumulates k in
-// order 0..K-1.
-constexpr int kTK = 16, kLDS = 132;
+// ---- small-batch projection, staged: one thread per weight row --------------
+// The same per-row order as xgemv_kernel, but the weights reach shared memory
+// through a ring of cp.async stages (kSt stages of 64 k for the CTA's rows,
+// each 16-byte chunk loaded by consecutive threads, so every row's 128 bytes
+// per stage arrive coalesced) and 64 threads per CTA keep twice as many CTAs
+// per projection. Thread t still accumulates its row's dot over k in order;
+// the row stride in shared memory (144 bytes) keeps the per-thread 16-byte
+// reads of 8 consecutive rows on distinct banks.
+constexpr int kRowB = 144;  // 128 bytes of a row's 64 k, padded
 
-template <int EPI, int TB>
-__global__ void __launch_bounds__(256) xgemm_kernel(const __half* __restrict__ x, int ldx,
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int EPI, int R, int kSt>
+__global__ void __launch_bounds__(64) xgemv2_kernel(const __half* __restrict__ x, int ldx,
                                                     const __half* __restrict__ W, int K, int N, int batch, Epi e,
                                                     float* __restrict__ amax_val, int* __restrict__ amax_idx) {
-  constexpr int BT = 16 * TB;  // batch rows per CTA
+  constexpr int NR = EPI == EPI_SWIGLU ? 2 : 1;
+  constexpr int ROWS = 64 * NR;          // weight rows of this CTA
+  constexpr int STAGE = ROWS * kRowB;    // bytes per ring stage
+  extern __shared__ __align__(16) uint8_t xg_sm[];
+  uint8_t* ring = xg_sm;
+  float* xs = reinterpret_cast<float*>(xg_sm + kSt * STAGE);  // [R][kXC]
+  const int t = threadIdx.x;
+  const int unit = blockIdx.x * 64 + t;
+  const int n_units = EPI == EPI_SWIGLU ? N / 2 : N;
+  const bool live = unit < n_units;
+  // weight row of CTA-local row r (SWIGLU: rows 0..63 gate, 64..127 up)
+  auto wrow = [&](int r) {
+    int u = blockIdx.x * 64 + (r & 63);
+    if (u >= n_units) u = n_units - 1;  // clamped: loads stay in bounds, results unused
+    if constexpr (EPI == EPI_SWIGLU) return (u >> 4) * 32 + (u & 15) + (r >= 64 ? 16 : 0);
+    return u;
+  };
+  const int nst = K / 64;
+  auto issue = [&](int s) {
+    if (s < nst) {
+      uint8_t* dst = ring + (s % kSt) * STAGE;
+#pragma unroll
+      for (int i = 0; i < ROWS * 8 / 64; ++i) {
+        const int c = t + 64 * i, r = c >> 3, col = c & 7;
+        cp_async16(dst + r * kRowB + col * 16, W + (size_t)wrow(r) * K + s * 64 + col * 8);
+      }
+    }
+    cp_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < kSt - 1; ++s) issue(s);  // weights: before the dependency wait
+  pdl_wait();
+  pdl_launch();
+  float acc[NR][R];
+#pragma unroll
+  for (int i = 0; i < NR; ++i)
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[i][r] = 0.f;
+  for (int s = 0; s < nst; ++s) {
+    cp_wait<kSt - 2>();
+    __syncthreads();  // stage s landed for every thread; stage s-1 is no longer read
+    issue(s + kSt - 1);
+    const int k0 = s * 64;
+    if ((k0 % kXC) == 0) {
+      for (int j = t; j < R * kXC; j += 64) {
+        const int r = j / kXC, kk = j % kXC;
+        xs[r * kXC + kk] = (r < batch && k0 + kk < K) ? __half2float(x[(size_t)r * ldx + k0 + kk]) : 0.f;
+      }
+      __syncthreads();
+    }
+    const uint8_t* st = ring + (s % kSt) * STAGE;
+    const int kx = k0 % kXC;
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      const uint4* wr = reinterpret_cast<const uint4*>(st + (t + 64 * i) * kRowB);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float w[8];
+        h8_to_f(wr[c], w);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const float4* xr = reinterpret_cast<const float4*>(xs + r * kXC + kx + c * 8);
+          const float4 x0 = xr[0], x1 = xr[1];
+          acc[i][r] = fmaf(w[0], x0.x, acc[i][r]);
+          acc[i][r] = fmaf(w[1], x0.y, acc[i][r]);
+          acc[i][r] = fmaf(w[2], x0.z, acc[i][r]);
+          acc[i][r] = fmaf(w[3], x0.w, acc[i][r]);
+          acc[i][r] = fmaf(w[4], x1.x, acc[i][r]);
+          acc[i][r] = fmaf(w[5], x1.y, acc[i][r]);
+          acc[i][r] = fmaf(w[6], x1.z, acc[i][r]);
+          acc[i][r] = fmaf(w[7], x1.w, acc[i][r]);
+        }
+      }
+    }
+  }
+  cp_wait<0>();
+  static_assert(EPI != EPI_ARGMAX, "the LM head keeps xgemv_kernel: one argmax partial per 128-row tile");
+  if (!live) return;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (r >= batch) break;
+    if constexpr (EPI == EPI_F16) store_f16(e, r, unit, acc[0][r]);
+    if constexpr (EPI == EPI_RESIDUAL) store_res(e, r, unit, acc[0][r]);
+    if constexpr (EPI == EPI_SWIGLU) store_swiglu(e, r, unit, acc[0][r], acc[NR - 1][r]);
+  }
+}
+
+// ---- batched projection: register-tiled, sequential k per output ------------
+// CTA tile TN weight rows x (16*TB) batch rows, (TN/8) x 16 threads, each with
+// 8 rows x TB batch columns. Thread (ty, tx) owns rows base..base+3 and
+// base+16..base+19 with base = (ty/4)*32 + (ty%4)*4 (so the gate and up rows
+// of one SWIGLU output pair sit in the same thread) and batch columns
+// tx*TB..tx*TB+TB-1. k advances 16 at a time through double-buffered shared
+// tiles (fp32, transposed: [k][row]); every output accumulates k in order
+// 0..K-1. TN = 64 doubles the CTAs of the narrow (1024-output) projections.
+constexpr int kTK = 16, kLDS = 132;
+
+template <int EPI, int TN, int TB>
+__global__ void __launch_bounds__(TN * 2) xgemm_kernel(const __half* __restrict__ x, int ldx,
+                                                       const __half* __restrict__ W, int K, int N, int batch, Epi e,
+                                                       float* __restrict__ amax_val, int* __restrict__ amax_idx) {
+  constexpr int BT = 16 * TB;     // batch rows per CTA
+  constexpr int NT = TN * 2;      // threads
   __shared__ __align__(16) float Ws[2][kTK][kLDS];
   __shared__ __align__(16) float Xs[2][kTK][kLDS];
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  const int n0 = blockIdx.x * 128, b0 = blockIdx.y * BT;
+  const int n0 = blockIdx.x * TN, b0 = blockIdx.y * BT;
   const int base = (ty >> 2) * 32 + (ty & 3) * 4;
-  // global -> register staging: W tile 128 rows x 16 k (thread: row tid/2, k half tid%2)
+  // global -> register staging: W tile TN rows x 16 k (thread: row tid/2, k half tid%2);
+  // X tile BT rows x 16 k in NT-thread passes
+  constexpr int XP = (BT * 2 + NT - 1) / NT;
   const int lr = tid >> 1, lk = (tid & 1) * 8;
   const bool wl = n0 + lr < N;
   const __half* wsrc = W + (size_t)(wl ? n0 + lr : 0) * K + lk;
-  const bool xl = tid < BT * 2 && b0 + lr < batch;
-  const __half* xsrc = x + (size_t)(xl ? b0 + lr : 0) * ldx + lk;
   const uint4 zero = make_uint4(0, 0, 0, 0);
   uint4 wr = wl ? __ldg(reinterpret_cast<const uint4*>(wsrc)) : zero;
   pdl_wait();
   pdl_launch();
-  uint4 xr = xl ? *reinterpret_cast<const uint4*>(xsrc) : zero;
+  uint4 xr[XP];
+  auto xload = [&](int kt) {
+#pragma unroll
+    for (int i = 0; i < XP; ++i) {
+      const int c = tid + NT * i, row = c >> 1;
+      const bool ok = c < BT * 2 && b0 + row < batch;
+      xr[i] = ok ? *reinterpret_cast<const uint4*>(x + (size_t)(b0 + row) * ldx + kt * kTK + (c & 1) * 8) : zero;
+    }
+  };
+  xload(0);
   auto stage = [&](int buf) {
     float f[8];
     h8_to_f(wr, f);
 #pragma unroll
     for (int i = 0; i < 8; ++i) Ws[buf][lk + i][lr] = f[i];
-    if (tid < BT * 2) {
-      h8_to_f(xr, f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) Xs[buf][lk + i][lr] = f[i];
+    for (int i = 0; i < XP; ++i) {
+      const int c = tid + NT * i;
+      if (c < BT * 2) {
+        h8_to_f(xr[i], f);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) Xs[buf][(c & 1) * 8 + q][c >> 1] = f[q];
+      }
     }
   };
   stage(0);
@@ -266,7 +391,7 @@ __global__ void __launch_bounds__(256) xgemm_kernel(const __half* __restrict__ x
     const int buf = kt & 1;
     if (kt + 1 < kt_n) {
       wr = wl ? __ldg(reinterpret_cast<const uint4*>(wsrc + (kt + 1) * kTK)) : zero;
-      xr = xl ? *reinterpret_cast<const uint4*>(xsrc + (kt + 1) * kTK) : zero;
+      xload(kt + 1);
     }
 #pragma unroll
     for (int kk = 0; kk < kTK; ++kk) {
@@ -292,6 +417,7 @@ __global__ void __launch_bounds__(256) xgemm_kernel(const __half* __restrict__ x
   }
   auto row_of = [&](int i) { return n0 + base + (i < 4 ? i : 12 + i); };  // i>=4: base+16+(i-4)
   if constexpr (EPI == EPI_ARGMAX) {
+    static_assert(TN == 128, "argmax partials are per 128-row tile");
     __syncthreads();  // the tiles are free: reuse them for the reduction
     float* rv = &Ws[0][0][0];                              // [16 ty][BT]
     int* ri = reinterpret_cast<int*>(&Xs[0][0][0]);        // [16 ty][BT]
@@ -382,6 +508,7 @@ __global__ void __launch_bounds__(256)
   for (int p = t; p < L; p += 256) {
     const uint4* kr = reinterpret_cast<const uint4*>(base + (size_t)p * (2 * KVH * HD) + kvh * HD);
     float dot[G] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
     for (int d8 = 0; d8 < HD / 8; ++d8) {
       float kf[8];
       h8_to_f(kr[d8], kf);
@@ -417,10 +544,24 @@ __global__ void __launch_bounds__(256)
   float acc[G] = {0.f, 0.f, 0.f, 0.f};
   float sum = 0.f;
   const __half* vb = base + KVH * HD + kvh * HD + t;
-  for (int p = 0; p < L; ++p) {
+  // positions in blocks of 8: the 8 value loads are issued before the
+  // sequential accumulation uses them (the order over positions is unchanged)
+  int p = 0;
+  for (; p + 8 <= L; p += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __half2float(vb[(size_t)(p + j) * (2 * KVH * HD)]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = acc[g] + xa_sm[g * L + p + j] * v[j];  // separate multiply and add
+      if (t < G) sum = sum + xa_sm[t * L + p + j];
+    }
+  }
+  for (; p < L; ++p) {
     const float v = __half2float(vb[(size_t)p * (2 * KVH * HD)]);
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = acc[g] + xa_sm[g * L + p] * v;  // separate multiply and add
+    for (int g = 0; g < G; ++g) acc[g] = acc[g] + xa_sm[g * L + p] * v;
     if (t < G) sum = sum + xa_sm[t * L + p];
   }
   __syncthreads();
@@ -437,13 +578,21 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---- DeltaNet ---------------------------------------------------------------
-// 128-wide sum of squares in the shaders' tree order (strides 64..1).
+// 128-wide sum of squares in the shaders' tree order (strides 64..1). The
+// strides 64 and 32 pair lanes of different warps (shared memory); strides
+// 16..1 run in warp 0 with shfl_down, which adds exactly the same pairs
+// (lane i takes lane i + stride), so the result is the shared-memory tree's.
 __device__ __forceinline__ float tree128(float* s, int t) {
   __syncthreads();
-  for (int stride = 64; stride > 0; stride >>= 1) {
-    if (t < stride) s[t] = s[t] + s[t + stride];
-    __syncthreads();
+  if (t < 64) s[t] = s[t] + s[t + 64];
+  __syncthreads();
+  if (t < 32) {
+    float v = s[t] + s[t + 32];
+#pragma unroll
+    for (int stride = 16; stride > 0; stride >>= 1) v = v + __shfl_down_sync(0xffffffffu, v, stride);
+    if (t == 0) s[0] = v;
   }
+  __syncthreads();
   const float r = s[0];
   __syncthreads();
   return r;
@@ -608,37 +757,76 @@ __global__ void __launch_bounds__(128)
   }
 }
 
-// Prefill, part 2: the recurrence over the prompt, token by token, for one
-// (sequence, head) per CTA with the state in registers; then the gated norm.
-__global__ void __launch_bounds__(128, 2)
+// Prefill, part 2: the recurrence over the prompt, token by token. Value
+// columns are independent in the recurrence, so a head's 128 columns are
+// split over 4 CTAs of one warp each (thread = column, its column of the
+// state in registers); the next token's inputs are loaded while the current
+// one is computed. Writes the raw outputs o = S^T (q * q_scale) as fp32
+// core [rows][2048]; part 3 applies the gated norm.
+constexpr int kRecCols = 32;
+__global__ void __launch_bounds__(kRecCols)
     xdn_prefill_rec_kernel(const __half* __restrict__ qi, const __half* __restrict__ ki,
                            const __half* __restrict__ vi, const float* __restrict__ gi,
-                           const float* __restrict__ bi, const __half* __restrict__ proj, int ld, int T,
-                           const float* __restrict__ norm_w, float eps, float* __restrict__ state,
-                           __half* __restrict__ out /*[rows][2048]*/) {
-  const int item = blockIdx.x, b = item / DNH, h = item % DNH, j = threadIdx.x;
-  __shared__ float sk[2][DND], sq[2][DND], red[DND];
+                           const float* __restrict__ bi, int T, float* __restrict__ state,
+                           float* __restrict__ core /*[rows][2048]*/) {
+  constexpr int SPLIT = DND / kRecCols;
+  const int item = blockIdx.x / SPLIT, part = blockIdx.x % SPLIT, b = item / DNH, h = item % DNH;
+  const int lane = threadIdx.x, j = part * kRecCols + lane;
+  __shared__ __align__(16) float sk[2][DND], sq[2][DND];
   float* Sg = state + (size_t)item * DND * DND;
   float S[DND];
 #pragma unroll
   for (int i = 0; i < DND; ++i) S[i] = Sg[i * DND + j];
   pdl_wait();
   pdl_launch();
-  const float w = norm_w[j];
-  for (int t = 0; t < T; ++t) {
+  const float q_scale = 1.0f / sqrtf((float)DND);
+  // this token's inputs: q, k (4 of the 128 per lane), v_j, g, beta
+  uint2 nq, nk;
+  float nv, ng, nb;
+  auto load = [&](int t) {
     const size_t r = (size_t)b * T + t;
+    nq = *reinterpret_cast<const uint2*>(qi + r * 2048 + h * DND + lane * 4);
+    nk = *reinterpret_cast<const uint2*>(ki + r * 2048 + h * DND + lane * 4);
+    nv = __half2float(vi[r * 2048 + h * DND + j]);
+    ng = gi[r * DNH + h];
+    nb = bi[r * DNH + h];
+  };
+  load(0);
+  for (int t = 0; t < T; ++t) {
     const int s = t & 1;
-    sq[s][j] = __half2float(qi[r * 2048 + h * DND + j]) * (1.0f / sqrtf((float)DND));
-    sk[s][j] = __half2float(ki[r * 2048 + h * DND + j]);
-    const float vj = __half2float(vi[r * 2048 + h * DND + j]);
-    const float g = gi[r * DNH + h], beta = bi[r * DNH + h];
-    const float z = __half2float(proj[r * ld + 6144 + h * DND + j]);
-    __syncthreads();
-    const float o = rec_column(S, sk[s], sq[s], vj, exp_d(g), beta);
-    out[r * 2048 + h * DND + j] = norm_gate(o, red, j, w, z, eps);
+    {
+      const __half2* q2 = reinterpret_cast<const __half2*>(&nq);
+      const __half2* k2 = reinterpret_cast<const __half2*>(&nk);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float2 qf = __half22float2(q2[e]), kf = __half22float2(k2[e]);
+        sq[s][lane * 4 + 2 * e] = qf.x * q_scale;
+        sq[s][lane * 4 + 2 * e + 1] = qf.y * q_scale;
+        sk[s][lane * 4 + 2 * e] = kf.x;
+        sk[s][lane * 4 + 2 * e + 1] = kf.y;
+      }
+    }
+    const float vj = nv, eg = exp_d(ng), beta = nb;
+    __syncwarp();
+    if (t + 1 < T) load(t + 1);
+    core[((size_t)b * T + t) * 2048 + h * DND + j] = rec_column(S, sk[s], sq[s], vj, eg, beta);
   }
 #pragma unroll
   for (int i = 0; i < DND; ++i) Sg[i * DND + j] = S[i];
+}
+
+// Prefill, part 3: the gated RMSNorm of every (token, head), all at once.
+// grid (rows, 16), 128 threads.
+__global__ void __launch_bounds__(128)
+    xdn_prefill_gate_kernel(const float* __restrict__ core, const __half* __restrict__ proj, int ld,
+                            const float* __restrict__ norm_w, float eps, __half* __restrict__ out) {
+  const int r = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
+  __shared__ float red[DND];
+  pdl_wait();
+  pdl_launch();
+  const float o = core[(size_t)r * 2048 + h * DND + j];
+  const float z = __half2float(proj[(size_t)r * ld + 6144 + h * DND + j]);
+  out[(size_t)r * 2048 + h * DND + j] = norm_gate(o, red, j, norm_w[j], z, eps);
 }
 
 template <int EPI, int R>
@@ -652,20 +840,67 @@ Status gemv_launch(const __half* x, int ldx, const __half* w, int K, int N, int 
   return Status::ok();
 }
 
-template <int EPI, int TB>
+template <int EPI, int R>
+Status gemv2_launch(const __half* x, int ldx, const __half* w, int K, int N, int batch, Epi e, float* av, int* ai,
+                    cudaStream_t st) {
+  constexpr int kSt = EPI == EPI_SWIGLU ? 4 : 6;
+  constexpr int NR = EPI == EPI_SWIGLU ? 2 : 1;
+  const size_t smem = (size_t)kSt * 64 * NR * kRowB + (size_t)R * kXC * 4;
+  // per device, once (the first call of a shape is eager, before any capture)
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    cudaError_t a = cudaFuncSetAttribute(xgemv2_kernel<EPI, R, kSt>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (a != cudaSuccess) return cuda_status(a, "xgemv2_kernel smem attribute");
+    configured.fetch_or(bit);
+  }
+  const int units = EPI == EPI_SWIGLU ? N / 2 : N;
+  cudaError_t err = launch_k(xgemv2_kernel<EPI, R, kSt>, dim3((units + 63) / 64), dim3(64), smem, st, x, ldx, w, K,
+                             N, batch, e, av, ai);
+  if (err != cudaSuccess) return cuda_status(err, "xgemv2_kernel");
+  SPOCK_LAUNCH_CHECK("xgemv2_kernel");
+  return Status::ok();
+}
+
+template <int EPI, int TN, int TB>
 Status gemm_launch(const __half* x, int ldx, const __half* w, int K, int N, int batch, Epi e, float* av, int* ai,
                    cudaStream_t st) {
   const int bt = 16 * TB;
-  cudaError_t err = launch_k(xgemm_kernel<EPI, TB>, dim3((N + 127) / 128, (batch + bt - 1) / bt), dim3(256), 0, st,
-                             x, ldx, w, K, N, batch, e, av, ai);
+  cudaError_t err = launch_k(xgemm_kernel<EPI, TN, TB>, dim3((N + TN - 1) / TN, (batch + bt - 1) / bt), dim3(TN * 2),
+                             0, st, x, ldx, w, K, N, batch, e, av, ai);
   if (err != cudaSuccess) return cuda_status(err, "xgemm_kernel");
   SPOCK_LAUNCH_CHECK("xgemm_kernel");
+  return Status::ok();
+}
+
+// The largest tile that still gives every SM two CTAs (fewer, larger tiles
+// re-read less but leave SMs idle on the narrow projections).
+template <int EPI>
+Status gemm_pick(const __half* x, int ldx, const __half* w, int K, int N, int batch, Epi e, float* av, int* ai,
+                 cudaStream_t st) {
+  auto ctas = [&](int tn, int tb) { return (int64_t)((N + tn - 1) / tn) * ((batch + 16 * tb - 1) / (16 * tb)); };
+  const int64_t want = 2 * 148;
+  if (EPI == EPI_ARGMAX || ctas(128, 8) >= want)
+    return batch > 64 ? gemm_launch<EPI, 128, 8>(x, ldx, w, K, N, batch, e, av, ai, st)
+                      : gemm_launch<EPI, 128, 4>(x, ldx, w, K, N, batch, e, av, ai, st);
+  if constexpr (EPI != EPI_ARGMAX) {
+    if (batch > 64 && ctas(64, 8) >= want) return gemm_launch<EPI, 64, 8>(x, ldx, w, K, N, batch, e, av, ai, st);
+    if (ctas(128, 4) >= want) return gemm_launch<EPI, 128, 4>(x, ldx, w, K, N, batch, e, av, ai, st);
+    return gemm_launch<EPI, 64, 4>(x, ldx, w, K, N, batch, e, av, ai, st);
+  }
   return Status::ok();
 }
 
 template <int EPI>
 Status proj_epi(const __half* x, int ldx, const __half* w, int K, int N, int batch, Epi e, float* av, int* ai,
                 cudaStream_t st) {
+  if constexpr (EPI != EPI_ARGMAX) {
+    if (batch == 1) return gemv2_launch<EPI, 1>(x, ldx, w, K, N, batch, e, av, ai, st);
+    if (batch == 2) return gemv2_launch<EPI, 2>(x, ldx, w, K, N, batch, e, av, ai, st);
+  }
   switch (batch) {
     case 1: return gemv_launch<EPI, 1>(x, ldx, w, K, N, batch, e, av, ai, st);
     case 2: return gemv_launch<EPI, 2>(x, ldx, w, K, N, batch, e, av, ai, st);
@@ -674,8 +909,7 @@ Status proj_epi(const __half* x, int ldx, const __half* w, int K, int N, int bat
     case 5: case 6: case 7: case 8: return gemv_launch<EPI, 8>(x, ldx, w, K, N, batch, e, av, ai, st);
     default: break;
   }
-  if (batch <= 64) return gemm_launch<EPI, 4>(x, ldx, w, K, N, batch, e, av, ai, st);
-  return gemm_launch<EPI, 8>(x, ldx, w, K, N, batch, e, av, ai, st);
+  return gemm_pick<EPI>(x, ldx, w, K, N, batch, e, av, ai, st);
 }
 
 }  // namespace
@@ -730,17 +964,21 @@ Status launch_exact_dn_decode(void* proj, int ld, void* conv, const void* conv_w
 
 Status launch_exact_dn_prefill(const void* proj, int ld, int batch, int T, const void* conv_w, const void* conv_old,
                                void* conv_new, const float* alb, const float* norm_w, float eps, void* q, void* k,
-                               void* v, float* g, float* beta, float* state, void* out, cudaStream_t st) {
+                               void* v, float* g, float* beta, float* core, float* state, void* out, cudaStream_t st) {
   cudaError_t e = launch_k(xk::xdn_prefill_conv_kernel, dim3(batch * T, xk::DNH), dim3(128), 0, st,
                            (const __half*)proj, ld, T, (const __half*)conv_w, (const __half*)conv_old,
                            (__half*)conv_new, alb, (__half*)q, (__half*)k, (__half*)v, g, beta);
   if (e != cudaSuccess) return cuda_status(e, "xdn_prefill_conv_kernel");
   SPOCK_LAUNCH_CHECK("xdn_prefill_conv_kernel");
-  e = launch_k(xk::xdn_prefill_rec_kernel, dim3(batch * xk::DNH), dim3(128), 0, st, (const __half*)q,
-               (const __half*)k, (const __half*)v, (const float*)g, (const float*)beta, (const __half*)proj, ld, T,
-               norm_w, eps, state, (__half*)out);
+  e = launch_k(xk::xdn_prefill_rec_kernel, dim3(batch * xk::DNH * (xk::DND / xk::kRecCols)), dim3(xk::kRecCols), 0,
+               st, (const __half*)q, (const __half*)k, (const __half*)v, (const float*)g, (const float*)beta, T, state,
+               core);
   if (e != cudaSuccess) return cuda_status(e, "xdn_prefill_rec_kernel");
   SPOCK_LAUNCH_CHECK("xdn_prefill_rec_kernel");
+  e = launch_k(xk::xdn_prefill_gate_kernel, dim3(batch * T, xk::DNH), dim3(128), 0, st, (const float*)core,
+               (const __half*)proj, ld, norm_w, eps, (__half*)out);
+  if (e != cudaSuccess) return cuda_status(e, "xdn_prefill_gate_kernel");
+  SPOCK_LAUNCH_CHECK("xdn_prefill_gate_kernel");
   return Status::ok();
 }
 

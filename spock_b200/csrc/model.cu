@@ -79,7 +79,8 @@ Status launch_exact_dn_decode(void* proj, int ld, void* conv, const void* conv_w
                               float eps, float* state, void* out, int ldo, int batch, cudaStream_t st);
 Status launch_exact_dn_prefill(const void* proj, int ld, int batch, int T, const void* conv_w, const void* conv_old,
                                void* conv_new, const float* alb, const float* norm_w, float eps, void* q, void* k,
-                               void* v, float* g, float* beta, float* state, void* out, cudaStream_t stream);
+                               void* v, float* g, float* beta, float* core, float* state, void* out,
+                               cudaStream_t stream);
 Status launch_dn_prefill_conv(const void* proj, int ld, int batch, int T, int H, const void* conv_w,
                               const void* conv_old, void* conv_new, const float* a_log_bias, void* q, void* k, void* v,
                               float* g, float* beta, cudaStream_t st);
@@ -389,7 +390,7 @@ Status record_prefill_exact(spock_model* m, const int32_t* prompt, int T, cudaSt
       if (cudaMemcpyAsync(p.conv_old, conv, (size_t)B * CONV * 4 * 2, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
         return Status::err(SPOCK_ERR_CUDA, "model prefill: conv snapshot failed");
       TRY(spock::launch_exact_dn_prefill(p.proj, DN_IN, B, T, l.conv_w, p.conv_old, conv, l.a_log_bias, l.dn_norm, eps,
-                                         p.q, p.k, p.v, p.g, p.beta, state, p.mix, st));
+                                         p.q, p.k, p.v, p.g, p.beta, p.core, state, p.mix, st));
       TRY(xproj(m, spock::EPI_RESIDUAL, p.mix, DNH * DND, l.w_out, DNH * DND, HID, R, p.h, HID, p.h, st));
     } else {
       TRY(xproj(m, spock::EPI_F16, p.x, HID, l.w_in, HID, ATT_IN, R, p.proj, ATT_IN, nullptr, st));
