@@ -264,6 +264,16 @@ int spock_attention_decode(spock_ctx* ctx, int32_t exact, const void* proj, cons
                            float eps, float rope_theta, const int32_t* pos, void* kv_cache, int32_t max_seq,
                            int64_t rows, void* out, void* stream);
 
+/* The same for `len` consecutive prompt tokens of each of `batch` sequences
+ * (the layer-major prefill's attention, vk_session.cpp:1166-1443 in the
+ * reference): proj [batch][len][5120]; pos int32 [batch] is each sequence's
+ * first prompt position (token t sits at pos + t); every row's K/V is stored
+ * first, then row t attends causally to positions 0 .. pos + t.
+ * out [batch][len][2048]. The fast path runs the tcgen05 tile kernel. */
+int spock_attention_prefill(spock_ctx* ctx, int32_t exact, const void* proj, const void* q_norm, const void* k_norm,
+                            float eps, float rope_theta, const int32_t* pos, void* kv_cache, int32_t max_seq,
+                            int64_t batch, int32_t len, void* out, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Full-model decode (Qwen3.5-0.8B layout): the decode glue around the mixer. */
 /* ------------------------------------------------------------------------ */

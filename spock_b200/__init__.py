@@ -39,7 +39,7 @@ EXPORTED = ["spock_create", "spock_destroy", "spock_last_error", "spock_sync",
             "spock_model_create", "spock_model_destroy", "spock_model_last_error", "spock_model_set_weight",
             "spock_model_reset", "spock_model_step", "spock_model_generate", "spock_model_load_artifact",
             "spock_model_prefill", "spock_noalloc_sync", "spock_model_sync",
-            "spock_rms_norm", "spock_matvec", "spock_argmax", "spock_attention_decode"]
+            "spock_rms_norm", "spock_matvec", "spock_argmax", "spock_attention_decode", "spock_attention_prefill"]
 
 
 class SpockError(RuntimeError):
@@ -95,6 +95,8 @@ def lib():
         L.spock_argmax.argtypes = [vp, vp, i64, i64, vp, vp]
         L.spock_attention_decode.argtypes = [vp, i32, vp, vp, vp, ctypes.c_float, ctypes.c_float, vp, vp, i32, i64,
                                              vp, vp]
+        L.spock_attention_prefill.argtypes = [vp, i32, vp, vp, vp, ctypes.c_float, ctypes.c_float, vp, vp, i32, i64,
+                                              i32, vp, vp]
         L.spock_chunk_last_to_fp16.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp]
         L.spock_deltanet_decode_step.argtypes = [vp, ctypes.POINTER(DnLayer), i64] + [vp] * 9
         L.spock_deltanet_recurrent.argtypes = [vp, i64, i32, i32, i32] + [vp] * 8
@@ -244,6 +246,19 @@ def attention_decode(proj, q_norm, k_norm, pos, kv_cache, eps=1e-6, theta=1e7, e
     ctx.check(lib().spock_attention_decode(ctx.h, int(bool(exact)), _ptr(proj), _ptr(q_norm), _ptr(k_norm), eps, theta,
                                            _ptr(pos), _ptr(kv_cache), kv_cache.shape[1], rows, _ptr(out),
                                            _stream(stream)))
+    return out
+
+
+def attention_prefill(proj, q_norm, k_norm, pos, kv_cache, eps=1e-6, theta=1e7, exact=False, ctx=None, stream=None):
+    """Gated attention over `len` prompt tokens per sequence: proj [batch, len, 5120] fp16, pos int32 [batch]
+    (first prompt position), kv_cache [batch, max_seq, 2, 2, 256] fp16 -> out [batch, len, 2048] fp16."""
+    import torch
+    ctx = ctx or Context.get(proj.device.index or 0)
+    B, T = proj.shape[0], proj.shape[1]
+    out = torch.empty((B, T, 2048), dtype=torch.float16, device=proj.device)
+    ctx.check(lib().spock_attention_prefill(ctx.h, int(bool(exact)), _ptr(proj), _ptr(q_norm), _ptr(k_norm), eps,
+                                            theta, _ptr(pos), _ptr(kv_cache), kv_cache.shape[1], B, T, _ptr(out),
+                                            _stream(stream)))
     return out
 
 

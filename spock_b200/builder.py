@@ -6,7 +6,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 SOURCES = ["capi.cu", "decode_step.cu", "chunk_prefill.cu", "chunk_pipeline.cu", "gemm.cu", "model_kernels.cu", "prefill.cu",
-           "exact.cu", "ops.cu", "model.cu"]
+           "exact.cu", "ops.cu", "attn_tc.cu", "model.cu"]
 # per-file flags: the exact-order kernels must not contract a*b+c into fma
 EXTRA = {"exact.cu": ["--fmad=false"]}
 LIB = os.path.join(HERE, "libspock_b200.so")

@@ -281,4 +281,17 @@ __attribute__((visibility("default"))) int spock_attention_decode(spock_ctx* ctx
                                                 max_seq, rows, out, (cudaStream_t)stream));
 }
 
+__attribute__((visibility("default"))) int spock_attention_prefill(spock_ctx* ctx, int32_t exact, const void* proj,
+                                                                   const void* q_norm, const void* k_norm, float eps,
+                                                                   float rope_theta, const int32_t* pos,
+                                                                   void* kv_cache, int32_t max_seq, int64_t batch,
+                                                                   int32_t len, void* out, void* stream) {
+  if (!ctx) return fail(nullptr, SPOCK_ERR_INVALID, "spock_attention_prefill: ctx is NULL");
+  if (!proj || !q_norm || !k_norm || !pos || !kv_cache || !out || batch <= 0 || len <= 0 || max_seq <= 0)
+    return fail(ctx, SPOCK_ERR_INVALID, "spock_attention_prefill: bad arguments");
+  DeviceGuard dg(ctx->device);
+  return finish(ctx, spock::op_attention_decode(ctx->ops, exact, proj, q_norm, k_norm, eps, rope_theta, pos, kv_cache,
+                                                max_seq, batch * len, out, (cudaStream_t)stream, len));
+}
+
 }  // extern "C"

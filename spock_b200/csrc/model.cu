@@ -41,9 +41,8 @@ Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* k
 Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
                           int64_t kv_layer_off, const int* pos, float scale, void* out, int rows,
                           cudaStream_t st, int rows_per_seq = 1);
-Status launch_attn_prefill(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
-                           int64_t kv_layer_off, const int* pos, float scale, void* out, int batch, int T,
-                           cudaStream_t st);
+Status launch_attn_prefill_tc(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride, int max_seq,
+                              const int* pos, float scale, void* out, int batch, int T, int* err, cudaStream_t st);
 Status launch_decode_step_strided(const spock_dn_layer& L, int64_t batch, void* qkv, int qkv_ld,
                                   void* conv_state, float* state, const void* a, const void* b, int ab_ld,
                                   const void* z, int z_ld, void* out, int out_ld, void* core_raw, int* err,
@@ -445,9 +444,9 @@ Status record_prefill(spock_model* m, const int32_t* prompt, int T, cudaStream_t
       const int64_t layer_off = (int64_t)l.attn_idx * m->d.max_seq * 2 * KVH * HD;
       TRY(spock::launch_attn_prep(p.proj, ATT_IN, l.q_norm, l.k_norm, m->rope, m->pos, p.aq, p.agate, m->kv,
                                   m->kv_seq_stride, layer_off, eps, R, st, T));
-      if (T > 1)  // query tiles on the tensor cores
-        TRY(spock::launch_attn_prefill(p.aq, p.agate, m->kv, m->kv_seq_stride, layer_off, m->pos, 1.0f / 16.0f, p.mix,
-                                       B, T, st));
+      if (T > 1)  // query tiles on the tcgen05 tensor cores
+        TRY(spock::launch_attn_prefill_tc(p.aq, p.agate, (const __half*)m->kv + layer_off, m->kv_seq_stride,
+                                          m->d.max_seq, m->pos, 1.0f / 16.0f, p.mix, B, T, m->err_flag, st));
       else
         TRY(spock::launch_attn_decode(p.aq, p.agate, m->kv, m->kv_seq_stride, layer_off, m->pos, 1.0f / 16.0f, p.mix,
                                       R, st, T));

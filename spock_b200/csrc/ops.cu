@@ -22,6 +22,8 @@ Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64
                           cudaStream_t st, int rows_per_seq = 1);
 Status launch_exact_proj(int epi, const void* x, int ldx, const void* w, int K, int N, int batch, void* y, int ldy,
                          const void* res, float* amax_val, int* amax_idx, cudaStream_t st);
+Status launch_attn_prefill_tc(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride, int max_seq,
+                              const int* pos, float scale, void* out, int batch, int T, int* err, cudaStream_t st);
 Status launch_exact_attn(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride, int64_t kv_layer_off,
                          const int* pos, int max_seq, float scale, void* out, int rows, int rows_per_seq,
                          cudaStream_t st);
@@ -139,7 +141,7 @@ Status op_matvec(OpsScratch& sc, int epilogue, int exact, const void* w, int out
 
 Status op_attention_decode(OpsScratch& sc, int exact, const void* proj, const void* qn, const void* kn, float eps,
                            float theta, const int32_t* pos, void* kv, int max_seq, int64_t rows, void* out,
-                           cudaStream_t st) {
+                           cudaStream_t st, int rows_per_seq) {
   if (rows > 0x7fffffff) return Status::err(SPOCK_ERR_INVALID, "spock_attention_decode: too many rows");
   // RoPE table [max_seq][32 x (cos, sin)], built on the host with the
   // reference's formula (vk_session.cpp:333-346) and kept per (theta, max_seq)
@@ -167,8 +169,14 @@ Status op_attention_decode(OpsScratch& sc, int exact, const void* proj, const vo
   __half* gate = q + (size_t)rows * 2048;
   const int64_t stride = (int64_t)max_seq * 2 * 2 * 256;  // one layer per sequence
   const float* rope = static_cast<const float*>(sc.rope.buf);
-  if ((s = launch_attn_prep(proj, 5120, qn, kn, rope, pos, q, gate, kv, stride, 0, eps, (int)rows, st)).code) return s;
-  if (exact) return launch_exact_attn(q, gate, kv, stride, 0, pos, max_seq, 1.0f / 16.0f, out, (int)rows, 1, st);
+  if ((s = launch_attn_prep(proj, 5120, qn, kn, rope, pos, q, gate, kv, stride, 0, eps, (int)rows, st,
+                            rows_per_seq)).code)
+    return s;
+  if (exact)
+    return launch_exact_attn(q, gate, kv, stride, 0, pos, max_seq, 1.0f / 16.0f, out, (int)rows, rows_per_seq, st);
+  if (rows_per_seq > 1)  // prompt rows: the tcgen05 prefill kernel
+    return launch_attn_prefill_tc(q, gate, kv, stride, max_seq, pos, 1.0f / 16.0f, out, (int)(rows / rows_per_seq),
+                                  rows_per_seq, sc.err, st);
   return launch_attn_decode(q, gate, kv, stride, 0, pos, 1.0f / 16.0f, out, (int)rows, st);
 }
 

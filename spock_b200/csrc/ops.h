@@ -25,5 +25,5 @@ Status op_matvec(OpsScratch& sc, int epilogue, int exact, const void* w, int out
                  int64_t rows, void* y, const void* res, int sms, cudaStream_t st);
 Status op_attention_decode(OpsScratch& sc, int exact, const void* proj, const void* qn, const void* kn, float eps,
                            float theta, const int32_t* pos, void* kv, int max_seq, int64_t rows, void* out,
-                           cudaStream_t st);
+                           cudaStream_t st, int rows_per_seq = 1);
 }  // namespace spock

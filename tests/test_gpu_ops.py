@@ -144,3 +144,33 @@ def test_attention_decode(cuda_ok, exact):
             assert np.array_equal(got[r], ref), r
         else:
             assert close16(got[r], ref), (r, int(fp16_ulp_diff(got[r], ref).max()))
+
+
+@pytest.mark.parametrize("exact", [True, False])
+def test_attention_prefill(cuda_ok, exact):
+    """The layer-major prefill's attention for 2 sequences x 70 prompt tokens
+    (3 query tiles of the tcgen05 kernel, 2-3 KV tiles each), the second
+    sequence continuing after 40 cached positions: every row against the
+    oracle's token-serial attention over the same cache."""
+    rng = np.random.default_rng(12)
+    B, T, max_seq = 2, 70, 128
+    pos = np.array([0, 40], np.int32)
+    proj = _h((B, T, 5120), 1.0, rng)
+    qn, kn = _h(256, 0.1, rng), _h(256, 0.1, rng)
+    cache = _h((B, max_seq, 2, 2, 256), 1.0, rng)
+    kv = _dev(cache)
+    out = spock_b200.attention_prefill(_dev(proj), _dev(qn), _dev(kn), _dev(pos), kv, exact=exact)
+    torch.cuda.synchronize()
+    got = _bits(out)
+    worst = 0
+    for b in range(B):
+        c = cache[b].view(np.uint16)
+        for t in range(T):
+            ref, c = oracle.attention_decode(proj[b, t].view(np.uint16), qn.view(np.uint16), kn.view(np.uint16), c,
+                                             pos[b] + t)
+            if exact:
+                assert np.array_equal(got[b, t], ref), (b, t)
+            else:
+                assert close16(got[b, t], ref), (b, t, int(fp16_ulp_diff(got[b, t], ref).max()))
+            worst = max(worst, int(fp16_ulp_diff(got[b, t], ref).max()))
+        assert np.array_equal(_bits(kv)[b, :pos[b] + T], c[:pos[b] + T]), b
