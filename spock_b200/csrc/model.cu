@@ -40,7 +40,7 @@ Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* k
                         int64_t kv_layer_off, float eps, int rows, cudaStream_t st, int rows_per_seq = 1);
 Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
                           int64_t kv_layer_off, const int* pos, float scale, void* out, int rows,
-                          cudaStream_t st, int rows_per_seq = 1);
+                          cudaStream_t st, int rows_per_seq = 1, float* ws = nullptr, int* tickets = nullptr);
 Status launch_attn_prefill_tc(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride, int max_seq,
                               const int* pos, float scale, void* out, int batch, int T, int* err, cudaStream_t st);
 Status launch_decode_step_strided(const spock_dn_layer& L, int64_t batch, void* qkv, int qkv_ld,
@@ -117,6 +117,9 @@ struct spock_model {
   void *h = nullptr, *x = nullptr, *proj = nullptr, *mix = nullptr, *mlp = nullptr, *q = nullptr, *gate = nullptr;
   float *ws = nullptr;
   size_t ws_bytes = 0, tickets_bytes = 0;
+  // split decode attention (few rows): partials [rows][2][splits][1032] and tickets [rows][2]
+  float* attn_ws = nullptr;
+  int* attn_tickets = nullptr;
   int* tickets = nullptr;
   float* amax_val = nullptr;
   int* amax_idx = nullptr;
@@ -288,7 +291,7 @@ Status record_step(spock_model* m, cudaStream_t st) {
       TRY(spock::launch_attn_prep(m->proj, ATT_IN, l.q_norm, l.k_norm, m->rope, m->pos, m->q, m->gate, m->kv,
                                   m->kv_seq_stride, layer_off, eps, B, st));
       TRY(spock::launch_attn_decode(m->q, m->gate, m->kv, m->kv_seq_stride, layer_off, m->pos, 1.0f / 16.0f,
-                                    m->mix, B, st));
+                                    m->mix, B, st, 1, m->attn_ws, m->attn_tickets));
       TRY(gemm(m, spock::EPI_RESIDUAL, m->mix, l.w_out, HID, QH * HD, m->h, HID, m->h, st));
     }
     TRY(normed(spock::EPI_SWIGLU, l.post_norm, l.w_gu, 2 * INTER, m->mlp, INTER, nullptr));
@@ -449,7 +452,7 @@ Status record_prefill(spock_model* m, const int32_t* prompt, int T, cudaStream_t
                                           m->d.max_seq, m->pos, 1.0f / 16.0f, p.mix, B, T, m->err_flag, st));
       else
         TRY(spock::launch_attn_decode(p.aq, p.agate, m->kv, m->kv_seq_stride, layer_off, m->pos, 1.0f / 16.0f, p.mix,
-                                      R, st, T));
+                                      R, st, T, m->attn_ws, m->attn_tickets));
       TRY(gemm_rows(m, spock::EPI_RESIDUAL, p.mix, l.w_out, HID, QH * HD, p.h, HID, p.h, R, st));
     }
     TRY(spock::launch_rmsnorm(p.h, l.post_norm, p.x, eps, R, st));
@@ -577,6 +580,8 @@ __attribute__((visibility("default"))) int spock_model_create(spock_ctx* ctx, co
   A(&m->tok_out, (size_t)B * 4);
   A(&m->pos, (size_t)B * 4);
   A(&m->own_err, 4);
+  A(&m->attn_ws, (size_t)64 * 2 * 1032 * 4);  // rows x splits <= 64 (attn_decode_splits)
+  A(&m->attn_tickets, (size_t)16 * 2 * 4);
   m->err_flag = ctx ? spock::ctx_err_word(ctx) : m->own_err;
   const int ndn = n_dn(m), nat = n_attn(m);
   A(&m->dn_state, (size_t)ndn * B * DNH * DND * DND * 4);
@@ -824,6 +829,7 @@ __attribute__((visibility("default"))) int spock_model_reset(spock_model* m, int
   // launch, but a launch whose bounded wait gave up may leave them dirty
   cudaMemset(m->ws, 0, m->ws_bytes);
   cudaMemset(m->tickets, 0, m->tickets_bytes);
+  cudaMemset(m->attn_tickets, 0, (size_t)16 * 2 * 4);
   cudaError_t e = cudaDeviceSynchronize();
   return e == cudaSuccess ? SPOCK_OK : mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));
 }

@@ -113,9 +113,12 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// grid (rows, KVH), 256 threads = 8 warps; rows as in attn_prep_kernel, each
-// query row attends causally to positions 0 .. pos[seq] + row % T.
-// Warp w takes positions w, w+8, ...;
+// grid (rows, KVH, ns), 256 threads = 8 warps; rows as in attn_prep_kernel,
+// each query row attends causally to positions 0 .. pos[seq] + row % T.
+// With ns > 1 (few rows) the positions are split into ns contiguous ranges,
+// one per CTA; each CTA leaves its partial (max, sum, weighted V) in ws and
+// the last of a row's ns CTAs (atomic ticket, reset for the next launch)
+// merges them in range order. Within a CTA, warp w takes positions w, w+8, ...;
 // lane l owns dims 8l..8l+7 of the 4 query heads of this kv head (GQA group).
 // Online softmax per warp, merged across warps in shared memory; the output is
 // fp16(acc / (sum + 1e-30)) and then fp16(out * sigmoid(gate)).
@@ -123,7 +126,7 @@ __global__ void __launch_bounds__(256)
     attn_decode_kernel(const __half* __restrict__ q /*[batch][QH][HD]*/, const __half* __restrict__ gate,
                        const __half* __restrict__ kv, int64_t kv_seq_stride, int64_t kv_layer_off,
                        const int* __restrict__ pos, float scale, __half* __restrict__ out /*[rows][QH*HD]*/,
-                       int rows_per_seq) {
+                       int rows_per_seq, int ns, float* __restrict__ ws, int* __restrict__ tickets) {
   const int kvh = blockIdx.y, b = blockIdx.x;  // b: row
   const int seq = b / rows_per_seq;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -152,7 +155,8 @@ __global__ void __launch_bounds__(256)
     for (int k = 0; k < 8; ++k) acc[g][k] = 0.f;
   }
   const __half* base = kv + (size_t)seq * kv_seq_stride + kv_layer_off;
-  for (int p = warp; p < L; p += 8) {
+  const int span = (L + ns - 1) / ns, p_lo = blockIdx.z * span, p_hi = min(L, p_lo + span);
+  for (int p = p_lo + warp; p < p_hi; p += 8) {
     const __half* kr = base + (size_t)p * (2 * KVH * HD) + kvh * HD + lane * 8;
     const __half* vr = base + (size_t)p * (2 * KVH * HD) + KVH * HD + kvh * HD + lane * 8;
     const uint4 ku = *reinterpret_cast<const uint4*>(kr);
@@ -210,6 +214,42 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int k = 0; k < 4; ++k) at[k] += sm_acc[w][g][d0 + k] * c;
   }
+  if (ns > 1) {
+    // this range's partial -> ws[row][kvh][range]: m[4] | l[4] | acc[4][256]
+    float* part = ws + (((size_t)b * KVH + kvh) * ns + blockIdx.z) * (2 * G + G * HD);
+    if ((threadIdx.x & 63) == 0) {
+      part[g] = mt;
+      part[G + g] = lt;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) part[2 * G + g * HD + d0 + k] = at[k];
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+      int* tk = tickets + (size_t)b * KVH + kvh;
+      const int n = atomicAdd(tk, 1);
+      s_last = n == ns - 1;
+      if (s_last) *tk = 0;  // ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* parts = ws + ((size_t)b * KVH + kvh) * ns * (2 * G + G * HD);
+    mt = -INFINITY;
+    for (int z = 0; z < ns; ++z) mt = fmaxf(mt, __ldcg(parts + z * (2 * G + G * HD) + g));
+    lt = 0.f;
+    at[0] = at[1] = at[2] = at[3] = 0.f;
+    for (int z = 0; z < ns; ++z) {
+      const float* pz = parts + z * (2 * G + G * HD);
+      const float mz = __ldcg(pz + g);
+      if (mz == -INFINITY) continue;
+      const float c = expf(mz - mt);
+      lt += __ldcg(pz + G + g) * c;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) at[k] += __ldcg(pz + 2 * G + g * HD + d0 + k) * c;
+    }
+  }
   const float inv = 1.0f / (lt + 1e-30f);
   const int qh = kvh * G + g;
 #pragma unroll
@@ -245,11 +285,16 @@ Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* k
   return Status::ok();
 }
 
+// Position ranges per row for the split decode attention: enough CTAs to
+// occupy the SMs when there are few rows (the partials need ws/tickets).
+int attn_decode_splits(int rows) { return rows <= 4 ? 16 : (rows <= 16 ? 4 : 1); }
+
 Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
                           int64_t kv_layer_off, const int* pos, float scale, void* out, int rows,
-                          cudaStream_t st, int rows_per_seq) {
-  launch_k(attn_decode_kernel, dim3(rows, KVH), dim3(256), 0, st, (const __half*)q, (const __half*)gate,
-           (const __half*)kv, kv_seq_stride, kv_layer_off, pos, scale, (__half*)out, rows_per_seq);
+                          cudaStream_t st, int rows_per_seq, float* ws, int* tickets) {
+  const int ns = (ws && tickets) ? attn_decode_splits(rows) : 1;
+  launch_k(attn_decode_kernel, dim3(rows, KVH, ns), dim3(256), 0, st, (const __half*)q, (const __half*)gate,
+           (const __half*)kv, kv_seq_stride, kv_layer_off, pos, scale, (__half*)out, rows_per_seq, ns, ws, tickets);
   SPOCK_LAUNCH_CHECK("attn_decode_kernel");
   return Status::ok();
 }

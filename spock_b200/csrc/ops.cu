@@ -19,7 +19,8 @@ Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* k
                         int64_t kv_layer_off, float eps, int rows, cudaStream_t st, int rows_per_seq = 1);
 Status launch_attn_decode(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride,
                           int64_t kv_layer_off, const int* pos, float scale, void* out, int rows,
-                          cudaStream_t st, int rows_per_seq = 1);
+                          cudaStream_t st, int rows_per_seq = 1, float* ws = nullptr, int* tickets = nullptr);
+int attn_decode_splits(int rows);
 Status launch_exact_proj(int epi, const void* x, int ldx, const void* w, int K, int N, int batch, void* y, int ldy,
                          const void* res, float* amax_val, int* amax_idx, cudaStream_t st);
 Status launch_attn_prefill_tc(const void* q, const void* gate, const void* kv, int64_t kv_seq_stride, int max_seq,
@@ -177,7 +178,14 @@ Status op_attention_decode(OpsScratch& sc, int exact, const void* proj, const vo
   if (rows_per_seq > 1)  // prompt rows: the tcgen05 prefill kernel
     return launch_attn_prefill_tc(q, gate, kv, stride, max_seq, pos, 1.0f / 16.0f, out, (int)(rows / rows_per_seq),
                                   rows_per_seq, sc.err, st);
-  return launch_attn_decode(q, gate, kv, stride, 0, pos, 1.0f / 16.0f, out, (int)rows, st);
+  const int ns = attn_decode_splits((int)rows);
+  if (ns > 1) {
+    if ((s = grow(sc.attn_ws, (size_t)rows * 2 * ns * 1032 * 4, false)).code) return s;
+    if ((s = grow(sc.attn_tk, (size_t)rows * 2 * 4, true)).code) return s;
+  }
+  return launch_attn_decode(q, gate, kv, stride, 0, pos, 1.0f / 16.0f, out, (int)rows, st, 1,
+                            ns > 1 ? static_cast<float*>(sc.attn_ws.buf) : nullptr,
+                            ns > 1 ? static_cast<int*>(sc.attn_tk.buf) : nullptr);
 }
 
 }  // namespace spock

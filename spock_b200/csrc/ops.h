@@ -11,11 +11,13 @@ struct OpsScratch {
   ChunkScratch amax;     // argmax partials [tiles][rows] value + index
   ChunkScratch qg;       // attention: normalised / rotated q and the gate
   ChunkScratch rope;     // RoPE table [rope_seq][64]
+  ChunkScratch attn_ws;  // split decode attention: partials
+  ChunkScratch attn_tk;  // split decode attention: tickets (zero between launches)
   float rope_theta = 0.f;
   int rope_seq = 0;
   int* err = nullptr;    // the context's error word
   void release() {
-    for (ChunkScratch* s : {&xpad, &ws, &tickets, &amax, &qg, &rope}) s->release();
+    for (ChunkScratch* s : {&xpad, &ws, &tickets, &amax, &qg, &rope, &attn_ws, &attn_tk}) s->release();
   }
 };
 
