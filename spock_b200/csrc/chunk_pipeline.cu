@@ -65,7 +65,8 @@ static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 
 enum Bar {
   QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE0, G1_DONE1, TBE_READY, WT_DONE,
-  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, AW_READY, GC_READY0, GC_READY1, DRAIN, NUM_BARS
+  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, AW_READY, GC_READY0, GC_READY1, D1_FREE, S_DONE, DRAIN,
+  NUM_BARS
 };
 
 struct Small {
@@ -126,8 +127,23 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 }
 
 // Optional per-phase cycle accounting (compile with -DSPOCK_PHASE_PROF; never
-// in the shipped library): one row of 32 counters per CTA and role.
-#ifdef SPOCK_PHASE_PROF
+// in the shipped library): one row of 32 counters per CTA and role. With
+// -DSPOCK_TRACE_ONLY only the per-item event timestamps of CTA 0 are kept
+// (one clock read per event), which perturbs the timing far less.
+#if defined(SPOCK_TRACE_ONLY) && !defined(SPOCK_PHASE_PROF)
+__device__ long long g_trace[64 * 32];
+#define TRACE(ev, n)                                                                 \
+  do {                                                                               \
+    if (blockIdx.x == 0 && (n) < 64) g_trace[(n) * 32 + (ev)] = clock64();           \
+  } while (0)
+#define PROF_DECL
+#define PROF_MARK(role, k) \
+  do {                     \
+  } while (0)
+#define PROF_FLUSH(role) \
+  do {                   \
+  } while (0)
+#elif defined(SPOCK_PHASE_PROF)
 __device__ unsigned long long g_phase_prof[148 * 4 * 32];
 #define PROF_DECL                       \
   long long _pt = clock64();            \
@@ -232,7 +248,7 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
     // Greedy issue: each of the four MMA queues stays in item order, and
     // whichever queue's next group is ready goes first, so the prep of item
     // n+1 (G1, W^T) is not held behind the recurrence of item n.
-    int g1 = 0, wt = 0, um = 0, m2 = 0, pa = 0;
+    int g1 = 0, wt = 0, uu = 0, um = 0, m2 = 0, pa = 0;
     uint32_t idle = 0;
 #ifdef SPOCK_PHASE_PROF
     long long iters = 0;
@@ -249,6 +265,8 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_f16(mS, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_VS + ks * 2048, 8192, 1024),
                       ID_2A, 1);
+        // the next item's S16 waits only for the state update, not the output
+        tc::mma_commit(&sh->bar[S_DONE]);
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + 8192 + ks * 32, 16, 1024),
                       tc::sdesc(sbase + OFF_VN + ks * 2048, 8192, 1024), ID_U, 1);
@@ -261,13 +279,22 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
         ++m2;
         progressed = true;
       }
-      if (um < wt && um == m2 && tc::mbar_test_wait(&sh->bar[PREP_DONE], um & 1) &&
-          tc::mbar_test_wait(&sh->bar[S16_READY], um & 1) && tc::mbar_test_wait(&sh->bar[AW_READY], um & 1)) {
-        // U + MMA1 of item um: D1 = [T diag(beta); 0] V ; D1 += [-W ; Q'] S16
+      // U of item uu as soon as D1 is free (the REC group has stored the
+      // previous item's output rows) and PREP has published T diag(beta) and V:
+      // it then runs while the REC group builds -W and Q'
+      if (uu < N && uu == um && uu == m2 && tc::mbar_test_wait(&sh->bar[PREP_DONE], uu & 1) &&
+          tc::mbar_test_wait(&sh->bar[D1_FREE], uu & 1)) {
         tc::tc_fence_after();
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + ks * 32, 16, 1024),
                       tc::sdesc(sbase + OFF_V + ks * 2048, 8192, 1024), ID_U, ks > 0);
+        ++uu;
+        progressed = true;
+      }
+      if (um < wt && um < uu && tc::mbar_test_wait(&sh->bar[S16_READY], um & 1) &&
+          tc::mbar_test_wait(&sh->bar[AW_READY], um & 1)) {
+        // MMA1 of item um: D1 (= [T diag(beta); 0] V) += [-W ; Q'] S16
+        tc::tc_fence_after();
         for (int ks = 0; ks < 8; ++ks)
           tc::mma_f16(mD1, tc::sdesc(sbase + OFF_AW + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
                       tc::sdesc(sbase + OFF_SB + ks * 2048, 16384, 1024), ID_U, 1);
@@ -645,9 +672,14 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     // output of the previous item, off the S16 path; D1 is next written by
     // MMA1 of this item, which waits for AW_READY below
     if (n > 0) {
+      wait_all(M2_DONE, (n - 1) & 1);  // the previous item's output MMAs
+      tc::tc_fence_after();
       store_out(n - 1);
-      tc::tc_fence_before();
     }
+    // D1 is free for this item's U (its previous rows have all been read)
+    tc::tc_fence_before();
+    sync();
+    if (rt == 0) tc::mbar_arrive_expect_tx(&sh->bar[D1_FREE], 0);
     // 2b. A operand of MMA1: -W (from W^T in TMEM) and Q' = diag(s e^gc) Q.
     //     MMA1 of the previous item, the last reader of AW, has completed.
     wait_all(WT_DONE, n & 1);
@@ -728,8 +760,9 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     if (n + 1 < N) convert_v(n + 1);
     PROF_MARK(1, 4);
     if (rt == 0) TRACE(23, n);
-    // 4. output rows (lanes 64..127); final state after a pair's last chunk
-    wait_all(M2_DONE, n & 1);
+    // 4. final state after a pair's last chunk (the output rows are stored
+    //    at the next item, or after the loop)
+    wait_all(S_DONE, n & 1);
     PROF_MARK(1, 5);
     if (rt == 0) TRACE(24, n);
     tc::tc_fence_after();
@@ -748,7 +781,11 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     if (rt == 0) TRACE(25, n);
     if (group_any(BAR_REC, 128, bad)) break;
   }
-  if (N > 0 && !*abort) store_out(N - 1);
+  if (N > 0 && !*abort) {
+    wait_all(M2_DONE, (N - 1) & 1);
+    tc::tc_fence_after();
+    store_out(N - 1);
+  }
   PROF_FLUSH(1);
   if (*abort && rt == 0) atomicExch(err, 2);
 }
@@ -840,6 +877,8 @@ extern "C" __attribute__((visibility("default"))) int spock_debug_phase_profile(
   if (n > 148 * 4 * 32) n = 148 * 4 * 32;
   return (int)cudaMemcpyFromSymbol(out, spock::pipe::g_phase_prof, n * sizeof(unsigned long long));
 }
+#endif
+#if defined(SPOCK_PHASE_PROF) || defined(SPOCK_TRACE_ONLY)
 extern "C" __attribute__((visibility("default"))) int spock_debug_trace(long long* out) {
   return (int)cudaMemcpyFromSymbol(out, spock::pipe::g_trace, 64 * 32 * sizeof(long long));
 }

@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(128, 1)
   uint32_t ncols = 32;
   while ((int)ncols < a.bn) ncols <<= 1;
 
+  const int pre = nst < kStages ? nst : kStages;
   if (t == 0) {
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&full[s], 1);
@@ -115,7 +116,16 @@ __global__ void __launch_bounds__(128, 1)
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmw);
     tc::prefetch_tmap(&tmx);
+    // The weights do not depend on the previous kernel or on TMEM: the first
+    // stages' weight tiles stream while the TMEM allocation (which may wait
+    // for the previous kernel's CTA on this SM) and its dependency drain.
+    for (int i = 0; i < pre; ++i) {
+      tc::mbar_arrive_expect_tx(&full[i], subs(i) * sub_bytes);
+      for (int j = 0; j < subs(i); ++j)
+        tma_load_2d(sm + i * stage_bytes + j * sub_bytes, &tmw, &full[i], (kb0 + i * kKB + j) * 64, tile * 128);
+    }
   }
+  __syncwarp();
   if (warp == 0) {
     tc::tmem_alloc(s_tmem, ncols);
     tc::tmem_relinquish();
@@ -126,15 +136,7 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t tb = *s_tmem;
   bool ok = true;
 
-  if (warp == 0 && lane == 0) {  // TMA producer
-    // The weights do not depend on the previous kernel: the first stages'
-    // weight tiles stream while it drains; activations after pdl_wait.
-    const int pre = nst < kStages ? nst : kStages;
-    for (int i = 0; i < pre; ++i) {
-      tc::mbar_arrive_expect_tx(&full[i], subs(i) * sub_bytes);
-      for (int j = 0; j < subs(i); ++j)
-        tma_load_2d(sm + i * stage_bytes + j * sub_bytes, &tmw, &full[i], (kb0 + i * kKB + j) * 64, tile * 128);
-    }
+  if (warp == 0 && lane == 0) {  // TMA producer (the first stages' weights are in flight)
     pdl_wait();
     pdl_launch();
     for (int i = 0; i < pre; ++i)
