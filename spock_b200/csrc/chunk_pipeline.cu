@@ -65,7 +65,7 @@ static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 
 enum Bar {
   QK_FULL0, QK_FULL1, QK_EMPTY0, QK_EMPTY1, V_FULL, V_EMPTY, PREP_A, G1_DONE0, G1_DONE1, TBE_READY, WT_DONE,
-  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, AW_READY, GC_READY0, GC_READY1, D1_FREE, S_DONE, DRAIN,
+  PREP_DONE, S16_READY, M1_DONE, VN_READY, M2_DONE, V_CONV, AW_READY, GC_READY0, GC_READY1, D1_FREE, DRAIN,
   NUM_BARS
 };
 
@@ -265,8 +265,6 @@ __device__ void mma_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, int* err
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_f16(mS, tc::sdesc(k + ks * 2048, 16384, 1024), tc::sdesc(sbase + OFF_VS + ks * 2048, 8192, 1024),
                       ID_2A, 1);
-        // the next item's S16 waits only for the state update, not the output
-        tc::mma_commit(&sh->bar[S_DONE]);
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + 8192 + ks * 32, 16, 1024),
                       tc::sdesc(sbase + OFF_VN + ks * 2048, 8192, 1024), ID_U, 1);
@@ -761,8 +759,10 @@ __device__ void rec_role(uint8_t* sm, Small* sh, uint32_t tb, Items it, const fl
     PROF_MARK(1, 4);
     if (rt == 0) TRACE(23, n);
     // 4. final state after a pair's last chunk (the output rows are stored
-    //    at the next item, or after the loop)
-    wait_all(S_DONE, n & 1);
+    //    at the next item, or after the loop). All of M2 must be complete, not
+    //    just the state update: the next item's S16 overwrites VN/VS, which
+    //    the output MMA reads.
+    wait_all(M2_DONE, n & 1);
     PROF_MARK(1, 5);
     if (rt == 0) TRACE(24, n);
     tc::tc_fence_after();
