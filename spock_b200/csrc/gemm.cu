@@ -3,27 +3,15 @@
 // lm_head_tiled shaders (shaders/matvec.comp:28-41, matvec_tiled.comp:41-83,
 // lm_head_tiled.comp:40-86). Their outputs are fp16-rounded; so are these.
 //
-// Swap-AB tcgen05 GEMM: a 128-row slab of W is the M=128 operand (K-major, TMA,
-// 128B swizzle) and a block of up to 256 activation rows is the N operand, so
-// one pass over the weights serves the whole batch; decode is HBM-bound on W.
-// Prefill row counts run as many such blocks in one launch.
-// Accumulators live in TMEM (lane = weight row, column = batch row).
-//
-// Grid: (row tiles, K splits, batch blocks). Large batches are split over
-// batch blocks of bn >= 32 rows first (no partial sums: the CTAs of one row
-// tile share its weight slab through L2), then over K while the grid is
-// shorter than the SM count (one CTA streams its slab at a bounded rate, so a
-// short grid leaves HBM idle). Up to 8 K splits of a tile run as one
-// thread-block cluster: ranks 1.. park their fp32 partial tile in shared
-// memory and rank 0 adds them in rank order through distributed shared memory
-// (deterministic, no global traffic). More splits (small batches with long K)
-// add vector atomics into an L2-resident accumulator; the last CTA of a tile
-// (atomic ticket) reads the sum once, clears it for the next launch and runs
-// the epilogue, with the split count capped so partial traffic stays below
-// the weight traffic it parallelises.
-//
-// The epilogue stages the fp16 tile in shared memory (TMEM lanes are weight
-// rows) and writes it back, with the residual, in 16-byte row segments.
+// More than 8 activation rows: a persistent tcgen05 GEMM (gemm_tc_kernel).
+// A 128-row slab of W is the M=128 operand (K-major, TMA, 128B swizzle) and
+// a block of up to 256 activation rows is the N operand, so one pass over the
+// weights serves a whole block; decode is HBM-bound on W. Accumulators live
+// in TMEM (lane = weight row, column = activation row), double-buffered so a
+// unit's epilogue overlaps the next unit's MMAs. Short grids split K over a
+// thread-block cluster whose ranks exchange fp32 partials through an
+// L2-resident workspace and reduce them in rank order (deterministic).
+// Up to 8 rows run on CUDA cores (gemv_kernel), streaming the weights once.
 //
 // Epilogues (fused):
 //   F16      y = fp16(acc)
@@ -34,6 +22,7 @@
 //            goes to a partials array, reduced by argmax_finish (argmax.comp)
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -44,9 +33,6 @@ namespace spock {
 
 namespace {
 
-constexpr int kMaxStages = 12;
-constexpr int kMaxCluster = 8;  // portable thread-block cluster size
-constexpr int kRingBytes = 4 * (128 * 128 + 256 * 128);  // 192 KB: the ring never exceeds it
 constexpr uint32_t kWaitLimit = 1u << 25;
 
 __device__ __forceinline__ bool wait_spin(uint64_t* bar, uint32_t parity) {
@@ -65,69 +51,199 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Thread-block cluster helpers (distributed shared memory, no TMA).
+// Barrier across the CTAs of a thread-block cluster (release / acquire).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, int rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
+// ---- batched rows (> kGemvMaxB): persistent tcgen05 GEMM --------------------
+// A unit is one 128-row weight tile x one block of bn activation rows (the MMA
+// N), optionally one of `split` K ranges. Roles per CTA (384 threads):
+//   warp 0      TMA producer: weight tile [128][64] and activation block
+//               [bn][64] per ring stage (128B swizzle, no multicast)
+//   warp 1      MMA issuer: 4 x K16 tcgen05.mma per stage into a TMEM
+//               accumulator; two accumulators alternate between units, so
+//               one unit's epilogue runs under the next unit's MMAs
+//   warp 2      TMEM allocation
+//   warps 4-11  epilogue: two warpgroups (columns interleaved in 32-wide
+//               chunks), each warp reading its 32 TMEM lanes (weight rows)
+// Without a K split the grid is min(units, SMs) and each CTA walks units
+// blockIdx.x, blockIdx.x + gridDim.x, ... With a split each CTA owns exactly
+// one (unit, K range); the ranks of a unit form one thread-block cluster
+// (co-scheduled, so they can wait on each other), park their fp32 partial
+// chunks in an L2-resident workspace, and after a cluster barrier each
+// chunk's owner adds the ranks' partials in rank order (deterministic) and
+// runs the epilogue for it.
+constexpr int kTcEpiWarps = 8;
+constexpr int kTcThreads = 128 + 32 * kTcEpiWarps;
+constexpr int kTcMaxStages = 8;
+constexpr int kTcRing = 196608;      // 4 stages at bn = 256, more at narrower bn
+constexpr int kStgHalves = 32 * 34;  // per-warp 32 x 32 transpose tile (ARGMAX rows padded to 34)
+constexpr int kTcSmem = 1024 + kTcRing + kTcEpiWarps * kStgHalves * 2 + 2 * 4 * 32 * 8 + (2 * kTcMaxStages + 8) * 8;
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-// kKB: 64-wide k blocks per ring stage. Each stage round (TMA, MMA, commit,
-// hand-off) has a fixed cost, so long unsplit K loops at prefill row counts
-// take two blocks per stage; short decode loops keep one (more CTAs per SM).
-template <int kEpi, int kKB>
-__global__ void __launch_bounds__(128, 1)
-    gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
-                       GemmArgs a) {
+// One 32 x 32 chunk of a unit's accumulator: v[k] = acc[weight row
+// tile*128 + wq*32 + lane][activation row col0 + k]. Transposed through the
+// warp's staging tile so global stores are 16-byte row segments.
+template <int kEpi>
+__device__ __forceinline__ void tc_store_chunk(const GemmArgs& a, const float (&v)[32], __half* stg, int tile,
+                                               int col0, int ncol, int wq, int lane, int half, bool ok,
+                                               float* amx_v, int* amx_i) {
+  if constexpr (kEpi == EPI_ARGMAX) {
+    const int row = tile * 128 + wq * 32 + lane;
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      stg[k * 34 + lane] = row < a.n_out ? __float2half_rn(v[k]) : __ushort_as_half(0xfc00);
+    __syncwarp();
+    // lane = activation row: the warp's 32 weight rows in order ('>' keeps the lowest index)
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+      const float f = __half2float(stg[lane * 34 + j]);
+      if (f > bv) {
+        bv = f;
+        bi = tile * 128 + wq * 32 + j;
+      }
+    }
+    amx_v[(half * 4 + wq) * 32 + lane] = bv;
+    amx_i[(half * 4 + wq) * 32 + lane] = bi;
+    named_sync(1 + half, 128);
+    if (wq == 0) {  // the tile's four 32-row parts in row order
+      for (int q = 1; q < 4; ++q) {
+        const float ov = amx_v[(half * 4 + q) * 32 + lane];
+        if (ov > bv) {
+          bv = ov;
+          bi = amx_i[(half * 4 + q) * 32 + lane];
+        }
+      }
+      const int b = col0 + lane;
+      if (ok && lane < ncol && b < a.batch) {
+        a.amax_val[(size_t)tile * a.batch + b] = bv;
+        a.amax_idx[(size_t)tile * a.batch + b] = bi;
+      }
+    }
+    named_sync(1 + half, 128);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) stg[k * 32 + lane] = __float2half_rn(v[k]);
+    __syncwarp();
+    if constexpr (kEpi == EPI_SWIGLU) {
+      // weight rows 32wq..32wq+31 of the tile are [gate 16 | up 16]: outputs
+      // tile*64 + 16wq + 0..15; two 8-output segments per activation row
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int item = lane + 32 * j, k = item >> 1, s = item & 1, b = col0 + k;
+        const int out = tile * 64 + wq * 16 + 8 * s;
+        if (!(ok && k < ncol && b < a.batch && out < a.n_out / 2)) continue;
+        const uint4 gq = *reinterpret_cast<const uint4*>(stg + k * 32 + 8 * s);
+        const uint4 uq = *reinterpret_cast<const uint4*>(stg + k * 32 + 16 + 8 * s);
+        const __half* gh = reinterpret_cast<const __half*>(&gq);
+        const __half* uh = reinterpret_cast<const __half*>(&uq);
+        uint4 val;
+        __half* o = reinterpret_cast<__half*>(&val);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float g = __half2float(gh[e]), u = __half2float(uh[e]);
+          o[e] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * u);
+        }
+        *reinterpret_cast<uint4*>(a.y + (size_t)b * a.ldy + out) = val;
+      }
+    } else {
+      // four 8-output segments per activation row: 128 segments, 4 per lane
+      uint4 rv[4];
+      if constexpr (kEpi == EPI_RESIDUAL) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int item = lane + 32 * j, k = item >> 2, s = item & 3, b = col0 + k;
+          const int out = tile * 128 + wq * 32 + 8 * s;
+          if (ok && k < ncol && b < a.batch && out < a.n_out)
+            rv[j] = *reinterpret_cast<const uint4*>(a.res + (size_t)b * a.ldy + out);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int item = lane + 32 * j, k = item >> 2, s = item & 3, b = col0 + k;
+        const int out = tile * 128 + wq * 32 + 8 * s;
+        if (!(ok && k < ncol && b < a.batch && out < a.n_out)) continue;
+        uint4 val = *reinterpret_cast<const uint4*>(stg + k * 32 + 8 * s);
+        if constexpr (kEpi == EPI_RESIDUAL) {
+          __half2* pv = reinterpret_cast<__half2*>(&val);
+          const __half2* pr = reinterpret_cast<const __half2*>(&rv[j]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 x = __half22float2(pv[e]), y = __half22float2(pr[e]);
+            pv[e] = __floats2half2_rn(x.x + y.x, x.y + y.y);
+          }
+        }
+        *reinterpret_cast<uint4*>(a.y + (size_t)b * a.ldy + out) = val;
+      }
+    }
+    __syncwarp();  // the staging tile is rewritten by the next chunk
+  }
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
-  const int a_bytes = 128 * 128, b_bytes = a.bn * 128, sub_bytes = a_bytes + b_bytes, stage_bytes = kKB * sub_bytes;
-  const int kStages = a.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * stage_bytes);
-  uint64_t* empty = full + kMaxStages;
-  uint64_t* done = empty + kMaxStages;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(done + 1);
-  int* s_last = reinterpret_cast<int*>(s_tmem + 1);
+  const int bn = a.bn, S = a.nsplit, nst = a.stages;
+  const int stage_bytes = 16384 + bn * 128;
+  __half* stg_all = reinterpret_cast<__half*>(sm + kTcRing);
+  float* amx_v = reinterpret_cast<float*>(sm + kTcRing + kTcEpiWarps * kStgHalves * 2);
+  int* amx_i = reinterpret_cast<int*>(amx_v + 2 * 4 * 32);
+  uint64_t* full = reinterpret_cast<uint64_t*>(amx_i + 2 * 4 * 32);
+  uint64_t* empty = full + kTcMaxStages;
+  uint64_t* accf = empty + kTcMaxStages;  // [2] MMA -> epilogue
+  uint64_t* acce = accf + 2;              // [2] epilogue -> MMA
+  uint64_t* drain = acce + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int tile = blockIdx.x, split = blockIdx.y, n0 = blockIdx.z * a.bn;
-  const int kb0 = split * a.kb_per_split;
+  const int nb = (a.bpad + bn - 1) / bn;
+  const int units = ((a.n_out + 127) / 128) * nb;
+  const int rank = S > 1 ? (int)(blockIdx.x % S) : 0;
+  const int u0 = S > 1 ? (int)(blockIdx.x / S) : (int)blockIdx.x;
+  const int ustep = S > 1 ? units : (int)gridDim.x;  // split: one unit per CTA
+  const int kb0 = rank * a.kb_per_split;
   const int nkb = min(a.kb_per_split, a.k / 64 - kb0);
-  const int nst = (nkb + kKB - 1) / kKB;  // ring stages of this CTA
-  auto subs = [&](int i) { return min(kKB, nkb - i * kKB); };
-  uint32_t ncols = 32;
-  while ((int)ncols < a.bn) ncols <<= 1;
+  uint32_t bnp = 32;
+  while ((int)bnp < bn) bnp <<= 1;
+  const int nch = (bn + 31) / 32;
+  int pre = 0;
 
-  const int pre = nst < kStages ? nst : kStages;
   if (t == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < nst; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
-    tc::mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&accf[b], 1);
+      tc::mbar_init(&acce[b], kTcEpiWarps);
+    }
+    tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmw);
     tc::prefetch_tmap(&tmx);
-    // The weights do not depend on the previous kernel or on TMEM: the first
-    // stages' weight tiles stream while the TMEM allocation (which may wait
-    // for the previous kernel's CTA on this SM) and its dependency drain.
-    for (int i = 0; i < pre; ++i) {
-      tc::mbar_arrive_expect_tx(&full[i], subs(i) * sub_bytes);
-      for (int j = 0; j < subs(i); ++j)
-        tma_load_2d(sm + i * stage_bytes + j * sub_bytes, &tmw, &full[i], (kb0 + i * kKB + j) * 64, tile * 128);
+    // The weights do not depend on the previous kernel: the first stages'
+    // weight tiles stream while the TMEM allocation and that kernel drain.
+    if (u0 < units) {
+      pre = nkb < nst ? nkb : nst;
+      for (int i = 0; i < pre; ++i) {
+        tc::mbar_arrive_expect_tx(&full[i], stage_bytes);
+        tma_load_2d(sm + i * stage_bytes, &tmw, &full[i], (kb0 + i) * 64, (u0 / nb) * 128);
+      }
     }
   }
   __syncwarp();
-  if (warp == 0) {
-    tc::tmem_alloc(s_tmem, ncols);
+  if (warp == 2) {
+    tc::tmem_alloc(s_tmem, 2 * bnp);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -135,259 +251,128 @@ __global__ void __launch_bounds__(128, 1)
   tc::tc_fence_after();
   const uint32_t tb = *s_tmem;
   bool ok = true;
+  int issued = 0;
 
-  if (warp == 0 && lane == 0) {  // TMA producer (the first stages' weights are in flight)
-    pdl_wait();
-    pdl_launch();
-    for (int i = 0; i < pre; ++i)
-      for (int j = 0; j < subs(i); ++j)
-        tma_load_2d(sm + i * stage_bytes + j * sub_bytes + a_bytes, &tmx, &full[i], (kb0 + i * kKB + j) * 64, n0);
-    for (int i = pre; i < nst && ok; ++i) {
-      const int s = i % kStages;
-      ok = wait_spin(&empty[s], ((i / kStages) - 1) & 1);
-      if (!ok) break;
-      uint8_t* st = sm + s * stage_bytes;
-      tc::mbar_arrive_expect_tx(&full[s], subs(i) * sub_bytes);
-      for (int j = 0; j < subs(i); ++j) {
-        tma_load_2d(st + j * sub_bytes, &tmw, &full[s], (kb0 + i * kKB + j) * 64, tile * 128);
-        tma_load_2d(st + j * sub_bytes + a_bytes, &tmx, &full[s], (kb0 + i * kKB + j) * 64, n0);
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      pdl_wait();
+      pdl_launch();
+      for (int u = u0; u < units && ok; u += ustep) {
+        const int tile = u / nb, rb = u % nb;
+        for (int j = 0; j < nkb; ++j, ++issued) {
+          const int s = issued % nst;
+          uint8_t* st = sm + s * stage_bytes;
+          if (issued < pre) {  // weight tile already in flight
+            tma_load_2d(st + 16384, &tmx, &full[s], (kb0 + j) * 64, rb * bn);
+            continue;
+          }
+          if (issued >= nst && !(ok = wait_spin(&empty[s], ((issued / nst) - 1) & 1))) break;
+          tc::mbar_arrive_expect_tx(&full[s], stage_bytes);
+          tma_load_2d(st, &tmw, &full[s], (kb0 + j) * 64, tile * 128);
+          tma_load_2d(st + 16384, &tmx, &full[s], (kb0 + j) * 64, rb * bn);
+        }
       }
     }
-  } else if (warp == 1 && lane == 0) {  // MMA issuer
-    const uint32_t idesc = tc::idesc_f16(128, a.bn, false, false);
-    const uint32_t sbase = tc::smem_u32(sm);
-    for (int i = 0; i < nst && ok; ++i) {
-      const int s = i % kStages;
-      ok = wait_spin(&full[s], (i / kStages) & 1);
-      if (!ok) break;
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      const uint32_t idesc = tc::idesc_f16(128, bn, false, false);
+      const uint32_t sbase = tc::smem_u32(sm);
+      int it = 0, i = 0;
+      for (int u = u0; u < units && ok; u += ustep, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !(ok = wait_spin(&acce[b], ((i >> 1) - 1) & 1))) break;
+        tc::tc_fence_after();
+        const uint32_t d = tb + b * bnp;
+        for (int j = 0; j < nkb; ++j, ++it) {
+          const int s = it % nst;
+          if (!(ok = wait_spin(&full[s], (it / nst) & 1))) break;
+          tc::tc_fence_after();
+          const uint32_t st = sbase + s * stage_bytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc::mma_f16(d, tc::sdesc(st + kk * 32, 16, 1024), tc::sdesc(st + 16384 + kk * 32, 16, 1024), idesc,
+                        (j | kk) ? 1u : 0u);
+          tc::mma_commit(&empty[s]);
+        }
+        if (ok) tc::mma_commit(&accf[b]);
+      }
+      tc::mma_commit(drain);  // every MMA of this thread has finished before TMEM is freed
+      if (!wait_spin(drain, 0)) ok = false;
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // Epilogue. After a timeout a warp keeps the same control flow (the
+    // ARGMAX combine synchronises the four warps of a warpgroup) but stops
+    // waiting and writes nothing.
+    const int ew = warp - 4, wq = warp & 3, half = ew >> 2;
+    __half* stg = stg_all + ew * kStgHalves;
+    pdl_wait();  // reads and writes what earlier kernels use
+    int i = 0;
+    for (int u = u0; u < units; u += ustep, ++i) {
+      const int tile = u / nb, rb = u % nb, b = i & 1;
+      if (ok) ok = wait_spin(&accf[b], (i >> 1) & 1);
       tc::tc_fence_after();
-      for (int j = 0; j < subs(i); ++j) {
-        const uint32_t st = sbase + s * stage_bytes + j * sub_bytes;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_f16(tb, tc::sdesc(st + kk * 32, 16, 1024), tc::sdesc(st + a_bytes + kk * 32, 16, 1024), idesc,
-                      (i > 0 || j > 0 || kk > 0) ? 1u : 0u);
-      }
-      tc::mma_commit(&empty[s]);
-    }
-    tc::mma_commit(done);
-  }
-  __syncwarp();
-  pdl_wait();  // the epilogue reads and writes what earlier kernels use
-  if constexpr (kEpi == EPI_RESIDUAL) {
-    // pull this CTA's residual rows (2 x 128 B each) into L2 while the K loop runs
-    for (int j = t; j < 2 * a.bn; j += 128) {
-      const int b = n0 + (j >> 1), col = tile * 128 + (j & 1) * 64;
-      if (b < a.batch && col < a.n_out)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.res + (size_t)b * a.ldy + col));
-    }
-  }
-  // epilogue: all 128 threads; thread t <-> weight row tile*128 + t
-  if (!wait_spin(done, 0)) ok = false;
-  if (__syncthreads_or(!ok)) {
-    if (t == 0) atomicExch(a.err, 3);
-    if (a.csplit) {  // the cluster's two barriers stay matched; the leader's result is void
-      cluster_sync();
-      cluster_sync();
-    } else if (a.nsplit > 1) {
-      // Still take part in the tile's ticket, so it returns to zero; if this
-      // CTA is the last one, it clears the accumulator slice the others added
-      // to (the result is void either way, but the next launch starts clean).
-      __threadfence();
-      __syncthreads();
-      if (t == 0) {
-        int* ticket_p = a.tickets + tile * gridDim.z + blockIdx.z;
-        const int ticket = atomicAdd(ticket_p, 1);
-        *s_last = (ticket == a.nsplit - 1);
-        if (*s_last) *ticket_p = 0;
-      }
-      __syncthreads();
-      if (*s_last) {
-        float* wsp = a.ws + (size_t)(tile * 128 + t) * a.bpad + n0;
-        for (int c = 0; c < a.bn; ++c) __stcg(wsp + c, 0.f);
-      }
-    }
-    tc::tc_fence_before();
-    __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tb, ncols);
-    return;
-  }
-  tc::tc_fence_after();
-  const int row = tile * 128 + t;
-  const uint32_t taddr = tb + ((uint32_t)(warp * 32) << 16);
-
-  bool finisher = true;
-  // cluster split: ranks 1.. leave their fp32 partial [bn][128] in their own
-  // shared memory; rank 0 adds them to its accumulator in rank order
-  const float* part = reinterpret_cast<const float*>(sm);
-  if (a.csplit) {
-    if (blockIdx.y != 0) {
-      float* mine = reinterpret_cast<float*>(sm);
-      for (int c0 = 0; c0 < a.bn; c0 += 32) {
+      const uint32_t tq = tb + b * bnp + ((uint32_t)(wq * 32) << 16);
+      for (int c = half; c < nch; c += 2) {
+        if (S > 1 && c % S == rank) continue;  // this rank's own chunks wait for the others
         float v[32];
-        tc::tmem_ld32(taddr + c0, v);
+        tc::tmem_ld32(tq + c * 32, v);
+        if (S == 1) {
+          tc_store_chunk<kEpi>(a, v, stg, tile, rb * bn + c * 32, min(32, bn - c * 32), wq, lane, half, ok, amx_v,
+                               amx_i);
+        } else if (ok) {  // partial chunk -> workspace [unit][rank][chunk][32 cols][128 rows]
+          float* p = a.ws + (((size_t)u * S + rank) * nch + c) * 4096 + wq * 32 + lane;
 #pragma unroll
-        for (int k = 0; k < 32; ++k)
-          if (c0 + k < a.bn) mine[(c0 + k) * 128 + t] = v[k];
+          for (int k = 0; k < 32; ++k) __stcg(p + k * 128, v[k]);
+        }
       }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[b]);
     }
-    cluster_sync();
-    finisher = blockIdx.y == 0;
-  } else if (a.nsplit > 1) {
-    // partial tile -> accumulator [row][n0 + col] (vector atomics, resolved in L2)
-    float* wsp = a.ws + (size_t)row * a.bpad + n0;
-    for (int c0 = 0; c0 < a.bn; c0 += 32) {
-      float v[32];
-      tc::tmem_ld32(taddr + c0, v);
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (c0 + 4 * q < a.bn)
-          atomicAdd(reinterpret_cast<float4*>(wsp + c0) + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
-    }
-    __threadfence();
-    __syncthreads();
-    if (t == 0) {
-      int* ticket_p = a.tickets + tile * gridDim.z + blockIdx.z;
-      const int ticket = atomicAdd(ticket_p, 1);
-      *s_last = (ticket == a.nsplit - 1);
-      if (*s_last) *ticket_p = 0;  // ready for the next launch
-    }
-    __syncthreads();
-    finisher = *s_last != 0;
-    __threadfence();
   }
-
-  if (finisher) {
-    // the pipeline's stages are idle now: fp16 staging tile [bn][width]
-    __half* stg = reinterpret_cast<__half*>(sm);
-    constexpr int width = 128;  // staged weight rows (SWIGLU: gate and up, 64 outputs)
-    for (int c0 = 0; c0 < a.bn; c0 += 32) {
-      float v[32];
-      if (a.nsplit > 1 && !a.csplit) {
-        float4* p = reinterpret_cast<float4*>(a.ws + (size_t)row * a.bpad + n0 + c0);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (c0 + 4 * q < a.bn) {
-            const float4 x = __ldcg(p + q);
-            v[4 * q] = x.x;
-            v[4 * q + 1] = x.y;
-            v[4 * q + 2] = x.z;
-            v[4 * q + 3] = x.w;
-            __stcg(p + q, make_float4(0.f, 0.f, 0.f, 0.f));  // cleared for the next launch
+  // every role has left its loop (all waits are bounded)
+  __syncthreads();
+  if (S > 1) {
+    __threadfence();
+    cluster_sync();  // every rank's partials are in the workspace
+    tc::tc_fence_after();
+    if (warp >= 4 && u0 < units) {
+      const int ew = warp - 4, wq = warp & 3, half = ew >> 2;
+      const int tile = u0 / nb, rb = u0 % nb;
+      const uint32_t tq = tb + ((uint32_t)(wq * 32) << 16);
+      for (int c = half; c < nch; c += 2) {
+        if (c % S != rank) continue;
+        float acc[32];
+        for (int q = 0; q < S; ++q) {
+          float p[32];
+          if (q == rank) {
+            tc::tmem_ld32(tq + c * 32, p);
           } else {
-            v[4 * q] = v[4 * q + 1] = v[4 * q + 2] = v[4 * q + 3] = 0.f;
+            const float* src = a.ws + (((size_t)u0 * S + q) * nch + c) * 4096 + wq * 32 + lane;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) p[k] = __ldcg(src + k * 128);
           }
+#pragma unroll
+          for (int k = 0; k < 32; ++k) acc[k] = q == 0 ? p[k] : acc[k] + p[k];
         }
-      } else {
-        tc::tmem_ld32(taddr + c0, v);
-        if (a.csplit) {
-          for (int r = 1; r < a.nsplit; ++r) {
-            const uint32_t base = map_rank(tc::smem_u32(part), r);
-            float pv[32];
-#pragma unroll
-            for (int k = 0; k < 32; ++k) pv[k] = c0 + k < a.bn ? ld_cluster_f32(base + ((c0 + k) * 128 + t) * 4) : 0.f;
-#pragma unroll
-            for (int k = 0; k < 32; ++k) v[k] += pv[k];
-          }
-        }
-      }
-      if constexpr (kEpi == EPI_F16 || kEpi == EPI_RESIDUAL || kEpi == EPI_SWIGLU) {
-        // SWIGLU stages fp16(gate) and fp16(up) rows; the store loop pairs them
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-          if (c0 + k < a.bn) stg[(c0 + k) * width + t] = __float2half_rn(v[k]);
-      } else {  // EPI_ARGMAX: fp16 logits staged; rows past n_out as -inf
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-          if (c0 + k < a.bn) stg[(c0 + k) * width + t] = row < a.n_out ? __float2half_rn(v[k]) : __ushort_as_half(0xfc00);
-      }
-    }
-    __syncthreads();
-    if constexpr (kEpi == EPI_ARGMAX) {
-      // per batch column: max over the tile's 128 rows in row order ('>' keeps the lowest index)
-      for (int bl = t; bl < a.bn; bl += 128) {
-        const int b = n0 + bl;
-        if (b >= a.batch) continue;
-        const uint4* col = reinterpret_cast<const uint4*>(stg + bl * width);
-        float val = -INFINITY;
-        int idx = 0x7fffffff;
-        for (int c = 0; c < width / 8; ++c) {
-          const uint4 u = col[c];
-          const __half* hv = reinterpret_cast<const __half*>(&u);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float f = __half2float(hv[e]);
-            if (f > val) {
-              val = f;
-              idx = tile * 128 + 8 * c + e;
-            }
-          }
-        }
-        a.amax_val[(size_t)tile * a.batch + b] = val;
-        a.amax_idx[(size_t)tile * a.batch + b] = idx;
-      }
-    } else {
-      // 16-byte segments: batch row bl, outputs out0 + 8c .. out0 + 8c + 7
-      constexpr int outs = kEpi == EPI_SWIGLU ? 64 : 128;  // outputs of this tile
-      const int out0 = tile * outs;
-      const int n_valid = (kEpi == EPI_SWIGLU ? a.n_out / 2 : a.n_out) - out0;
-      constexpr int segs = outs / 8;
-      // kU segments per thread per round: the residual loads of a round are all
-      // in flight before the first add (one dependent load per segment was the
-      // epilogue's critical path)
-      constexpr int kU = 4;
-      const int total = a.bn * segs;
-      for (int i0 = t; i0 < total; i0 += 128 * kU) {
-        uint4 rv[kU];
-        if constexpr (kEpi == EPI_RESIDUAL) {
-#pragma unroll
-          for (int u = 0; u < kU; ++u) {
-            const int i = i0 + u * 128, bl = i / segs, c = i % segs, b = n0 + bl;
-            if (i < total && b < a.batch && 8 * c < n_valid)
-              rv[u] = *reinterpret_cast<const uint4*>(a.res + (size_t)b * a.ldy + out0 + 8 * c);
-          }
-        }
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int i = i0 + u * 128, bl = i / segs, c = i % segs, b = n0 + bl;
-        if (i >= total || b >= a.batch || 8 * c >= n_valid) continue;
-        uint4 val;
-        if constexpr (kEpi == EPI_SWIGLU) {
-          // outputs 8c..8c+7 of the tile: weight rows [gate 16 | up 16] groups of 32
-          const int f = 8 * c, base = (f >> 4) * 32 + (f & 15);
-          const uint4 gq = *reinterpret_cast<const uint4*>(stg + bl * width + base);
-          const uint4 uq = *reinterpret_cast<const uint4*>(stg + bl * width + base + 16);
-          const __half* gh = reinterpret_cast<const __half*>(&gq);
-          const __half* uh = reinterpret_cast<const __half*>(&uq);
-          __half* o = reinterpret_cast<__half*>(&val);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float g16 = __half2float(gh[e]), u16 = __half2float(uh[e]);
-            const float silu = __fdiv_rn(g16, __fadd_rn(1.0f, expf(-g16)));
-            o[e] = __float2half_rn(__fmul_rn(silu, u16));
-          }
-        } else {
-          val = *reinterpret_cast<const uint4*>(stg + bl * width + 8 * c);
-        }
-        const size_t off = (size_t)b * a.ldy + out0 + 8 * c;
-        if constexpr (kEpi == EPI_RESIDUAL) {
-          __half2* pv = reinterpret_cast<__half2*>(&val);
-          const __half2* pr = reinterpret_cast<const __half2*>(&rv[u]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 x = __half22float2(pv[e]), y = __half22float2(pr[e]);
-            pv[e] = __floats2half2_rn(x.x + y.x, x.y + y.y);
-          }
-        }
-        *reinterpret_cast<uint4*>(a.y + off) = val;
-      }
+        tc_store_chunk<kEpi>(a, acc, stg_all + ew * kStgHalves, tile, rb * bn + c * 32, min(32, bn - c * 32), wq,
+                             lane, half, ok, amx_v, amx_i);
       }
     }
   }
-  if (a.csplit) cluster_sync();  // partials stay in place until the leader has read them
+  if (warp == 0) {
+    // loads still in flight (a timeout elsewhere) land before the CTA exits
+    if (lane == 0)
+      for (int q = issued > nst ? issued - nst : 0; q < issued; ++q)
+        if (!wait_spin(&full[q % nst], (q / nst) & 1)) ok = false;
+    __syncwarp();
+  }
+  if (!ok) atomicExch(a.err, 3);
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tb, ncols);
+  if (warp == 2) tc::tmem_dealloc(tb, 2 * bnp);
 }
 
 // ---- small batches (<= kGemvMaxB rows): CUDA-core weight streaming ---------
@@ -652,17 +637,57 @@ Status map2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int b
   return Status::ok();
 }
 
+// Clusters of `split` CTAs of gemm_tc_kernel<epi> that fit on the device at
+// once (cluster shapes do not tile every GPC exactly), queried once per shape.
+int max_clusters(int epi, int split) {
+  static std::mutex mu;
+  static int cache[4][9];
+  static bool init = false;
+  std::lock_guard<std::mutex> g(mu);
+  if (!init) {
+    for (auto& r : cache)
+      for (int& c : r) c = -1;
+    init = true;
+  }
+  int& c = cache[epi & 3][split];
+  if (c >= 0) return c;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(split);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  cudaError_t e = cudaErrorInvalidValue;
+  switch (epi) {
+    case EPI_F16: e = cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EPI_F16>, &cfg); break;
+    case EPI_RESIDUAL: e = cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EPI_RESIDUAL>, &cfg); break;
+    case EPI_SWIGLU: e = cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EPI_SWIGLU>, &cfg); break;
+    default: e = cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<EPI_ARGMAX>, &cfg); break;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;  // no split rather than a guess
+  }
+  return c = n;
+}
+
 }  // namespace
 
-// x: [bpad][k] fp16 (rows >= batch may hold anything; a prefill's row count,
-// bpad > 256, is one launch of 256-row or smaller blocks), W: [n_out][k] fp16.
-// Workspace needs nsplit * ceil(n_out/128) * 128 * bpad floats when nsplit > 1,
-// tickets ceil(n_out/128) ints (zero), ARGMAX partials ceil(n_out/128) * batch.
+// x: [bpad][k] fp16 (rows >= batch may hold anything; any row count is one
+// launch of 256-row or smaller blocks), W: [n_out][k] fp16. A K split uses
+// the workspace (a.ws, a.ws_bytes) only when it fits: units * split * 128 *
+// round_up(bn, 32) floats. ARGMAX partials: ceil(n_out/128) * batch.
 Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, cudaStream_t st) {
   if (a.k % 64 || a.bpad % 16 || a.bpad < 16 || a.batch > a.bpad || a.batch < 1)
     return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: k % 64, bpad a multiple of 16, batch <= bpad");
-  if (a.bpad > 256 && a.nsplit > kMaxCluster)
-    return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: bpad > 256 allows at most 8 K splits");
+  if (a.nsplit > 8 || (a.bn && (a.bn % 16 || a.bn > 256)))
+    return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: at most 8 K splits, bn a multiple of 16 up to 256");
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15))
     return Status::err(SPOCK_ERR_INVALID, "gemm: operands must be 16-byte aligned");
   if (epi != EPI_ARGMAX) {
@@ -719,69 +744,62 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     return Status::ok();
   }
   if (a.norm_w) return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: fused RMSNorm only on the small-batch path");
-  // batch blocks first (no partial sums), down to 32 rows. Prefill row counts
-  // (bpad > 256) start from 256-row blocks: one launch covers every row, and
-  // the weight slab of a tile is re-read by its row blocks from L2.
-  const bool fixed_bn = a.bn >= 16 && a.bn <= 256 && a.bn % 16 == 0;  // caller's choice (tuning)
-  if (!fixed_bn) a.bn = a.bpad > 256 ? 256 : a.bpad;
-  int nb = (a.bpad + a.bn - 1) / a.bn;
-  while (!fixed_bn && ntiles * nb < sms && a.bn % 32 == 0 && a.bn / 2 >= 32) {
-    a.bn /= 2;
-    nb = (a.bpad + a.bn - 1) / a.bn;
-  }
-  if (nb > 65535) return Status::err(SPOCK_ERR_UNSUPPORTED, "gemm: too many row blocks");
-  CUtensorMap mw, mx;
-  Status s = map2d(&mw, w, a.n_out, a.k, 128);
-  if (s.code) return s;
-  s = map2d(&mx, x, a.bpad, a.k, a.bn);
-  if (s.code) return s;
-  if (a.nsplit < 1 && nb > 1) {
-    // blocked batch: split K only to fill the SMs (a CTA streams one weight
-    // slab at a bounded rate), in clusters that reduce on chip
-    const int want = (sms + ntiles * nb - 1) / (ntiles * nb);
-    a.nsplit = want < kMaxCluster ? want : kMaxCluster;
-    if (a.nsplit > kbs / 2) a.nsplit = kbs / 2 > 1 ? kbs / 2 : 1;
-  }
-  if (a.nsplit < 1) {  // enough CTAs to stream the weights from every SM ...
-    int want = (sms + ntiles * nb - 1) / (ntiles * nb);
-    // ... but no more partial-tile traffic (128 x bn fp32) than weight traffic
-    const int cap = a.k / (2 * a.bn);
-    want = want > cap ? cap : want;
-    want = want < 1 ? 1 : want;
-    a.nsplit = want > kbs ? kbs : want;
-  }
-  a.kb_per_split = (kbs + a.nsplit - 1) / a.nsplit;
-  a.nsplit = (kbs + a.kb_per_split - 1) / a.kb_per_split;
-  // up to 8 splits reduce inside a cluster (deterministic, no workspace);
-  // more go through the atomic workspace
-  a.csplit = a.nsplit > 1 && a.nsplit <= kMaxCluster;
-  if (a.nsplit > 1 && !a.csplit && (!a.ws || !a.tickets))
-    return Status::err(SPOCK_ERR_INVALID, "gemm: split-K needs a workspace");
-  // Four stages by default: deeper rings cost CTAs per SM, which these short K loops need more.
-  // Unsplit prefill row counts take two k blocks per stage (kKB = 2).
-  const int kb_stage = a.bpad > 256 && a.nsplit == 1 ? 2 : 1;
-  const int stage_bytes = kb_stage * (128 * 128 + a.bn * 128);
-  if (a.stages < 1) a.stages = 4;
-  if (a.stages > kMaxStages) a.stages = kMaxStages;
-  while (a.stages > 2 && a.stages * stage_bytes > kRingBytes) --a.stages;
-  const int smem = a.stages * stage_bytes + 2 * kMaxStages * 8 + 64 + 8 * 256 * 4 + 1024;
-  dim3 grid(ntiles, a.nsplit, nb);
   {
     static std::once_flag once;
     static Status prep;
     std::call_once(once, [] { prep = gemm_prepare(); });
     if (prep.code) return prep;
   }
-#define SPOCK_GEMM_CASE(E)                                                                               \
-  case E: {                                                                                              \
-    if (a.csplit)                                                                                        \
-      launch_k_cluster(gemm_swapab_kernel<E, 1>, grid, dim3(128), dim3(1, a.nsplit, 1), smem, st, mw, mx, a); \
-    else if (kb_stage == 2)                                                                              \
-      launch_k(gemm_swapab_kernel<E, 2>, grid, dim3(128), smem, st, mw, mx, a);                          \
-    else                                                                                                 \
-      launch_k(gemm_swapab_kernel<E, 1>, grid, dim3(128), smem, st, mw, mx, a);                          \
-    break;                                                                                               \
+  // Plan (bn, split), in microseconds measured on B200: a 64-wide K block
+  // costs a CTA ~0.37 us (0.41 at bn = 256) whatever bn is, so wide units
+  // pay; units beyond one per SM queue on a CTA (their epilogues overlap);
+  // a split adds its partial traffic (~70 GB/s per SM) and needs all its
+  // clusters resident at once.
+  const size_t ws_floats = a.ws ? a.ws_bytes / 4 : 0;
+  int best_bn = 0, best_split = 1;
+  double best = 1e30;
+  for (int bn : {256, 128, 64, 32, 16, a.bpad}) {
+    if (bn > 256 || bn % 16 || bn > a.bpad) continue;
+    if (a.bn > 0 && bn != a.bn) continue;
+    const int nb = (a.bpad + bn - 1) / bn, units = ntiles * nb, nch = (bn + 31) / 32;
+    const double ckb = bn > 128 ? 0.41 : 0.37;
+    for (int split : {1, 2, 4, 8}) {
+      if (a.nsplit > 0 && split != a.nsplit) continue;
+      double cost;
+      if (split == 1) {
+        cost = (double)((units + sms - 1) / sms) * kbs * ckb;
+      } else {
+        const int per = (kbs + split - 1) / split;
+        if ((kbs + per - 1) / per != split || units > max_clusters(epi, split)) continue;
+        if ((size_t)units * split * nch * 4096 > ws_floats) continue;
+        cost = per * ckb + 2.0 * (split - 1) / split * nch * 16384 / 70e3;
+      }
+      if (cost < best - 1e-9) {
+        best = cost;
+        best_bn = bn;
+        best_split = split;
+      }
+    }
   }
+  if (!best_bn) return Status::err(SPOCK_ERR_INVALID, "gemm: no tile plan (workspace too small for the forced split)");
+  a.bn = best_bn;
+  a.nsplit = best_split;
+  a.kb_per_split = (kbs + a.nsplit - 1) / a.nsplit;
+  const int nb = (a.bpad + a.bn - 1) / a.bn, units = ntiles * nb;
+  a.stages = std::min(kTcMaxStages, kTcRing / (16384 + a.bn * 128));
+  CUtensorMap mw, mx;
+  Status s = map2d(&mw, w, a.n_out, a.k, 128);
+  if (s.code) return s;
+  s = map2d(&mx, x, a.bpad, a.k, a.bn);
+  if (s.code) return s;
+  const dim3 grid(a.nsplit > 1 ? units * a.nsplit : std::min(units, sms));
+  cudaError_t e = cudaSuccess;
+#define SPOCK_GEMM_CASE(E)                                                                                     \
+  case E:                                                                                                      \
+    e = a.nsplit > 1 ? launch_k_cluster(gemm_tc_kernel<E>, grid, dim3(kTcThreads), dim3(a.nsplit, 1, 1),       \
+                                        kTcSmem, st, mw, mx, a)                                                \
+                     : launch_k(gemm_tc_kernel<E>, grid, dim3(kTcThreads), kTcSmem, st, mw, mx, a);            \
+    break;
   switch (epi) {
     SPOCK_GEMM_CASE(EPI_F16)
     SPOCK_GEMM_CASE(EPI_RESIDUAL)
@@ -791,17 +809,16 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
       return Status::err(SPOCK_ERR_INVALID, "gemm: unknown epilogue");
   }
 #undef SPOCK_GEMM_CASE
-  SPOCK_LAUNCH_CHECK("gemm_swapab_kernel");
+  if (e != cudaSuccess) return cuda_status(e, "gemm_tc_kernel launch");
+  SPOCK_LAUNCH_CHECK("gemm_tc_kernel");
   return Status::ok();
 }
 
 // Sets every GEMM variant's shared-memory limit once (before any graph capture).
 Status gemm_prepare() {
-  const int smem = kRingBytes + 2 * kMaxStages * 8 + 64 + 8 * 256 * 4 + 1024;
   cudaError_t e = cudaSuccess;
-#define SPOCK_GEMM_ATTR(E)                                                                                      \
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<E, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_swapab_kernel<E, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+#define SPOCK_GEMM_ATTR(E) \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_tc_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   SPOCK_GEMM_ATTR(EPI_F16)
   SPOCK_GEMM_ATTR(EPI_RESIDUAL)
   SPOCK_GEMM_ATTR(EPI_SWIGLU)

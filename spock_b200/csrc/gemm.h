@@ -14,17 +14,15 @@ struct GemmArgs {
   int k;             // inner dim, multiple of 64
   int batch;         // real batch rows
   int bpad;          // padded batch rows of x, multiple of 16
-  int bn;            // batch rows per CTA (MMA N): 0 = launch_gemm chooses
+  int bn;            // activation rows per unit (MMA N, multiple of 16): 0 = launch_gemm chooses
   int kb_per_split;  // 64-wide k blocks per split; set by launch_gemm
-  int nsplit;        // K splits; 0 = let launch_gemm choose
-  int stages;        // TMA ring depth: 0 = launch_gemm chooses (4), capped by its 192 KB ring
-  int csplit;        // set by launch_gemm: the K splits of a tile form one thread-block
-                     // cluster and reduce their partials through distributed shared memory
+  int nsplit;        // K splits (1, 2, 4, 8); 0 = launch_gemm chooses
+  int stages;        // TMA ring depth; set by launch_gemm
   __half* y;         // [batch][ldy]; ldy % 8 == 0, 16-byte aligned
   int ldy;
   const __half* res;  // RESIDUAL: [batch][ldy]
-  float* ws;          // split accumulator [n_tiles*128][bpad], zero between launches
-  int* tickets;       // [n_tiles], zero before launch, left zero after
+  float* ws;          // K-split partials (L2-resident scratch, no state between launches)
+  size_t ws_bytes;
   float* amax_val;    // ARGMAX partials [n_tiles][batch]
   int* amax_idx;
   int* err;

@@ -116,11 +116,10 @@ struct spock_model {
   int bpad = 16, batch = 0;
   void *h = nullptr, *x = nullptr, *proj = nullptr, *mix = nullptr, *mlp = nullptr, *q = nullptr, *gate = nullptr;
   float *ws = nullptr;
-  size_t ws_bytes = 0, tickets_bytes = 0;
+  size_t ws_bytes = 0;
   // split decode attention (few rows): partials [rows][2][splits][1032] and tickets [rows][2]
   float* attn_ws = nullptr;
   int* attn_tickets = nullptr;
-  int* tickets = nullptr;
   float* amax_val = nullptr;
   int* amax_idx = nullptr;
   int *tok_in = nullptr, *tok_out = nullptr, *pos = nullptr;
@@ -196,7 +195,7 @@ Status gemm(spock_model* m, int epi, const void* x, const void* w, int n_out, in
   a.ldy = ldy;
   a.res = (const __half*)res;
   a.ws = m->ws;
-  a.tickets = m->tickets;
+  a.ws_bytes = m->ws_bytes;
   a.amax_val = m->amax_val;
   a.amax_idx = m->amax_idx;
   a.err = m->err_flag;
@@ -366,7 +365,7 @@ Status gemm_rows(spock_model* m, int epi, const void* x, const void* w, int n_ou
   a.ldy = ldy;
   a.res = (const __half*)res;
   a.ws = m->ws;
-  a.tickets = m->tickets;
+  a.ws_bytes = m->ws_bytes;
   a.amax_val = m->amax_val;
   a.amax_idx = m->amax_idx;
   a.err = m->err_flag;
@@ -569,11 +568,9 @@ __attribute__((visibility("default"))) int spock_model_create(spock_ctx* ctx, co
   A(&m->mlp, (size_t)B * INTER * 2);
   A(&m->q, (size_t)B * QH * HD * 2);
   A(&m->gate, (size_t)B * QH * HD * 2);
-  // split-K accumulator: one 128 x bpad fp32 tile per weight-row tile of the largest split GEMM
-  m->ws_bytes = (size_t)((2 * INTER + 127) / 128 + (DN_IN + 127) / 128) * 128 * B * 4;
-  m->tickets_bytes = (size_t)((d->vocab + 127) / 128 + 64) * 4;
+  // projection K-split partials: at most one 128 x 256 fp32 tile per SM
+  m->ws_bytes = (size_t)m->sms * 128 * 256 * 4;
   A(&m->ws, m->ws_bytes);
-  A(&m->tickets, m->tickets_bytes);
   A(&m->amax_val, (size_t)((d->vocab + 127) / 128) * B * 4);
   A(&m->amax_idx, (size_t)((d->vocab + 127) / 128) * B * 4);
   A(&m->tok_in, (size_t)B * 4);
@@ -825,10 +822,6 @@ __attribute__((visibility("default"))) int spock_model_reset(spock_model* m, int
   cudaMemset(m->conv_state, 0, (size_t)n_dn(m) * B * CONV * 4 * 2);
   cudaMemset(m->pos, 0, (size_t)B * 4);
   cudaMemset(m->kv, 0, (size_t)B * m->kv_seq_stride * 2);
-  // the projection split-K workspace and tickets: clean after any completed
-  // launch, but a launch whose bounded wait gave up may leave them dirty
-  cudaMemset(m->ws, 0, m->ws_bytes);
-  cudaMemset(m->tickets, 0, m->tickets_bytes);
   cudaMemset(m->attn_tickets, 0, (size_t)16 * 2 * 4);
   cudaError_t e = cudaDeviceSynchronize();
   return e == cudaSuccess ? SPOCK_OK : mfail(m, SPOCK_ERR_CUDA, cudaGetErrorString(e));

@@ -118,8 +118,7 @@ Status op_matvec(OpsScratch& sc, int epilogue, int exact, const void* w, int out
     if (cudaMemsetAsync(sc.xpad.buf, 0, (size_t)bpad * in_dim * 2, st) != cudaSuccess ||
         cudaMemcpyAsync(sc.xpad.buf, x, (size_t)rows * in_dim * 2, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return Status::err(SPOCK_ERR_CUDA, "spock_matvec: staging copy failed");
-    if ((s = grow(sc.ws, (size_t)ntiles * 128 * bpad * 4, true)).code) return s;
-    if ((s = grow(sc.tickets, (size_t)ntiles * 64 * 4, true)).code) return s;
+    if ((s = grow(sc.ws, (size_t)sms * 128 * 256 * 4, false)).code) return s;
     GemmArgs a{};
     a.n_out = n_rows;
     a.k = in_dim;
@@ -129,7 +128,7 @@ Status op_matvec(OpsScratch& sc, int epilogue, int exact, const void* w, int out
     a.ldy = ldy;
     a.res = (const __half*)res;
     a.ws = static_cast<float*>(sc.ws.buf);
-    a.tickets = static_cast<int*>(sc.tickets.buf);
+    a.ws_bytes = sc.ws.bytes;
     a.amax_val = av;
     a.amax_idx = ai;
     a.err = sc.err;

@@ -6,8 +6,7 @@
 namespace spock {
 struct OpsScratch {
   ChunkScratch xpad;     // fast projections: x zero-padded to a multiple of 16 rows
-  ChunkScratch ws;       // split-K accumulator (zero between launches)
-  ChunkScratch tickets;  // split-K tile tickets (zero between launches)
+  ChunkScratch ws;       // projection K-split partials
   ChunkScratch amax;     // argmax partials [tiles][rows] value + index
   ChunkScratch qg;       // attention: normalised / rotated q and the gate
   ChunkScratch rope;     // RoPE table [rope_seq][64]
@@ -17,7 +16,7 @@ struct OpsScratch {
   int rope_seq = 0;
   int* err = nullptr;    // the context's error word
   void release() {
-    for (ChunkScratch* s : {&xpad, &ws, &tickets, &amax, &qg, &rope, &attn_ws, &attn_tk}) s->release();
+    for (ChunkScratch* s : {&xpad, &ws, &amax, &qg, &rope, &attn_ws, &attn_tk}) s->release();
   }
 };
 
