@@ -43,14 +43,6 @@ __device__ __forceinline__ bool wait_spin(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          tc::smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
 // Barrier across the CTAs of a thread-block cluster (release / acquire).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -76,7 +68,8 @@ __device__ __forceinline__ void cluster_sync() {
 constexpr int kTcEpiWarps = 8;
 constexpr int kTcThreads = 128 + 32 * kTcEpiWarps;
 constexpr int kTcMaxStages = 8;
-constexpr int kTcRing = 196608;      // 4 stages at bn = 256, more at narrower bn
+constexpr int kTcKB = 2;             // 64-wide k blocks per ring stage
+constexpr int kTcRing = 196608;      // 2 stages at bn = 256, more at narrower bn
 constexpr int kStgHalves = 32 * 34;  // per-warp 32 x 32 transpose tile (ARGMAX rows padded to 34)
 constexpr int kTcSmem = 1024 + kTcRing + kTcEpiWarps * kStgHalves * 2 + 2 * 4 * 32 * 8 + (2 * kTcMaxStages + 8) * 8;
 
@@ -194,7 +187,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   const int bn = a.bn, S = a.nsplit, nst = a.stages;
-  const int stage_bytes = 16384 + bn * 128;
+  // A ring stage holds kTcKB k blocks: [W 128 x 64] x kTcKB then
+  // [x bn x 64] x kTcKB, one TMA box each. One barrier wait and one commit
+  // per stage (each costs the issuing thread about as much as a k block's
+  // MMAs at N <= 128, and each TMA issue about 200 cycles).
+  const int xoff = kTcKB * 16384, stage_bytes = kTcKB * (16384 + bn * 128);
   __half* stg_all = reinterpret_cast<__half*>(sm + kTcRing);
   float* amx_v = reinterpret_cast<float*>(sm + kTcRing + kTcEpiWarps * kStgHalves * 2);
   int* amx_i = reinterpret_cast<int*>(amx_v + 2 * 4 * 32);
@@ -213,6 +210,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int ustep = S > 1 ? units : (int)gridDim.x;  // split: one unit per CTA
   const int kb0 = rank * a.kb_per_split;
   const int nkb = min(a.kb_per_split, a.k / 64 - kb0);
+  const int nsg = (nkb + kTcKB - 1) / kTcKB;  // ring stages per unit
+  auto subs = [&](int js) { return min(kTcKB, nkb - js * kTcKB); };
   uint32_t bnp = 32;
   while ((int)bnp < bn) bnp <<= 1;
   const int nch = (bn + 31) / 32;
@@ -234,10 +233,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // The weights do not depend on the previous kernel: the first stages'
     // weight tiles stream while the TMEM allocation and that kernel drain.
     if (u0 < units) {
-      pre = nkb < nst ? nkb : nst;
-      for (int i = 0; i < pre; ++i) {
+      pre = nsg < nst ? nsg : nst;
+      for (int i = 0; i < pre; ++i) {  // boxes past K (or past a split's range) fill and count in full
         tc::mbar_arrive_expect_tx(&full[i], stage_bytes);
-        tma_load_2d(sm + i * stage_bytes, &tmw, &full[i], (kb0 + i) * 64, (u0 / nb) * 128);
+        tc::tma_load_3d(sm + i * stage_bytes, &tmw, &full[i], 0, (u0 / nb) * 128, kb0 + i * kTcKB);
       }
     }
   }
@@ -259,17 +258,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       pdl_launch();
       for (int u = u0; u < units && ok; u += ustep) {
         const int tile = u / nb, rb = u % nb;
-        for (int j = 0; j < nkb; ++j, ++issued) {
-          const int s = issued % nst;
+        for (int js = 0; js < nsg; ++js, ++issued) {
+          const int s = issued % nst, kb = kb0 + js * kTcKB;
           uint8_t* st = sm + s * stage_bytes;
-          if (issued < pre) {  // weight tile already in flight
-            tma_load_2d(st + 16384, &tmx, &full[s], (kb0 + j) * 64, rb * bn);
+          if (issued < pre) {  // weight tiles already in flight
+            tc::tma_load_3d(st + xoff, &tmx, &full[s], 0, rb * bn, kb);
             continue;
           }
           if (issued >= nst && !(ok = wait_spin(&empty[s], ((issued / nst) - 1) & 1))) break;
           tc::mbar_arrive_expect_tx(&full[s], stage_bytes);
-          tma_load_2d(st, &tmw, &full[s], (kb0 + j) * 64, tile * 128);
-          tma_load_2d(st + 16384, &tmx, &full[s], (kb0 + j) * 64, rb * bn);
+          tc::tma_load_3d(st, &tmw, &full[s], 0, tile * 128, kb);
+          tc::tma_load_3d(st + xoff, &tmx, &full[s], 0, rb * bn, kb);
         }
       }
     }
@@ -284,15 +283,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (i >= 2 && !(ok = wait_spin(&acce[b], ((i >> 1) - 1) & 1))) break;
         tc::tc_fence_after();
         const uint32_t d = tb + b * bnp;
-        for (int j = 0; j < nkb; ++j, ++it) {
-          const int s = it % nst;
+        for (int js = 0; js < nsg; ++js, ++it) {
+          const int s = it % nst, n = subs(js);
           if (!(ok = wait_spin(&full[s], (it / nst) & 1))) break;
           tc::tc_fence_after();
-          const uint32_t st = sbase + s * stage_bytes;
+          for (int q = 0; q < n; ++q) {
+            const uint32_t wa = sbase + s * stage_bytes + q * 16384, xa = sbase + s * stage_bytes + xoff + q * bn * 128;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc::mma_f16(d, tc::sdesc(st + kk * 32, 16, 1024), tc::sdesc(st + 16384 + kk * 32, 16, 1024), idesc,
-                        (j | kk) ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              tc::mma_f16(d, tc::sdesc(wa + kk * 32, 16, 1024), tc::sdesc(xa + kk * 32, 16, 1024), idesc,
+                          (js | q | kk) ? 1u : 0u);
+          }
           tc::mma_commit(&empty[s]);
         }
         if (ok) tc::mma_commit(&accf[b]);
@@ -333,7 +334,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   }
   // every role has left its loop (all waits are bounded)
-  __syncthreads();
+  const bool any_fail = __syncthreads_or(!ok);
   if (S > 1) {
     __threadfence();
     cluster_sync();  // every rank's partials are in the workspace
@@ -362,8 +363,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
-  if (warp == 0) {
-    // loads still in flight (a timeout elsewhere) land before the CTA exits
+  if (warp == 0 && any_fail) {
+    // loads still in flight (a timeout elsewhere) land before the CTA exits;
+    // without a failure the MMA issuer has consumed every stage
     if (lane == 0)
       for (int q = issued > nst ? issued - nst : 0; q < issued; ++q)
         if (!wait_spin(&full[q % nst], (q / nst) & 1)) ok = false;
@@ -623,14 +625,17 @@ EncodeTiledFn encode_fn2() {
   return fn;
 }
 
-Status map2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+// [rows][cols] fp16 viewed as [cols / 64][rows][64]: one box brings kTcKB
+// consecutive 64-wide k blocks of box_rows rows, each block a 128B-swizzled
+// [box_rows][64] tile (one TMA instruction per operand per ring stage).
+Status map_kb(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
   EncodeTiledFn fn = encode_fn2();
   if (!fn) return Status::err(SPOCK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)kTcKB};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return Status::err(SPOCK_ERR_CUDA, "cuTensorMapEncodeTiled failed (gemm)");
@@ -786,11 +791,11 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
   a.nsplit = best_split;
   a.kb_per_split = (kbs + a.nsplit - 1) / a.nsplit;
   const int nb = (a.bpad + a.bn - 1) / a.bn, units = ntiles * nb;
-  a.stages = std::min(kTcMaxStages, kTcRing / (16384 + a.bn * 128));
+  a.stages = std::min(kTcMaxStages, kTcRing / (kTcKB * (16384 + a.bn * 128)));
   CUtensorMap mw, mx;
-  Status s = map2d(&mw, w, a.n_out, a.k, 128);
+  Status s = map_kb(&mw, w, a.n_out, a.k, 128);
   if (s.code) return s;
-  s = map2d(&mx, x, a.bpad, a.k, a.bn);
+  s = map_kb(&mx, x, a.bpad, a.k, a.bn);
   if (s.code) return s;
   const dim3 grid(a.nsplit > 1 ? units * a.nsplit : std::min(units, sms));
   cudaError_t e = cudaSuccess;
