@@ -224,7 +224,7 @@ int spock_deltanet_recurrent(spock_ctx* ctx, int64_t batch, int32_t num_heads, i
 
 /* rms_norm.comp:31-70: y[r] = fp16(x[r] * 1/sqrt(mean(x[r]^2) + eps) * (1 + w)),
  * dim = 1024 (the hidden size; the only width the kernel implements). y may
- * alias x. */
+ * alias x; x, w and y are 8-byte aligned (SPOCK_ERR_INVALID otherwise). */
 int spock_rms_norm(spock_ctx* ctx, const void* x, const void* w, void* y, int64_t rows, int32_t dim, float eps,
                    void* stream);
 

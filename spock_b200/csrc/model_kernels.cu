@@ -32,84 +32,115 @@ __global__ void embed_kernel(const int* __restrict__ tokens, const uint4* __rest
   for (int i = threadIdx.x; i < HID / 8; i += blockDim.x) h[(size_t)b * (HID / 8) + i] = emb[(size_t)tok * (HID / 8) + i];
 }
 
-// One CTA (256 threads) per row.
+// One warp per row, 8 rows per 256-thread CTA. The shader's order is kept:
+// slot t (0..255) sums x[4t..4t+3]^2 in order, then a stride-128..1 tree over
+// the slots. Slot t = lane + 32 j lives in lane `lane`, so strides 128, 64
+// and 32 combine inside a lane and 16..1 go by shfl_down (bit-identical).
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__ x, const __half* __restrict__ w,
                                                       __half* __restrict__ y, float eps, int batch) {
-  const int b = blockIdx.x, t = threadIdx.x;
+  const int lane = threadIdx.x & 31, b = blockIdx.x * 8 + (threadIdx.x >> 5);
   pdl_wait();
   pdl_launch();
   if (b >= batch) return;
-  __shared__ float s[256];
-  const __half* xr = x + (size_t)b * HID;
-  float v[4], acc = 0.f;
+  const uint2* xr = reinterpret_cast<const uint2*>(x + (size_t)b * HID);
+  const uint2* wr = reinterpret_cast<const uint2*>(w);
+  float v[8][4], acc[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[i] = __half2float(xr[t * 4 + i]);
-    acc = __fadd_rn(acc, __fmul_rn(v[i], v[i]));
-  }
-  s[t] = acc;
-  __syncthreads();
-  for (int stride = 128; stride > 0; stride >>= 1) {
-    if (t < stride) s[t] = __fadd_rn(s[t], s[t + stride]);
-    __syncthreads();
-  }
-  const float nf = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s[0], (float)HID), eps)));
+  for (int j = 0; j < 8; ++j) {
+    const uint2 u = xr[lane + 32 * j];
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    const float2 f0 = __half22float2(h[0]), f1 = __half22float2(h[1]);
+    v[j][0] = f0.x;
+    v[j][1] = f0.y;
+    v[j][2] = f1.x;
+    v[j][3] = f1.y;
+    acc[j] = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float wv = __fadd_rn(1.0f, __half2float(w[t * 4 + i]));
-    y[(size_t)b * HID + t * 4 + i] = __float2half_rn(__fmul_rn(__fmul_rn(v[i], nf), wv));
+    for (int i = 0; i < 4; ++i) acc[j] = __fadd_rn(acc[j], __fmul_rn(v[j][i], v[j][i]));
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], acc[j + 4]);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) acc[j] = __fadd_rn(acc[j], acc[j + 2]);
+  acc[0] = __fadd_rn(acc[0], acc[1]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc[0] = __fadd_rn(acc[0], __shfl_down_sync(0xffffffffu, acc[0], o));
+  const float tot = __shfl_sync(0xffffffffu, acc[0], 0);
+  const float nf = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)HID), eps)));
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint2 wu = wr[lane + 32 * j];
+    const __half* wh = reinterpret_cast<const __half*>(&wu);
+    uint2 o;
+    __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      oh[i] = __float2half_rn(__fmul_rn(__fmul_rn(v[j][i], nf), __fadd_rn(1.0f, __half2float(wh[i]))));
+    reinterpret_cast<uint2*>(y + (size_t)b * HID)[lane + 32 * j] = o;
   }
 }
 
-// grid (rows, QH + KVH), 256 threads (thread d = head dimension d). Row r is
-// token r % T of sequence r / T (T = rows_per_seq: 1 in decode, the prompt
-// length in prefill), at position pos[seq] + r % T.
+// One warp per (row, head), 8 per 256-thread CTA: item = row * (QH + KVH) + head.
+// Row r is token r % T of sequence r / T (T = rows_per_seq: 1 in decode, the
+// prompt length in prefill), at position pos[seq] + r % T. Lane l holds head
+// dims d = l + 32 j; the per-head RMSNorm keeps rms_norm_per_head.comp's
+// one-element-per-slot stride-128..1 tree (strides 128..32 in-lane, 16..1 by
+// shuffle), and the RoPE pair (d, d + 32), d < 32, sits in one lane.
 // qkv: [rows][ld] with [q0 (256) | gate0 (256) | q1 | gate1 | ... | k (2x256) | v (2x256)].
 __global__ void __launch_bounds__(256)
     attn_prep_kernel(const __half* __restrict__ qkv, int ld, const __half* __restrict__ qn_w,
                      const __half* __restrict__ kn_w, const float* __restrict__ rope /*[max_seq][64] cos,sin*/,
                      const int* __restrict__ pos, __half* __restrict__ q_out /*[batch][QH][HD]*/,
                      __half* __restrict__ gate_out, __half* __restrict__ kv /*[batch][layers][max_seq][2][KVH][HD]*/,
-                     int64_t kv_seq_stride /*elements per sequence*/, int64_t kv_layer_off, float eps, int rows_per_seq) {
-  const int hh = blockIdx.y, b = blockIdx.x, d = threadIdx.x;  // b: row
-  const int seq = b / rows_per_seq;
+                     int64_t kv_seq_stride /*elements per sequence*/, int64_t kv_layer_off, float eps, int rows_per_seq,
+                     int rows) {
+  const int lane = threadIdx.x & 31, item = blockIdx.x * 8 + (threadIdx.x >> 5);
   pdl_wait();
   pdl_launch();
+  if (item >= rows * (QH + KVH)) return;
+  const int b = item / (QH + KVH), hh = item % (QH + KVH);
+  const int seq = b / rows_per_seq;
   const __half* row = qkv + (size_t)b * ld;
-  __shared__ float s[256];
-  __shared__ float sn[256];
   const bool is_q = hh < QH;
   const int kvh = hh - QH;
-  const float x = __half2float(is_q ? row[hh * 2 * HD + d] : row[QH * 2 * HD + kvh * HD + d]);
-  if (is_q) gate_out[((size_t)b * QH + hh) * HD + d] = row[hh * 2 * HD + HD + d];
-  // per-head RMSNorm (rms_norm_per_head.comp: one element per lane, stride-128..1 tree)
-  s[d] = __fmul_rn(x, x);
-  __syncthreads();
-  for (int stride = 128; stride > 0; stride >>= 1) {
-    if (d < stride) s[d] = __fadd_rn(s[d], s[d + stride]);
-    __syncthreads();
+  const __half* src = is_q ? row + hh * 2 * HD : row + QH * 2 * HD + kvh * HD;
+  const __half* nw = is_q ? qn_w : kn_w;
+  float x[8], s[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    x[j] = __half2float(src[lane + 32 * j]);
+    s[j] = __fmul_rn(x[j], x[j]);
   }
-  const float nf = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s[0], (float)HD), eps)));
-  const float wv = __fadd_rn(1.0f, __half2float(is_q ? qn_w[d] : kn_w[d]));
-  const float xn = __half2float(__float2half_rn(__fmul_rn(__fmul_rn(x, nf), wv)));
-  sn[d] = xn;
-  __syncthreads();
-  // partial RoPE: pairs (d, d+32) for d < 32 of the first 64 dims
-  float o = xn;
+  if (is_q)  // gate: 16-byte segments
+    reinterpret_cast<uint4*>(gate_out + ((size_t)b * QH + hh) * HD)[lane] =
+        reinterpret_cast<const uint4*>(row + hh * 2 * HD + HD)[lane];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) s[j] = __fadd_rn(s[j], s[j + 4]);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) s[j] = __fadd_rn(s[j], s[j + 2]);
+  s[0] = __fadd_rn(s[0], s[1]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s[0] = __fadd_rn(s[0], __shfl_down_sync(0xffffffffu, s[0], o));
+  const float tot = __shfl_sync(0xffffffffu, s[0], 0);
+  const float nf = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)HD), eps)));
+  float xn[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    xn[j] = __half2float(__float2half_rn(__fmul_rn(__fmul_rn(x[j], nf), __fadd_rn(1.0f, __half2float(nw[lane + 32 * j])))));
+  // partial RoPE on the first 64 dims: pair i = lane rotates (d = lane, d = lane + 32)
   const int p = pos[seq] + b % rows_per_seq;
-  if (d < ROT) {
-    const int i = d & 31;
-    const float c = rope[(size_t)p * ROT + 2 * i], sn_ = rope[(size_t)p * ROT + 2 * i + 1];
-    if (d < 32) o = __fsub_rn(__fmul_rn(xn, c), __fmul_rn(sn[d + 32], sn_));
-    else o = __fadd_rn(__fmul_rn(xn, c), __fmul_rn(sn[d - 32], sn_));
-  }
-  const __half oh = __float2half_rn(o);
-  if (is_q) {
-    q_out[((size_t)b * QH + hh) * HD + d] = oh;
-  } else {
-    __half* base = kv + (size_t)seq * kv_seq_stride + kv_layer_off + (size_t)p * (2 * KVH * HD);
-    base[kvh * HD + d] = oh;                                          // K
-    base[KVH * HD + kvh * HD + d] = row[QH * 2 * HD + KVH * HD + kvh * HD + d];  // V (no norm, no rope)
+  const float c = rope[(size_t)p * ROT + 2 * lane], sn = rope[(size_t)p * ROT + 2 * lane + 1];
+  const float r0 = __fsub_rn(__fmul_rn(xn[0], c), __fmul_rn(xn[1], sn));
+  const float r1 = __fadd_rn(__fmul_rn(xn[1], c), __fmul_rn(xn[0], sn));
+  xn[0] = r0;
+  xn[1] = r1;
+  __half* dst = is_q ? q_out + ((size_t)b * QH + hh) * HD
+                     : kv + (size_t)seq * kv_seq_stride + kv_layer_off + (size_t)p * (2 * KVH * HD) + kvh * HD;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) dst[lane + 32 * j] = __float2half_rn(xn[j]);
+  if (!is_q) {  // V (no norm, no rope), 16-byte segments
+    __half* vbase = kv + (size_t)seq * kv_seq_stride + kv_layer_off + (size_t)p * (2 * KVH * HD) + KVH * HD + kvh * HD;
+    reinterpret_cast<uint4*>(vbase)[lane] = reinterpret_cast<const uint4*>(row + QH * 2 * HD + KVH * HD + kvh * HD)[lane];
   }
 }
 
@@ -270,7 +301,8 @@ Status launch_embed(const int* tokens, const void* emb, void* h, int batch, cuda
 }
 
 Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batch, cudaStream_t st) {
-  launch_k(rmsnorm_kernel, dim3(batch), dim3(256), 0, st, (const __half*)x, (const __half*)w, (__half*)y, eps, batch);
+  launch_k(rmsnorm_kernel, dim3((batch + 7) / 8), dim3(256), 0, st, (const __half*)x, (const __half*)w, (__half*)y, eps,
+           batch);
   SPOCK_LAUNCH_CHECK("rmsnorm_kernel");
   return Status::ok();
 }
@@ -278,9 +310,9 @@ Status launch_rmsnorm(const void* x, const void* w, void* y, float eps, int batc
 Status launch_attn_prep(const void* qkv, int ld, const void* qn_w, const void* kn_w, const float* rope,
                         const int* pos, void* q_out, void* gate_out, void* kv, int64_t kv_seq_stride,
                         int64_t kv_layer_off, float eps, int rows, cudaStream_t st, int rows_per_seq) {
-  launch_k(attn_prep_kernel, dim3(rows, QH + KVH), dim3(256), 0, st, (const __half*)qkv, ld, (const __half*)qn_w,
-           (const __half*)kn_w, rope, pos, (__half*)q_out, (__half*)gate_out, (__half*)kv, kv_seq_stride,
-           kv_layer_off, eps, rows_per_seq);
+  launch_k(attn_prep_kernel, dim3((rows * (QH + KVH) + 7) / 8), dim3(256), 0, st, (const __half*)qkv, ld,
+           (const __half*)qn_w, (const __half*)kn_w, rope, pos, (__half*)q_out, (__half*)gate_out, (__half*)kv,
+           kv_seq_stride, kv_layer_off, eps, rows_per_seq, rows);
   SPOCK_LAUNCH_CHECK("attn_prep_kernel");
   return Status::ok();
 }

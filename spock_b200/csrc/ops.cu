@@ -78,6 +78,8 @@ Status grow(ChunkScratch& s, size_t bytes, bool zero) {
 Status op_rms_norm(const void* x, const void* w, void* y, int64_t rows, int dim, float eps, cudaStream_t st) {
   if (dim != 1024) return Status::err(SPOCK_ERR_UNSUPPORTED, "spock_rms_norm: the kernel implements dim 1024");
   if (rows > 0x7fffffff) return Status::err(SPOCK_ERR_INVALID, "spock_rms_norm: too many rows");
+  if (((uintptr_t)x | (uintptr_t)w | (uintptr_t)y) & 7)
+    return Status::err(SPOCK_ERR_INVALID, "spock_rms_norm: x, w and y must be 8-byte aligned");
   return launch_rmsnorm(x, w, y, eps, (int)rows, st);
 }
 

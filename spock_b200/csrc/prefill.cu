@@ -15,7 +15,6 @@ namespace {
 
 constexpr int kDim = 128;
 constexpr int kTokTile = 16;  // tokens per CTA of the conv kernel (many CTAs: each thread walks its tokens in order)
-constexpr int kTokGroup = 8;  // tokens per L2 barrier round
 
 // The shaders' stride-64..1 tree over s[0..127] by one warp (decode_step.cu).
 __device__ __forceinline__ float warp_tree128(const float* s, int lane) {
@@ -46,8 +45,8 @@ __global__ void __launch_bounds__(kDim)
   const int t0 = blockIdx.z * kTokTile, t1 = min(T, t0 + kTokTile);
   const int conv_dim = 3 * H * kDim;
   const int ch = blk * H * kDim + h * kDim + c;
-  __shared__ float sq[kTokGroup][kDim];
-  __shared__ float inv_s[kTokGroup];
+  __shared__ float sq[kTokTile][kDim];
+  __shared__ float inv_s[kTokTile];
   pdl_wait();
   pdl_launch();
   const __half* xrow = proj + (size_t)b * T * ld + ch;
@@ -62,45 +61,44 @@ __global__ void __launch_bounds__(kDim)
   auto xin = [&](int t) -> uint16_t {  // input of token t (t >= -4)
     return t >= 0 ? __half_as_ushort(xrow[(size_t)t * ld]) : sv[4 + t];
   };
+  // the tile's inputs, all loads in flight at once
+  uint16_t xs[kTokTile];
+#pragma unroll
+  for (int u = 0; u < kTokTile; ++u) xs[u] = t0 + u < t1 ? __half_as_ushort(xrow[(size_t)(t0 + u) * ld]) : 0;
   uint16_t s1 = xin(t0 - 3), s2 = xin(t0 - 2), s3 = xin(t0 - 1);
   __half* dst = (blk == 0 ? q_out : blk == 1 ? k_out : v_out) + (((size_t)b * H + h) * T) * kDim + c;
-  for (int tg = t0; tg < t1; tg += kTokGroup) {
-    float yf[kTokGroup];
+  float yf[kTokTile];
 #pragma unroll
-    for (int u = 0; u < kTokGroup; ++u) {
-      const int t = tg + u;
-      yf[u] = 0.f;
-      if (t < t1) {
-        const uint16_t x = xin(t);
-        float sum = 0.f;
-        sum = add_rn(sum, mul_rn(h2f(s1), w0));
-        sum = add_rn(sum, mul_rn(h2f(s2), w1));
-        sum = add_rn(sum, mul_rn(h2f(s3), w2));
-        sum = add_rn(sum, mul_rn(h2f(x), w3));
-        const float silu = __fdiv_rn(sum, add_rn(1.0f, expf(-sum)));
-        yf[u] = h2f(f2h(silu));
-        s1 = s2;
-        s2 = s3;
-        s3 = x;
-      }
-      if (blk < 2) sq[u][c] = mul_rn(yf[u], yf[u]);
+  for (int u = 0; u < kTokTile; ++u) {
+    yf[u] = 0.f;
+    if (t0 + u < t1) {
+      const uint16_t x = xs[u];
+      float sum = 0.f;
+      sum = add_rn(sum, mul_rn(h2f(s1), w0));
+      sum = add_rn(sum, mul_rn(h2f(s2), w1));
+      sum = add_rn(sum, mul_rn(h2f(s3), w2));
+      sum = add_rn(sum, mul_rn(h2f(x), w3));
+      const float silu = __fdiv_rn(sum, add_rn(1.0f, expf(-sum)));
+      yf[u] = h2f(f2h(silu));
+      s1 = s2;
+      s2 = s3;
+      s3 = x;
     }
-    if (blk < 2) {  // L2 of this head's q or k for each token of the group
-      __syncthreads();
-      const int warp = c >> 5, lane = c & 31;
-      for (int u = warp; u < kTokGroup; u += kDim / 32) {
-        const float tot = warp_tree128(sq[u], lane);
-        if (lane == 0) inv_s[u] = __fdiv_rn(1.0f, __fsqrt_rn(add_rn(tot, 1e-6f)));
-      }
-      __syncthreads();
+    if (blk < 2) sq[u][c] = mul_rn(yf[u], yf[u]);
+  }
+  if (blk < 2) {  // L2 of this head's q or k for each token of the tile
+    __syncthreads();
+    const int warp = c >> 5, lane = c & 31;
+    for (int u = warp; u < kTokTile; u += kDim / 32) {
+      const float tot = warp_tree128(sq[u], lane);
+      if (lane == 0) inv_s[u] = __fdiv_rn(1.0f, __fsqrt_rn(add_rn(tot, 1e-6f)));
     }
+    __syncthreads();
+  }
 #pragma unroll
-    for (int u = 0; u < kTokGroup; ++u) {
-      const int t = tg + u;
-      if (t >= t1) break;
-      dst[(size_t)t * kDim] = blk < 2 ? __float2half_rn(mul_rn(yf[u], inv_s[u])) : __float2half_rn(yf[u]);
-    }
-    if (blk < 2) __syncthreads();  // sq and inv_s are reused by the next group
+  for (int u = 0; u < kTokTile; ++u) {
+    if (t0 + u >= t1) break;
+    dst[(size_t)(t0 + u) * kDim] = blk < 2 ? __float2half_rn(mul_rn(yf[u], inv_s[u])) : __float2half_rn(yf[u]);
   }
   // the CTA holding the last token leaves the conv state at the prompt's last four inputs
   if (t1 == T) {
@@ -121,31 +119,44 @@ __global__ void __launch_bounds__(kDim)
   }
 }
 
-// grid (rows, H), 128 threads: gated RMSNorm of the chunk rule's output.
+// One warp per (row, head), 8 per 256-thread CTA: gated RMSNorm of the chunk
+// rule's output. Lane l holds channels l + 32 j; the sum of squares is
+// warp_tree128's order (the shader's stride-64..1 tree).
 // core: [batch][H][T][128] fp32; z from proj row [.. | z (H*128) | ..] at column z_off;
 // out: [rows][H*128] fp16 (token rows for the output projection).
-__global__ void __launch_bounds__(kDim)
+__global__ void __launch_bounds__(256)
     dn_prefill_gate_kernel(const float* __restrict__ core, const __half* __restrict__ proj, int ld, int z_off,
-                           const float* __restrict__ norm_w, float eps, int T, int H, __half* __restrict__ out) {
-  const int h = blockIdx.y, row = blockIdx.x, c = threadIdx.x;
-  const int b = row / T, t = row % T;
-  __shared__ float sq[kDim];
-  __shared__ float nf_s;
+                           const float* __restrict__ norm_w, float eps, int T, int H, int rows,
+                           __half* __restrict__ out) {
+  const int lane = threadIdx.x & 31, item = blockIdx.x * 8 + (threadIdx.x >> 5);
   pdl_wait();
   pdl_launch();
-  const float o = core[(((size_t)b * H + h) * T + t) * kDim + c];
-  const float zz = __half2float(proj[(size_t)row * ld + z_off + h * kDim + c]);
-  sq[c] = mul_rn(o, o);
-  __syncthreads();
-  if (c < 32) {
-    const float ss = warp_tree128(sq, c);
-    if (c == 0) nf_s = __fdiv_rn(1.0f, __fsqrt_rn(add_rn(__fdiv_rn(ss, (float)kDim), eps)));
+  if (item >= rows * H) return;
+  const int row = item / H, h = item % H, b = row / T, t = row % T;
+  const float* cr = core + (((size_t)b * H + h) * T + t) * kDim;
+  const __half* zr = proj + (size_t)row * ld + z_off + h * kDim;
+  float o[4], zz[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    o[j] = cr[lane + 32 * j];
+    zz[j] = __half2float(zr[lane + 32 * j]);
   }
-  __syncthreads();
-  const float normed = mul_rn(o, nf_s);
-  const float silu = __fdiv_rn(zz, add_rn(1.0f, expf(-zz)));
-  const float weighted = h2f(f2h(mul_rn(norm_w[c], normed)));
-  out[(size_t)row * (H * kDim) + h * kDim + c] = __float2half_rn(mul_rn(weighted, silu));
+  float v0 = mul_rn(o[0], o[0]), v1 = mul_rn(o[1], o[1]);
+  v0 = add_rn(v0, mul_rn(o[2], o[2]));
+  v1 = add_rn(v1, mul_rn(o[3], o[3]));
+  v0 = add_rn(v0, v1);
+#pragma unroll
+  for (int k = 16; k > 0; k >>= 1) v0 += __shfl_down_sync(0xffffffffu, v0, k);
+  const float ss = __shfl_sync(0xffffffffu, v0, 0);
+  const float nf = __fdiv_rn(1.0f, __fsqrt_rn(add_rn(__fdiv_rn(ss, (float)kDim), eps)));
+  __half* dst = out + (size_t)row * (H * kDim) + h * kDim;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float normed = mul_rn(o[j], nf);
+    const float silu = __fdiv_rn(zz[j], add_rn(1.0f, expf(-zz[j])));
+    const float weighted = h2f(f2h(mul_rn(norm_w[lane + 32 * j], normed)));
+    dst[lane + 32 * j] = __float2half_rn(mul_rn(weighted, silu));
+  }
 }
 
 // dst[b] = src[b * T + T - 1] (rows of `width` halves): the last prompt token of each sequence.
@@ -179,8 +190,8 @@ Status launch_dn_prefill_conv(const void* proj, int ld, int batch, int T, int H,
 
 Status launch_dn_prefill_gate(const float* core, const void* proj, int ld, int z_off, const float* norm_w, float eps,
                               int batch, int T, int H, void* out, cudaStream_t st) {
-  launch_k(dn_prefill_gate_kernel, dim3(batch * T, H), dim3(kDim), 0, st, core, (const __half*)proj, ld, z_off,
-           norm_w, eps, T, H, (__half*)out);
+  launch_k(dn_prefill_gate_kernel, dim3((batch * T * H + 7) / 8), dim3(256), 0, st, core, (const __half*)proj, ld,
+           z_off, norm_w, eps, T, H, batch * T, (__half*)out);
   SPOCK_LAUNCH_CHECK("dn_prefill_gate_kernel");
   return Status::ok();
 }
