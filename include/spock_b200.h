@@ -241,7 +241,7 @@ typedef enum {
 /* matvec.comp:28-41 over `rows` activation rows with a fused epilogue.
  * W [out_dim (x2 for SILU_GATE)][in_dim], x [rows][in_dim], y [rows][out_dim]
  * (ARGMAX: int32 [rows]); residual [rows][out_dim] for RESIDUAL (y may alias it).
- * Fast path (exact = 0): in_dim % 64 == 0, out_dim % 8 == 0, rows <= 256,
+ * Fast path (exact = 0): in_dim % 64 == 0, out_dim % 8 == 0, rows <= 65536,
  * ARGMAX at rows <= 8 needs in_dim <= 1024. Exact path: in_dim % 16 == 0.
  * Scratch (padded x, split-K workspace, argmax partials) grows in the context. */
 int spock_matvec(spock_ctx* ctx, int32_t epilogue, int32_t exact, const void* w, int32_t out_dim, int32_t in_dim,

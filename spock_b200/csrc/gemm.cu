@@ -217,16 +217,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nch = (bn + 31) / 32;
   int pre = 0;
 
+  if (warp == 0) {  // one barrier per lane
+    if (lane < nst) {
+      tc::mbar_init(&full[lane], 1);
+      tc::mbar_init(&empty[lane], 1);
+    } else if (lane >= 16 && lane < 18) {
+      tc::mbar_init(&accf[lane - 16], 1);
+      tc::mbar_init(&acce[lane - 16], kTcEpiWarps);
+    } else if (lane == 18) {
+      tc::mbar_init(drain, 1);
+    }
+    __syncwarp();
+  }
   if (t == 0) {
-    for (int s = 0; s < nst; ++s) {
-      tc::mbar_init(&full[s], 1);
-      tc::mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      tc::mbar_init(&accf[b], 1);
-      tc::mbar_init(&acce[b], kTcEpiWarps);
-    }
-    tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmw);
     tc::prefetch_tmap(&tmx);

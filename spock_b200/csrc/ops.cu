@@ -98,9 +98,9 @@ Status op_matvec(OpsScratch& sc, int epilogue, int exact, const void* w, int out
                                                    : EPI_ARGMAX;
   const int n_rows = epi == EPI_SWIGLU ? 2 * out_dim : out_dim;  // weight rows
   const int ntiles = (n_rows + 127) / 128;
-  if (rows > (exact ? (1 << 24) : 256))
+  if (rows > (exact ? (1 << 24) : (1 << 16)))
     return Status::err(SPOCK_ERR_UNSUPPORTED, exact ? "spock_matvec: at most 2^24 rows"
-                                                    : "spock_matvec: the fast path takes at most 256 rows per call");
+                                                    : "spock_matvec: the fast path takes at most 65536 rows per call");
   Status s;
   if (epi == EPI_ARGMAX) {
     s = grow(sc.amax, (size_t)ntiles * rows * 8, false);

@@ -72,6 +72,53 @@ def test_matvec_epilogues(cuda_ok, exact, rows):
     assert check(_bits(y), ref), int(fp16_ulp_diff(_bits(y), ref).max())
 
 
+def _ref_rows(W, X):
+    """fp16 bits of fp16(W @ x) per row, from a float64 product on the GPU."""
+    w = torch.from_numpy(W.view(np.float16)).to(DEV).double()
+    x = torch.from_numpy(X.view(np.float16)).to(DEV).double()
+    return (x @ w.T).half().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("rows", [512, 1000])
+def test_matvec_prefill_row_counts(cuda_ok, rows):
+    """The fast path at prefill row counts (a 512-token prompt, and a ragged
+    1000): the persistent GEMM's 256-row units, its K-split plans for the
+    1024-output projections, and the partial last unit. The products are
+    checked against a float64 product rounded to fp16 (the oracle's
+    sequential sums are too slow at these sizes; both round the same exact
+    value), the residual add and SwiGLU with the oracle's element rules, all
+    within the fast path's 2-ulp policy."""
+    rng = np.random.default_rng(rows)
+    X = _h((rows, 1024), 1.0, rng)
+    W = _h((8224, 1024), 0.02, rng)
+    y = spock_b200.matvec(_dev(W), _dev(X), spock_b200.MV_STORE)
+    torch.cuda.synchronize()
+    got, ref = _bits(y), _ref_rows(W.view(np.uint16), X.view(np.uint16))
+    assert close16(got, ref), int(fp16_ulp_diff(got, ref).max())
+    X2, H = _h((rows, 3584), 1.0, rng), _h((rows, 1024), 1.0, rng)
+    W2 = _h((1024, 3584), 0.02, rng)
+    h = _dev(H)
+    spock_b200.matvec(_dev(W2), _dev(X2), spock_b200.MV_RESIDUAL, residual=h, out=h)
+    torch.cuda.synchronize()
+    mv = _ref_rows(W2.view(np.uint16), X2.view(np.uint16))
+    ref = np.stack([oracle.residual_add(H[r].view(np.uint16), mv[r]) for r in range(rows)])
+    # The projection's fp16 rounding may differ by up to 2 ulps of the
+    # projection, which the residual add keeps in absolute terms (where the
+    # sum cancels, that is many ulps of the small result): allow 2 ulps of
+    # the projection plus one rounding of the sum.
+    f = lambda b: b.view(np.float16).astype(np.float32)
+    ulp = lambda b: np.spacing(np.abs(b.view(np.float16))).astype(np.float32)
+    err = np.abs(f(_bits(h)) - f(ref))
+    assert np.all(err <= 2 * ulp(mv) + ulp(ref)), float((err - 2 * ulp(mv) - ulp(ref)).max())
+    G, U = _h((3584, 1024), 0.02, rng), _h((3584, 1024), 0.02, rng)
+    Wgu = np.stack([G.reshape(224, 16, 1024), U.reshape(224, 16, 1024)], 1).reshape(7168, 1024)
+    y = spock_b200.matvec(_dev(Wgu), _dev(X), spock_b200.MV_SILU_GATE)
+    torch.cuda.synchronize()
+    g_, u_ = _ref_rows(G.view(np.uint16), X.view(np.uint16)), _ref_rows(U.view(np.uint16), X.view(np.uint16))
+    ref = np.stack([oracle.silu_gate(a, b) for a, b in zip(g_, u_)])
+    assert close16(_bits(y), ref), int(fp16_ulp_diff(_bits(y), ref).max())
+
+
 @pytest.mark.parametrize("exact", [True, False])
 @pytest.mark.parametrize("rows", [1, 3, 12])
 def test_lm_head_argmax_full_vocab(cuda_ok, exact, rows):
