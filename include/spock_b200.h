@@ -116,7 +116,7 @@ int spock_chunk_prefill(spock_ctx* ctx, const spock_chunk_desc* desc, const void
  *
  * Same arguments, layouts and results as spock_chunk_prefill, but no context:
  * the fp16 staging of q/k/v (needed for fp32 inputs or use_qk_l2norm=1) goes
- * to a fixed 16 MiB array compiled into the library, held on every GPU that
+ * to a fixed 24 MiB array compiled into the library, held on every GPU that
  * loads it until the process exits. Limit when staging is needed:
  * batch*num_heads*seq_len <= 16384; larger requests return SPOCK_ERR_INVALID
  * with the reason in spock_last_error(NULL). The call enqueues work on the
@@ -124,9 +124,9 @@ int spock_chunk_prefill(spock_ctx* ctx, const spock_chunk_desc* desc, const void
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture.
  * Under CUDA's lazy module loading that first lookup is also when the driver
- * loads the library's device code and commits the 16 MiB array on that
+ * loads the library's device code and commits the 24 MiB array on that
  * device, so the first call (or first spock_noalloc_sync) on a device costs
- * 16 MiB of device memory once; later calls allocate nothing.
+ * 24 MiB of device memory once; later calls allocate nothing.
  * All calls on a device share the array, so calls whose work overlaps on the
  * GPU (different streams, no ordering between them) race and must not be made.
  *

@@ -23,7 +23,13 @@
 //
 // Operands are fp16 with fp32 accumulation; S is rounded to fp16 only as an
 // MMA operand while its fp32 master copy stays in TMEM. Inputs arrive as fp16
-// or bf16 tiles by TMA (bf16 is converted to fp16 in shared memory).
+// or bf16 tiles by TMA (bf16 is converted to fp16 in shared memory). The
+// precise variant (fp32 inputs) carries the operands whose rounding reaches
+// the results as fp16 hi/lo pairs (x = hi + lo, about 22 bits): Q and K in
+// G1, T diag(beta) and V in U, P and v_new in the output, K and the decayed
+// v_new in the state update (hi*hi + hi*lo + lo*hi). A numpy model of these
+// rounding points singled them out: fp16 K in the state update alone gave the
+// 2e-4 state error, P / v_new / G1 the output error at large |v|.
 //
 // TMEM (512 columns): [0,128) S, [128,256) D1, [256,320) G1, [320,384) W^T.
 // Every wait on an mbarrier is bounded; on timeout the kernel records an error
@@ -66,18 +72,25 @@ constexpr int OFF_TM = OFF_NM + C * LDN * 4;
 constexpr int OFF_YM = OFF_TM + C * LDN * 4;
 constexpr int OFF_SMALL = OFF_YM + 3 * 256 * 4;
 constexpr int SMEM_BYTES = OFF_SMALL + 2048 + 1024;  // + alignment slack
-// Extra regions of the precise (fp32-input) variant: the low fp16 half of V,
-// and [T diag(beta)]_lo with its own zero block. The low half of
+// Extra regions of the precise (fp32-input) variant: the low fp16 halves of V
+// and K, and [T diag(beta)]_lo with its own zero block, followed by P_lo.
+// Q_lo / K_lo for G1 and v_new_lo for the output borrow the AW region while
+// it is idle. The low half of
 // diag(e^{gL-gc}) v_new reuses the AW region, which is dead after step 7.
 constexpr int OFF_VLO = 182 * 1024;
+constexpr int OFF_KLO = OFF_NM;  // low fp16 half of K, 2 x 8K, between the solve and the next G1
+static_assert(C * LDN * 4 >= 16 * 1024, "K_lo fits in the N matrix's region");
 constexpr int OFF_TBL = OFF_VLO + 16 * 1024;
-constexpr int SMEM_BYTES_PRECISE = OFF_TBL + 16 * 1024 + 1024;
+constexpr int OFF_PLO = OFF_TBL + 16 * 1024;  // P_lo: with TBL's zero block before it, [0 ; P_lo]
+constexpr int SMEM_BYTES_PRECISE = OFF_PLO + 8 * 1024 + 1024;
+static_assert(SMEM_BYTES_PRECISE <= 232448, "shared memory per CTA");
 static_assert(OFF_VLO >= OFF_SMALL + 2048, "smem regions overlap");
 
 template <bool kBf16In, int kOut, bool kPrecise>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_rule_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmvlo,
+                      const __grid_constant__ CUtensorMap tmklo, const __grid_constant__ CUtensorMap tmqlo,
                       const float* __restrict__ g,
                       const float* __restrict__ beta, const float* __restrict__ init,
                       void* __restrict__ out, float* __restrict__ final_state, int S,
@@ -108,7 +121,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::prefetch_tmap(&tmq);
     tc::prefetch_tmap(&tmk);
     tc::prefetch_tmap(&tmv);
-    if constexpr (kPrecise) tc::prefetch_tmap(&tmvlo);
+    if constexpr (kPrecise) {
+      tc::prefetch_tmap(&tmvlo);
+      tc::prefetch_tmap(&tmklo);
+      tc::prefetch_tmap(&tmqlo);
+    }
   }
   if (warp == 0) {
     tc::tmem_alloc(s_tmem, 512);
@@ -160,13 +177,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int c = 0; c < nchunks; ++c) {
     // ---- 1. loads: q/k/v tiles by TMA, g/beta by threads -----------------
     if (t == 0) {
-      tc::mbar_arrive_expect_tx(bar_tma, (kPrecise ? 8 : 6) * 64 * 64 * 2);
+      tc::mbar_arrive_expect_tx(bar_tma, (kPrecise ? 12 : 6) * 64 * 64 * 2);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         tc::tma_load_3d(sm + OFF_QK + h * 16384, &tmq, bar_tma, h * 64, c * C, p);
         tc::tma_load_3d(sm + OFF_QK + h * 16384 + 8192, &tmk, bar_tma, h * 64, c * C, p);
         tc::tma_load_3d(sm + OFF_V + h * 8192, &tmv, bar_tma, h * 64, c * C, p);
-        if constexpr (kPrecise) tc::tma_load_3d(sm + OFF_VLO + h * 8192, &tmvlo, bar_tma, h * 64, c * C, p);
+        if constexpr (kPrecise) {
+          tc::tma_load_3d(sm + OFF_VLO + h * 8192, &tmvlo, bar_tma, h * 64, c * C, p);
+          // [Q_lo ; K_lo] in the AW region (idle until Q' at step 4), laid out as [Q ; K]
+          tc::tma_load_3d(sm + OFF_AW + h * 16384, &tmqlo, bar_tma, h * 64, c * C, p);
+          tc::tma_load_3d(sm + OFF_AW + h * 16384 + 8192, &tmklo, bar_tma, h * 64, c * C, p);
+        }
       }
     }
     if (t < C) {
@@ -233,6 +255,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mma_f16(mG1, tc::sdesc(sbase + OFF_QK + koff, 16, 1024),
                     tc::sdesc(sbase + OFF_QK + 8192 + koff, 16, 1024), ID_G1, ks > 0);
       }
+      if constexpr (kPrecise) {  // [Q;K]_hi K_lo^T + [Q;K]_lo K_hi^T
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
+          tc::mma_f16(mG1, tc::sdesc(sbase + OFF_QK + koff, 16, 1024),
+                      tc::sdesc(sbase + OFF_AW + 8192 + koff, 16, 1024), ID_G1, 1);
+          tc::mma_f16(mG1, tc::sdesc(sbase + OFF_AW + koff, 16, 1024),
+                      tc::sdesc(sbase + OFF_QK + 8192 + koff, 16, 1024), ID_G1, 1);
+        }
+      }
       tc::mma_commit(bar_mma);
     }
     if (!wait_mma()) { failed = true; break; }
@@ -252,7 +284,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int j = q * 8 + k;
             x[k] = (j <= t) ? (a[j] * scale) * expf(gi - s_g[j]) : 0.f;
           }
-          *reinterpret_cast<uint4*>(dst + sw128(t, q)) = pack8(x);
+          const uint4 xh = pack8(x);
+          *reinterpret_cast<uint4*>(dst + sw128(t, q)) = xh;
+          if constexpr (kPrecise) {  // P_lo
+            float xr[8];
+            unpack8(xh, xr);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) xr[k] = x[k] - xr[k];
+            *reinterpret_cast<uint4*>(sm + OFF_PLO + sw128(t, q)) = pack8(xr);
+          }
         }
       } else {  // N row i
         const int i = t - C;
@@ -308,6 +348,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     // ---- 5. D1 = [T diag(beta); 0] V ; Wt = K^T (T diag(beta e^gc))^T -----------
+    if constexpr (kPrecise) {
+      // the low fp16 half of K into the N matrix's region, dead until the
+      // next chunk's G1 epilogue; the state update (step 9) reads it
+      if (t == 0) {
+        tc::mbar_arrive_expect_tx(bar_tma, 2 * 64 * 64 * 2);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) tc::tma_load_3d(sm + OFF_KLO + h * 8192, &tmklo, bar_tma, h * 64, c * C, p);
+      }
+    }
     if (t == 0) {
       tc::tc_fence_after();
 #pragma unroll
@@ -370,7 +419,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int ch = (cb & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(sm + OFF_VN + h * 8192 + sw128(t, ch)) = pack8(&v[8 * q]);
+          const uint4 vh = pack8(&v[8 * q]);
+          *reinterpret_cast<uint4*>(sm + OFF_VN + h * 8192 + sw128(t, ch)) = vh;
+          if constexpr (kPrecise) {  // v_new low half into the second half of the dead AW region
+            float vr[8];
+            unpack8(vh, vr);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) vr[k] = v[8 * q + k] - vr[k];
+            *reinterpret_cast<uint4*>(sm + OFF_AW + 16384 + h * 8192 + sw128(t, ch)) = pack8(vr);
+          }
           float y[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) y[k] = v[8 * q + k] * fs;
@@ -391,6 +448,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     // ---- 9. S += K^T VS ; D1 += [0 ; P] VN ---------------------------------------
+    if constexpr (kPrecise) {
+      ok = tc::mbar_wait_bounded(bar_tma, ph_tma, kWaitLimit);
+      ph_tma ^= 1;
+      if (__syncthreads_or(!ok)) { failed = true; break; }
+    }
     if (t == 0) {
       tc::tc_fence_after();
 #pragma unroll
@@ -402,11 +464,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < 4; ++ks)
           tc::mma_f16(mS, tc::sdesc(sbase + OFF_QK + 8192 + ks * 2048, 16384, 1024),
                       tc::sdesc(sbase + OFF_AW + ks * 2048, 8192, 1024), ID_2A, 1);
+        // K_lo^T VS_hi: fp16 K alone put ~2e-4 relative error into the state
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_f16(mS, tc::sdesc(sbase + OFF_KLO + ks * 2048, 8192, 1024),
+                      tc::sdesc(sbase + OFF_VS + ks * 2048, 8192, 1024), ID_2A, 1);
       }
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + 8192 + ks * 32, 16, 1024),
                     tc::sdesc(sbase + OFF_VN + ks * 2048, 8192, 1024), ID_1, 1);
+      if constexpr (kPrecise) {  // [0;P_hi] VN_lo + [0;P_lo] VN_hi
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TB + 8192 + ks * 32, 16, 1024),
+                      tc::sdesc(sbase + OFF_AW + 16384 + ks * 2048, 8192, 1024), ID_1, 1);
+          tc::mma_f16(mD1, tc::sdesc(sbase + OFF_TBL + 8192 + ks * 32, 16, 1024),
+                      tc::sdesc(sbase + OFF_VN + ks * 2048, 8192, 1024), ID_1, 1);
+        }
+      }
       tc::mma_commit(bar_mma);
     }
     if (!wait_mma()) { failed = true; break; }
@@ -549,15 +625,18 @@ namespace {
 // run the serial kernel above in its precise (hi/lo) form.
 template <bool kBf16In, int kOut, bool kPrecise>
 Status launch_kernel(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                     const CUtensorMap& mvlo, const float* g, const float* beta, const float* init,
-                     void* out, float* final_state, int64_t pairs, int S, int* err, cudaStream_t st) {
+                     const CUtensorMap& mvlo, const CUtensorMap& mklo, const CUtensorMap& mqlo,
+                     const float* g, const float* beta,
+                     const float* init, void* out, float* final_state, int64_t pairs, int S, int* err,
+                     cudaStream_t st) {
   if constexpr (!kPrecise)
     return launch_chunk_pipeline<kBf16In, kOut>(mq, mk, mv, g, beta, init, out, final_state, pairs, S, err, st);
   auto kern = chunk_rule_kernel<kBf16In, kOut, kPrecise>;
   const int smem = kPrecise ? SMEM_BYTES_PRECISE : SMEM_BYTES;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "chunk_rule_kernel smem attribute");
-  kern<<<(unsigned)pairs, kThreads, smem, st>>>(mq, mk, mv, mvlo, g, beta, init, out, final_state, S, err);
+  kern<<<(unsigned)pairs, kThreads, smem, st>>>(mq, mk, mv, mvlo, mklo, mqlo, g, beta, init, out, final_state, S,
+                                                err);
   SPOCK_LAUNCH_CHECK("chunk_rule_kernel");
   return Status::ok();
 }
@@ -583,12 +662,12 @@ Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, co
   const void *q16 = q, *k16 = k, *v16 = v;
   bool bf16 = d.dtype_in == SPOCK_BF16;
   const bool precise = d.dtype_in == SPOCK_F32;
-  const void* vlo16 = nullptr;
+  const void *vlo16 = nullptr, *klo16 = nullptr, *qlo16 = nullptr;
   if (d.dtype_in == SPOCK_F32 || d.use_qk_l2norm) {
     // Stage fp16 copies (the optional L2 norm, and for fp32 inputs the low
     // fp16 half of v) in the context's scratch.
     const size_t n = (size_t)pairs * S * D;
-    cudaError_t e = scratch.reserve((precise ? 4 : 3) * n * sizeof(__half));
+    cudaError_t e = scratch.reserve((precise ? 6 : 3) * n * sizeof(__half));
     if (e != cudaSuccess) return Status::err(SPOCK_ERR_ALLOC, "chunk prefill: scratch allocation failed");
     __half* base = static_cast<__half*>(scratch.buf);
     const int64_t rows = (int64_t)pairs * S;
@@ -597,7 +676,7 @@ Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, co
     for (int i = 0; i < 3; ++i) {
       const int l2 = (i < 2) && d.use_qk_l2norm;
       __half* dst = base + i * n;
-      __half* lo = (precise && i == 2) ? base + 3 * n : nullptr;
+      __half* lo = !precise ? nullptr : base + (i == 2 ? 3 : i == 1 ? 4 : 5) * n;
       if (d.dtype_in == SPOCK_F32)
         chunk_stage_fp16_kernel<float><<<blocks, 256, 0, stream>>>((const float*)src[i], dst, lo, rows, l2);
       else if (d.dtype_in == SPOCK_F16)
@@ -609,10 +688,14 @@ Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, co
     q16 = base;
     k16 = base + n;
     v16 = base + 2 * n;
-    if (precise) vlo16 = base + 3 * n;
+    if (precise) {
+      vlo16 = base + 3 * n;
+      klo16 = base + 4 * n;
+      qlo16 = base + 5 * n;
+    }
     bf16 = false;
   }
-  CUtensorMap mq, mk, mv, mvlo;
+  CUtensorMap mq, mk, mv, mvlo, mklo, mqlo;
   Status s = make_map(&mq, q16, pairs, S);
   if (s.code) return s;
   s = make_map(&mk, k16, pairs, S);
@@ -621,9 +704,13 @@ Status launch_chunk_prefill(ChunkScratch& scratch, const spock_chunk_desc& d, co
   if (s.code) return s;
   s = make_map(&mvlo, precise ? vlo16 : v16, pairs, S);
   if (s.code) return s;
+  s = make_map(&mklo, precise ? klo16 : k16, pairs, S);
+  if (s.code) return s;
+  s = make_map(&mqlo, precise ? qlo16 : q16, pairs, S);
+  if (s.code) return s;
 #define SPOCK_CHUNK_CASE(BF, OUT, PR)                                                          \
   if (bf16 == BF && d.dtype_out == OUT && precise == PR)                                       \
-    return launch_kernel<BF, OUT, PR>(mq, mk, mv, mvlo, g, beta, init, out, final_state, pairs, \
+    return launch_kernel<BF, OUT, PR>(mq, mk, mv, mvlo, mklo, mqlo, g, beta, init, out, final_state, pairs, \
                                       S, err_flag, stream);
   SPOCK_CHUNK_CASE(false, SPOCK_F32, false)
   SPOCK_CHUNK_CASE(false, SPOCK_F16, false)
@@ -668,7 +755,7 @@ namespace {
 // seq_len*128), i.e. batch*num_heads*seq_len <= 16384 token-heads.
 constexpr size_t kNoAllocMaxElems = size_t(1) << 21;
 constexpr size_t kNoAllocHeader = 256;  // error word of the bounded waits
-constexpr size_t kNoAllocBytes = kNoAllocHeader + 4 * kNoAllocMaxElems * sizeof(__half);  // 16 MiB + 256 B
+constexpr size_t kNoAllocBytes = kNoAllocHeader + 6 * kNoAllocMaxElems * sizeof(__half);  // 24 MiB + 256 B
 
 // Every GPU that loads this library holds this array until the process exits.
 // It is shared by all calls on a device and keeps the last call's contents.
@@ -729,7 +816,7 @@ Status chunk_prefill_noalloc(const spock_chunk_desc& d, const void* q, const voi
   // tensors are fully rewritten by every call.
   int* err_flag = reinterpret_cast<int*>(base);
 
-  const void *q16 = q, *k16 = k, *v16 = v, *vlo16 = nullptr;
+  const void *q16 = q, *k16 = k, *v16 = v, *vlo16 = nullptr, *klo16 = nullptr, *qlo16 = nullptr;
   bool bf16 = d.dtype_in == SPOCK_BF16;
   const bool precise = d.dtype_in == SPOCK_F32;
   if (stage) {
@@ -740,7 +827,7 @@ Status chunk_prefill_noalloc(const spock_chunk_desc& d, const void* q, const voi
     for (int i = 0; i < 3; ++i) {
       const int l2 = (i < 2) && d.use_qk_l2norm;
       __half* dst = st + i * n;
-      __half* lo = (precise && i == 2) ? st + 3 * n : nullptr;
+      __half* lo = !precise ? nullptr : st + (i == 2 ? 3 : i == 1 ? 4 : 5) * n;
       if (d.dtype_in == SPOCK_F32)
         chunk_stage_fp16_kernel<float><<<blocks, 256, 0, stream>>>((const float*)src[i], dst, lo, rows, l2);
       else if (d.dtype_in == SPOCK_F16)
@@ -752,17 +839,23 @@ Status chunk_prefill_noalloc(const spock_chunk_desc& d, const void* q, const voi
     q16 = st;
     k16 = st + n;
     v16 = st + 2 * n;
-    if (precise) vlo16 = st + 3 * n;
+    if (precise) {
+      vlo16 = st + 3 * n;
+      klo16 = st + 4 * n;
+      qlo16 = st + 5 * n;
+    }
     bf16 = false;
   }
-  CUtensorMap mq, mk, mv, mvlo;
+  CUtensorMap mq, mk, mv, mvlo, mklo, mqlo;
   if ((s = make_map(&mq, q16, pairs, S)).code) return s;
   if ((s = make_map(&mk, k16, pairs, S)).code) return s;
   if ((s = make_map(&mv, v16, pairs, S)).code) return s;
   if ((s = make_map(&mvlo, precise ? vlo16 : v16, pairs, S)).code) return s;
+  if ((s = make_map(&mklo, precise ? klo16 : k16, pairs, S)).code) return s;
+  if ((s = make_map(&mqlo, precise ? qlo16 : q16, pairs, S)).code) return s;
 #define SPOCK_NOALLOC_CASE(BF, OUT, PR)                                                            \
   if (bf16 == BF && d.dtype_out == OUT && precise == PR)                                           \
-    return launch_kernel<BF, OUT, PR>(mq, mk, mv, mvlo, g, beta, init, out, final_state, pairs, S, \
+    return launch_kernel<BF, OUT, PR>(mq, mk, mv, mvlo, mklo, mqlo, g, beta, init, out, final_state, pairs, S, \
                                       err_flag, stream);
   SPOCK_NOALLOC_CASE(false, SPOCK_F32, false)
   SPOCK_NOALLOC_CASE(false, SPOCK_F16, false)

@@ -41,20 +41,27 @@ def batched_oracle(q, k, v, g, b, init=None, l2=False):
     return np.stack(outs), np.stack(sts)
 
 
+# The reference probe's own bar for the chunk rule
+# (apps/spock-deltanet-chunk-prefill-probe.cpp:467-469), met by the fp32
+# (precise) path on config 0.
+PROBE_TOL = 1e-4
+
+
 def test_config0_fp32(cuda_ok):
-    """H16, S104 (padded to 128), C64, d128, fp32."""
+    """H16, S104 (padded to 128), C64, d128, fp32. Held to
+    the reference probe's 1e-4, not only the north star's 1e-3."""
     q, k, v, g, b = chunk_inputs(16, 104, seed=0, batch=1)
     ro, rs = batched_oracle(q, k, v, g, b)
     go, gs = run_gpu(q, k, v, g, b)
-    assert max_rel(go, ro) <= TOL and max_rel(gs, rs) <= TOL, (max_rel(go, ro), max_rel(gs, rs))
+    assert max_rel(go, ro) <= PROBE_TOL and max_rel(gs, rs) <= PROBE_TOL, (max_rel(go, ro), max_rel(gs, rs))
 
 
 def test_probe_golden_fixture(cuda_ok):
     """The reference probe's xorshift case (v in [-20,20], g in [-9,0)) vs the
-    reference's own outputs stored in the fixture."""
+    reference's own outputs stored in the fixture, at the probe's 1e-4."""
     d = np.load(os.path.join(GOLD, "chunk_probe_h4.npz"))
     go, gs = run_gpu(d["q"][None], d["k"][None], d["v"][None], d["g"][None], d["beta"][None])
-    assert max_rel(go[0], d["ref_out"]) <= TOL and max_rel(gs[0], d["ref_state"]) <= TOL, (
+    assert max_rel(go[0], d["ref_out"]) <= PROBE_TOL and max_rel(gs[0], d["ref_state"]) <= PROBE_TOL, (
         max_rel(go[0], d["ref_out"]), max_rel(gs[0], d["ref_state"]))
 
 

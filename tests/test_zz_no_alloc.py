@@ -73,7 +73,7 @@ def test_noalloc_matches_context_entry_point_twice(cuda_ok):
 
 
 def test_noalloc_at_its_limit_fp32_matches_oracle(cuda_ok):
-    """Exactly 16384 token-heads of fp32 input: all four staged tensors
+    """Exactly 16384 token-heads of fp32 input: all six staged tensors
     (q, k, v and v's low half) fill the fixed array."""
     (hq, hk, hv, hg, hb), (q, k, v, g, b) = _inputs(16, 1024, 31, 1)
     out = torch.full((1, 16, 1024, 128), float("nan"), device=DEV)
