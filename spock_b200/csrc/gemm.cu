@@ -758,11 +758,12 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     std::call_once(once, [] { prep = gemm_prepare(); });
     if (prep.code) return prep;
   }
-  // Plan (bn, split), in microseconds measured on B200: a 64-wide K block
-  // costs a CTA ~0.37 us (0.41 at bn = 256) whatever bn is, so wide units
-  // pay; units beyond one per SM queue on a CTA (their epilogues overlap);
-  // a split adds its partial traffic (~70 GB/s per SM) and needs all its
-  // clusters resident at once.
+  // Plan (bn, split) from per-launch costs measured on B200 (microseconds,
+  // 2-k-block stages; the ~3 us of fixed cost per launch is common to all):
+  // a 64-wide K block costs a CTA 0.24 us at bn <= 64, 0.33 at bn = 128 and
+  // 0.48 at bn = 256; units beyond one per SM queue on a CTA (their
+  // epilogues overlap); a split adds ~2.5 us of partial exchange and
+  // reduction and needs all its clusters resident at once.
   const size_t ws_floats = a.ws ? a.ws_bytes / 4 : 0;
   int best_bn = 0, best_split = 1;
   double best = 1e30;
@@ -770,7 +771,7 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
     if (bn > 256 || bn % 16 || bn > a.bpad) continue;
     if (a.bn > 0 && bn != a.bn) continue;
     const int nb = (a.bpad + bn - 1) / bn, units = ntiles * nb, nch = (bn + 31) / 32;
-    const double ckb = bn > 128 ? 0.41 : 0.37;
+    const double ckb = bn > 128 ? 0.48 : bn > 64 ? 0.33 : 0.24;
     for (int split : {1, 2, 4, 8}) {
       if (a.nsplit > 0 && split != a.nsplit) continue;
       double cost;
@@ -780,7 +781,7 @@ Status launch_gemm(int epi, const void* x, const void* w, GemmArgs a, int sms, c
         const int per = (kbs + split - 1) / split;
         if ((kbs + per - 1) / per != split || units > max_clusters(epi, split)) continue;
         if ((size_t)units * split * nch * 4096 > ws_floats) continue;
-        cost = per * ckb + 2.0 * (split - 1) / split * nch * 16384 / 70e3;
+        cost = per * ckb + 2.5 + 0.1 * split;
       }
       if (cost < best - 1e-9) {
         best = cost;
