@@ -770,7 +770,7 @@ def main():
             print(json.dumps({
                 "impl": "reference", "metric": "chunk-prefill Mtok/s (token = one sequence position across all 16 heads)",
                 "value": round(val, 6), "unit": "Mtok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded, config-0 distributions)",
                 "config": {"workload": "config 2: batched chunk prefill (bounded sample per step)", "heads": H,
                            "chunk": C, "k_dim": K, "v_dim": V},
