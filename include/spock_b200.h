@@ -243,7 +243,9 @@ typedef enum {
  * (ARGMAX: int32 [rows]); residual [rows][out_dim] for RESIDUAL (y may alias it).
  * Fast path (exact = 0): in_dim % 64 == 0, out_dim % 8 == 0, rows <= 65536,
  * ARGMAX at rows <= 8 needs in_dim <= 1024. Exact path: in_dim % 16 == 0.
- * Scratch (padded x, split-K workspace, argmax partials) grows in the context. */
+ * Scratch (padded x, split-K workspace, argmax partials) grows in the context
+ * and is shared by its calls: calls on one context whose work overlaps on the
+ * GPU (different streams) must be ordered by the caller. */
 int spock_matvec(spock_ctx* ctx, int32_t epilogue, int32_t exact, const void* w, int32_t out_dim, int32_t in_dim,
                  const void* x, int64_t rows, void* y, const void* residual, void* stream);
 
