@@ -149,8 +149,9 @@ __global__ void __launch_bounds__(256)
 // With ns > 1 (few rows) the positions are split into ns contiguous ranges,
 // one per CTA; each CTA leaves its partial (max, sum, weighted V) in ws and
 // the last of a row's ns CTAs (atomic ticket, reset for the next launch)
-// merges them in range order. Within a CTA, warp w takes positions w, w+8, ...;
-// lane l owns dims 8l..8l+7 of the 4 query heads of this kv head (GQA group).
+// merges them in range order. Within a CTA, warp w takes positions w, w+8, ...,
+// two per round with the next round's K/V rows already loading; lane l owns
+// dims 8l..8l+7 of the 4 query heads of this kv head (GQA group).
 // Online softmax per warp, merged across warps in shared memory; the output is
 // fp16(acc / (sum + 1e-30)) and then fp16(out * sigmoid(gate)).
 __global__ void __launch_bounds__(256)
@@ -187,11 +188,18 @@ __global__ void __launch_bounds__(256)
   }
   const __half* base = kv + (size_t)seq * kv_seq_stride + kv_layer_off;
   const int span = (L + ns - 1) / ns, p_lo = blockIdx.z * span, p_hi = min(L, p_lo + span);
-  for (int p = p_lo + warp; p < p_hi; p += 8) {
-    const __half* kr = base + (size_t)p * (2 * KVH * HD) + kvh * HD + lane * 8;
-    const __half* vr = base + (size_t)p * (2 * KVH * HD) + KVH * HD + kvh * HD + lane * 8;
-    const uint4 ku = *reinterpret_cast<const uint4*>(kr);
-    const uint4 vu = *reinterpret_cast<const uint4*>(vr);
+  // K and V rows of position p (zeros past the range; the update skips them)
+  auto load = [&](int p, uint4& ku, uint4& vu) {
+    if (p < p_hi) {
+      const __half* row = base + (size_t)p * (2 * KVH * HD) + kvh * HD + lane * 8;
+      ku = *reinterpret_cast<const uint4*>(row);
+      vu = *reinterpret_cast<const uint4*>(row + KVH * HD);
+    } else {
+      ku = vu = make_uint4(0, 0, 0, 0);
+    }
+  };
+  // online softmax update of this warp's state with one position
+  auto update = [&](const uint4& ku, const uint4& vu) {
     float kf[8], vf[8];
     const __half2* k2 = reinterpret_cast<const __half2*>(&ku);
     const __half2* v2 = reinterpret_cast<const __half2*>(&vu);
@@ -203,21 +211,44 @@ __global__ void __launch_bounds__(256)
       vf[2 * k] = c.x;
       vf[2 * k + 1] = c.y;
     }
+    float dot[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float dot = 0.f;
+      dot[g] = 0.f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) dot = fmaf(qv[g][k], kf[k], dot);
+      for (int k = 0; k < 8; ++k) dot[g] = fmaf(qv[g][k], kf[k], dot[g]);
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      const float sc = dot * scale;
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], o);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float sc = dot[g] * scale;
       const float mn = fmaxf(m[g], sc);
-      const float corr = expf(m[g] - mn), w = expf(sc - mn);
+      const float corr = __expf(m[g] - mn), w = __expf(sc - mn);
       l[g] = l[g] * corr + w;
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[g][k] = fmaf(w, vf[k], acc[g][k] * corr);
       m[g] = mn;
     }
+  };
+  // two positions per round (p, p + 8); the next round's rows are loaded
+  // before this round's arithmetic
+  int p = p_lo + warp;
+  uint4 k0, v0, k1, v1;
+  load(p, k0, v0);
+  load(p + 8, k1, v1);
+  for (; p < p_hi; p += 16) {
+    uint4 nk0, nv0, nk1, nv1;
+    load(p + 16, nk0, nv0);
+    load(p + 24, nk1, nv1);
+    update(k0, v0);
+    if (p + 8 < p_hi) update(k1, v1);
+    k0 = nk0;
+    v0 = nv0;
+    k1 = nk1;
+    v1 = nv1;
   }
   __shared__ float sm_m[8][G], sm_l[8][G];
   __shared__ float sm_acc[8][G][HD];
